@@ -1,0 +1,372 @@
+"""graphzero_b200: B200 leaf evaluation and batched PUCT search for GraphZero.
+
+Python mirror of the C ABI in include/graphzero_b200.h.  The compute path is
+the CUDA library libgraphzero_b200.so built in this directory (see
+graphzero_b200.build); importing this package fails loudly when it is
+missing — there is no CPU or eager fallback.
+
+The interface follows the reference's model interface INeuralNet
+(networks/neural_network.h:16-27: init / predict / save / load / destroy /
+broadcast_weights) and its factory create_neural_net(type, game)
+(networks/neural_network.c:6-13), with batched device-pointer calls added.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libgraphzero_b200.so"
+
+TICTACTOE, CONNECT4, CHESS = 0, 1, 2
+GAT, RESNET = 0, 1
+PREC_AUTO, PREC_FP32, PREC_BF16, PREC_FP16 = 0, 1, 2, 3
+GAME_NAMES = {"tictactoe": TICTACTOE, "connect4": CONNECT4, "chess": CHESS}
+
+OK, ERR_INVALID_ARG, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_IO, ERR_CAPACITY, ERR_UNSUPPORTED = range(8)
+
+
+class GZError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"[{status}] {message}")
+        self.status = status
+
+
+if not LIB_PATH.exists():
+    raise ImportError(f"{LIB_PATH} is missing: run `python graphzero_b200/build.py` (nvcc, sm_100a)")
+_lib = C.CDLL(str(LIB_PATH))
+
+_vp, _i8p, _f32p, _i32p = C.c_void_p, C.POINTER(C.c_int8), C.POINTER(C.c_float), C.POINTER(C.c_int32)
+
+
+class NetConfig(C.Structure):
+    _fields_ = [("game", C.c_int), ("kind", C.c_int), ("precision", C.c_int), ("max_batch", C.c_int)]
+
+
+class MctsConfig(C.Structure):
+    _fields_ = [("game", C.c_int), ("trees", C.c_int), ("leaves_per_tree", C.c_int), ("c_puct", C.c_float),
+                ("virtual_loss", C.c_int), ("node_capacity", C.c_int), ("dirichlet_alpha", C.c_float),
+                ("dirichlet_eps", C.c_float), ("seed", C.c_uint64)]
+
+
+# name -> (restype, argtypes)
+_SIGS = {
+    "gz_status_string": (C.c_char_p, [C.c_int]),
+    "gz_last_error": (C.c_char_p, []),
+    "gz_version": (C.c_char_p, []),
+    "gz_game_shape": (C.c_int, [C.c_int, _i32p]),
+    "gz_game_graph": (C.c_int, [C.c_int, _i32p, _i32p]),
+    "gz_game_next_state": (C.c_int, [C.c_int, _i8p, C.c_int, C.c_int, _i8p, C.POINTER(C.c_int)]),
+    "gz_game_valid_moves": (C.c_int, [C.c_int, _i8p, C.POINTER(C.c_uint8)]),
+    "gz_game_ended": (C.c_int, [C.c_int, _i8p, C.c_int, C.POINTER(C.c_int)]),
+    "gz_weight_count": (C.c_size_t, [C.c_int, C.c_int]),
+    "gz_synth_weights": (C.c_int, [C.c_int, C.c_int, C.c_uint64, C.c_float, C.c_int, _f32p, C.c_size_t]),
+    "gz_synth_positions": (C.c_int, [C.c_int, C.c_uint64, C.c_uint64, C.c_int, _i8p, _i8p]),
+    "gz_net_create": (C.c_int, [C.POINTER(NetConfig), C.c_int, C.POINTER(_vp)]),
+    "gz_net_destroy": (C.c_int, [_vp]),
+    "gz_net_weight_count": (C.c_size_t, [_vp]),
+    "gz_net_kernel_name": (C.c_char_p, [_vp]),
+    "gz_net_load_weights": (C.c_int, [_vp, _f32p, C.c_size_t]),
+    "gz_net_save_weights": (C.c_int, [_vp, _f32p, C.c_size_t]),
+    "gz_net_predict_batch": (C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp, _vp]),
+    "gz_net_predict_host": (C.c_int, [_vp, _i8p, _i8p, C.c_int, _f32p, _f32p]),
+    "gz_net_predict": (C.c_int, [_vp, _f32p, _f32p, _f32p]),
+    "gz_net_broadcast": (C.c_int, [_vp, _vp, C.c_int, _vp]),
+    "gz_nccl_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
+    "gz_nccl_comm_init": (C.c_int, [C.POINTER(C.c_uint8), C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
+    "gz_nccl_comm_destroy": (C.c_int, [_vp]),
+    "gz_mcts_create": (C.c_int, [C.POINTER(MctsConfig), C.c_int, C.POINTER(_vp)]),
+    "gz_mcts_destroy": (C.c_int, [_vp]),
+    "gz_mcts_reset_roots": (C.c_int, [_vp, _vp, _vp, _vp]),
+    "gz_mcts_select": (C.c_int, [_vp, _vp]),
+    "gz_mcts_leaf_buffers": (C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp)]),
+    "gz_mcts_copy_leaves": (C.c_int, [_vp, _i8p, _i8p, _i8p, _vp]),
+    "gz_mcts_backup": (C.c_int, [_vp, _vp, _vp, _vp]),
+    "gz_mcts_step": (C.c_int, [_vp, _vp, _vp]),
+    "gz_mcts_run": (C.c_int, [_vp, _vp, C.c_int, _vp]),
+    "gz_mcts_root_stats": (C.c_int, [_vp, _i32p, _f32p, _vp]),
+    "gz_mcts_tree_sizes": (C.c_int, [_vp, _i32p, _i32p, _vp]),
+    "gz_mcts_choose": (C.c_int, [_vp, C.c_int, _vp, _vp]),
+    "gz_mcts_play": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
+    "gz_mcts_check": (C.c_int, [_vp]),
+}
+for _name, (_res, _args) in _SIGS.items():
+    _f = getattr(_lib, _name)
+    _f.restype, _f.argtypes = _res, _args
+
+EXPORTED_SYMBOLS = tuple(_SIGS)
+
+
+def _check(status: int) -> None:
+    if status != OK:
+        raise GZError(status, _lib.gz_last_error().decode(errors="replace"))
+
+
+def _ptr(a: np.ndarray, t):
+    return a.ctypes.data_as(C.POINTER(t))
+
+
+def _dev(x) -> int:
+    """Raw device address of a torch tensor (or an int address)."""
+    if x is None:
+        return None
+    return x if isinstance(x, int) else x.data_ptr()
+
+
+def _stream(s) -> int | None:
+    if s is None:
+        try:
+            import torch
+            return torch.cuda.current_stream().cuda_stream
+        except Exception:  # noqa: BLE001
+            return None
+    return s if isinstance(s, int) else s.cuda_stream
+
+
+def version() -> str:
+    return _lib.gz_version().decode()
+
+
+class GameShape:
+    __slots__ = ("nodes", "rows", "cols", "actions", "features", "layers", "policy_per_node", "board_bytes", "nnz")
+
+    def __init__(self, v):
+        for k, x in zip(self.__slots__, v):
+            setattr(self, k, int(x))
+
+
+def game_shape(game: int) -> GameShape:
+    out = np.zeros(9, np.int32)
+    _check(_lib.gz_game_shape(game, _ptr(out, C.c_int32)))
+    return GameShape(out)
+
+
+def game_graph(game: int) -> tuple[np.ndarray, np.ndarray]:
+    s = game_shape(game)
+    rp = np.zeros(s.nodes + 1, np.int32)
+    col = np.zeros(s.nnz, np.int32)
+    _check(_lib.gz_game_graph(game, _ptr(rp, C.c_int32), _ptr(col, C.c_int32)))
+    return rp, col
+
+
+def next_state(game: int, board: np.ndarray, player: int, action: int) -> tuple[np.ndarray, int]:
+    b = np.ascontiguousarray(board, np.int8)
+    out = np.zeros_like(b)
+    np_ = C.c_int()
+    _check(_lib.gz_game_next_state(game, _ptr(b, C.c_int8), player, action, _ptr(out, C.c_int8), C.byref(np_)))
+    return out, np_.value
+
+
+def valid_moves(game: int, board: np.ndarray) -> np.ndarray:
+    b = np.ascontiguousarray(board, np.int8)
+    out = np.zeros(game_shape(game).actions, np.uint8)
+    _check(_lib.gz_game_valid_moves(game, _ptr(b, C.c_int8), _ptr(out, C.c_uint8)))
+    return out.astype(bool)
+
+
+def game_ended(game: int, board: np.ndarray, player: int) -> int:
+    b = np.ascontiguousarray(board, np.int8)
+    r = C.c_int()
+    _check(_lib.gz_game_ended(game, _ptr(b, C.c_int8), player, C.byref(r)))
+    return r.value
+
+
+def weight_count(game: int, kind: int = GAT) -> int:
+    return int(_lib.gz_weight_count(game, kind))
+
+
+def synth_weights(game: int, kind: int = GAT, seed: int = 0x6A5A, bias_scale: float = 0.0,
+                  bf16_exact: bool = True) -> np.ndarray:
+    n = weight_count(game, kind)
+    if n == 0:
+        raise GZError(ERR_INVALID_ARG, f"no weight layout for game {game} kind {kind}")
+    w = np.empty(n, np.float32)
+    _check(_lib.gz_synth_weights(game, kind, seed, bias_scale, int(bf16_exact), _ptr(w, C.c_float), n))
+    return w
+
+
+def synth_positions(game: int, n: int, seed: int = 0x6A5A, first: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    s = game_shape(game)
+    boards = np.zeros((n, s.board_bytes), np.int8)
+    side = np.zeros(n, np.int8)
+    _check(_lib.gz_synth_positions(game, seed, first, n, _ptr(boards, C.c_int8), _ptr(side, C.c_int8)))
+    return boards, side
+
+
+class Net:
+    """A network on one device: the INeuralNet replacement."""
+
+    def __init__(self, game: int, kind: int = GAT, device: int = 0, precision: int = PREC_AUTO,
+                 max_batch: int = 4096):
+        cfg = NetConfig(game, kind, precision, max_batch)
+        h = _vp()
+        _check(_lib.gz_net_create(C.byref(cfg), device, C.byref(h)))
+        self._h = h
+        self.game, self.kind, self.device, self.max_batch = game, kind, device, max_batch
+        self.shape = game_shape(game)
+
+    @property
+    def handle(self) -> int:
+        return self._h.value
+
+    def close(self) -> None:
+        if self._h:
+            _lib.gz_net_destroy(self._h)
+            self._h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass
+
+    def weight_count(self) -> int:
+        return int(_lib.gz_net_weight_count(self._h))
+
+    @property
+    def kernel_name(self) -> str:
+        return _lib.gz_net_kernel_name(self._h).decode()
+
+    def load_weights(self, blob: np.ndarray) -> None:
+        blob = np.ascontiguousarray(blob, np.float32)
+        _check(_lib.gz_net_load_weights(self._h, _ptr(blob, C.c_float), blob.size))
+
+    def save_weights(self) -> np.ndarray:
+        out = np.empty(self.weight_count(), np.float32)
+        _check(_lib.gz_net_save_weights(self._h, _ptr(out, C.c_float), out.size))
+        return out
+
+    def predict_batch(self, d_boards, d_side, n: int, d_pi, d_v, stream=None) -> None:
+        """Device-pointer batch evaluation (torch tensors or raw addresses)."""
+        _check(_lib.gz_net_predict_batch(self._h, _dev(d_boards), _dev(d_side), n, _dev(d_pi), _dev(d_v),
+                                         _stream(stream)))
+
+    def predict_host(self, boards: np.ndarray, side: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+        boards = np.ascontiguousarray(boards, np.int8)
+        side = np.ascontiguousarray(side, np.int8)
+        n = side.shape[0]
+        pi = np.empty((n, self.shape.actions), np.float32)
+        v = np.empty(n, np.float32)
+        _check(_lib.gz_net_predict_host(self._h, _ptr(boards, C.c_int8), _ptr(side, C.c_int8), n,
+                                        _ptr(pi, C.c_float), _ptr(v, C.c_float)))
+        return pi, v
+
+    def predict(self, canonical_board: np.ndarray) -> tuple[np.ndarray, float]:
+        """INeuralNet::predict: one canonical float board (own stones +1)."""
+        b = np.ascontiguousarray(canonical_board, np.float32).reshape(-1)
+        pi = np.empty(self.shape.actions, np.float32)
+        v = np.empty(1, np.float32)
+        _check(_lib.gz_net_predict(self._h, _ptr(b, C.c_float), _ptr(pi, C.c_float), _ptr(v, C.c_float)))
+        return pi, float(v[0])
+
+    def broadcast(self, comm: int, root: int = 0, stream=None) -> None:
+        _check(_lib.gz_net_broadcast(self._h, comm, root, _stream(stream)))
+
+
+def create_neural_net(net_type: str, game: int | str, device: int = 0, **kw) -> Net:
+    """Factory mirroring create_neural_net (networks/neural_network.c:6-13)."""
+    g = GAME_NAMES[game] if isinstance(game, str) else game
+    kinds = {"gat": GAT, "resnet": RESNET}
+    if net_type not in kinds:
+        raise GZError(ERR_INVALID_ARG, f"unknown network type {net_type!r}")
+    return Net(g, kinds[net_type], device=device, **kw)
+
+
+def nccl_unique_id() -> bytes:
+    buf = (C.c_uint8 * 128)()
+    _check(_lib.gz_nccl_unique_id(buf))
+    return bytes(buf)
+
+
+def nccl_comm_init(uid: bytes, world: int, rank: int, device: int) -> int:
+    buf = (C.c_uint8 * 128).from_buffer_copy(uid)
+    comm = _vp()
+    _check(_lib.gz_nccl_comm_init(buf, world, rank, device, C.byref(comm)))
+    return comm.value
+
+
+def nccl_comm_destroy(comm: int) -> None:
+    _check(_lib.gz_nccl_comm_destroy(comm))
+
+
+class Mcts:
+    """Batched PUCT search over `trees` concurrent games on one device."""
+
+    def __init__(self, game: int, trees: int, leaves_per_tree: int = 4, c_puct: float = 1.5, virtual_loss: int = 3,
+                 node_capacity: int = 4096, dirichlet_alpha: float = 1.0, dirichlet_eps: float = 0.0,
+                 seed: int = 0x6A5A, device: int = 0):
+        cfg = MctsConfig(game, trees, leaves_per_tree, c_puct, virtual_loss, node_capacity, dirichlet_alpha,
+                         dirichlet_eps, seed)
+        h = _vp()
+        _check(_lib.gz_mcts_create(C.byref(cfg), device, C.byref(h)))
+        self._h = h
+        self.game, self.trees, self.leaves, self.device = game, trees, leaves_per_tree, device
+        self.shape = game_shape(game)
+
+    def close(self) -> None:
+        if self._h:
+            _lib.gz_mcts_destroy(self._h)
+            self._h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass
+
+    def reset_roots(self, d_boards, d_side, stream=None) -> None:
+        _check(_lib.gz_mcts_reset_roots(self._h, _dev(d_boards), _dev(d_side), _stream(stream)))
+
+    def select(self, stream=None) -> None:
+        _check(_lib.gz_mcts_select(self._h, _stream(stream)))
+
+    def leaf_buffers(self) -> tuple[int, int, int]:
+        b, s, t = _vp(), _vp(), _vp()
+        _check(_lib.gz_mcts_leaf_buffers(self._h, C.byref(b), C.byref(s), C.byref(t)))
+        return b.value, s.value, t.value
+
+    def copy_leaves(self, stream=None) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+        L = self.trees * self.leaves
+        b = np.zeros((L, self.shape.nodes), np.int8)
+        s = np.zeros(L, np.int8)
+        t = np.zeros(L, np.int8)
+        _check(_lib.gz_mcts_copy_leaves(self._h, _ptr(b, C.c_int8), _ptr(s, C.c_int8), _ptr(t, C.c_int8),
+                                        _stream(stream)))
+        return b, s, t
+
+    def backup(self, d_pi, d_v, stream=None) -> None:
+        _check(_lib.gz_mcts_backup(self._h, _dev(d_pi), _dev(d_v), _stream(stream)))
+
+    def step(self, net: Net, stream=None) -> None:
+        _check(_lib.gz_mcts_step(self._h, net._h, _stream(stream)))
+
+    def run(self, net: Net, sims: int, stream=None) -> None:
+        _check(_lib.gz_mcts_run(self._h, net._h, sims, _stream(stream)))
+
+    def root_stats(self, stream=None) -> tuple[np.ndarray, np.ndarray]:
+        visits = np.zeros((self.trees, self.shape.actions), np.int32)
+        wsum = np.zeros((self.trees, self.shape.actions), np.float32)
+        _check(_lib.gz_mcts_root_stats(self._h, _ptr(visits, C.c_int32), _ptr(wsum, C.c_float), _stream(stream)))
+        return visits, wsum
+
+    def tree_sizes(self, stream=None) -> tuple[np.ndarray, np.ndarray]:
+        nodes = np.zeros(self.trees, np.int32)
+        edges = np.zeros(self.trees, np.int32)
+        _check(_lib.gz_mcts_tree_sizes(self._h, _ptr(nodes, C.c_int32), _ptr(edges, C.c_int32), _stream(stream)))
+        return nodes, edges
+
+    def choose(self, temp_moves: int, d_actions, stream=None) -> None:
+        _check(_lib.gz_mcts_choose(self._h, temp_moves, _dev(d_actions), _stream(stream)))
+
+    def play(self, d_actions, reserve: int, d_done=None, stream=None) -> None:
+        _check(_lib.gz_mcts_play(self._h, _dev(d_actions), reserve, _dev(d_done), _stream(stream)))
+
+    def check(self) -> None:
+        _check(_lib.gz_mcts_check(self._h))
+
+
+def loaded_library_path() -> str:
+    return os.fspath(LIB_PATH)

@@ -1,0 +1,635 @@
+// C ABI implementation: handles, argument checks, status codes, the
+// host-buffer and single-position compatibility calls, NCCL weight broadcast,
+// and the batched search driver.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <vector>
+
+#include "../../include/graphzero_b200.h"
+#include "gz_games.h"
+#include "gz_internal.h"
+#include "gz_mcts.h"
+#include "gz_synth.h"
+
+using namespace gz;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+gz_status fail(gz_status s, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return s;
+}
+
+#define GZ_CUDA(call)                                                                                  \
+  do {                                                                                                 \
+    cudaError_t e_ = (call);                                                                           \
+    if (e_ != cudaSuccess) return fail(GZ_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                       __FILE__, __LINE__);                                           \
+  } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) ok = true;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+#define GZ_DEVICE(dev)                                                                      \
+  DeviceGuard guard_((dev));                                                                \
+  if (!guard_.ok) return fail(GZ_ERR_CUDA, "cannot select CUDA device %d", (int)(dev));
+
+bool valid_game(int g) { return g == kTicTacToe || g == kConnect4 || g == kChess; }
+
+// ---- NCCL, resolved at run time so the library has no link-time NCCL
+// dependency (and shares the NCCL already loaded by the host process). ----
+struct Nccl {
+  void* h = nullptr;
+  ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*errorString)(ncclResult_t) = nullptr;
+};
+
+Nccl* nccl() {
+  static Nccl n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* names[] = {"libnccl.so.2", "libnccl.so"};
+    for (const char* nm : names)
+      if ((n.h = dlopen(nm, RTLD_NOW | RTLD_LOCAL))) break;
+    if (!n.h) return;
+    n.getUniqueId = (decltype(n.getUniqueId))dlsym(n.h, "ncclGetUniqueId");
+    n.commInitRank = (decltype(n.commInitRank))dlsym(n.h, "ncclCommInitRank");
+    n.commDestroy = (decltype(n.commDestroy))dlsym(n.h, "ncclCommDestroy");
+    n.broadcast = (decltype(n.broadcast))dlsym(n.h, "ncclBroadcast");
+    n.errorString = (decltype(n.errorString))dlsym(n.h, "ncclGetErrorString");
+  });
+  if (!n.h || !n.getUniqueId || !n.commInitRank || !n.commDestroy || !n.broadcast) return nullptr;
+  return &n;
+}
+
+}  // namespace
+
+struct gz_net {
+  int game, kind, precision, device, max_batch;
+  size_t weight_count;
+  float* d_weights = nullptr;  // fp32 blob (source of truth on the device)
+  int* d_csr = nullptr;        // row_ptr + col
+  void* d_tc = nullptr;        // tensor-core packed weights (bf16 path)
+  size_t tc_bytes = 0;
+  // host-call staging
+  int8_t *h_in = nullptr, *d_in = nullptr;
+  float *h_out = nullptr, *d_out = nullptr;
+  cudaStream_t stream = nullptr;
+};
+
+struct gz_mcts {
+  MctsDev d{};
+  int device;
+  std::vector<void*> allocs;
+  float *d_pi = nullptr, *d_v = nullptr;
+  int32_t* d_tmp = nullptr;
+};
+
+namespace {
+
+bool use_tensor_cores(const gz_net* n) {
+  if (n->kind != GZ_NET_GAT) return false;
+  if (n->precision == GZ_PREC_FP32) return false;
+  if (n->precision == GZ_PREC_BF16 || n->precision == GZ_PREC_FP16) return true;
+  return n->game != kTicTacToe && gat_tc_packed_bytes(n->game) > 0;  // AUTO
+}
+
+gz_status prepare_weights(gz_net* n, cudaStream_t s) {
+  if (n->kind == GZ_NET_GAT && use_tensor_cores(n)) {
+    GZ_CUDA(launch_gat_tc_pack(n->game, n->d_weights, n->d_tc, s));
+  }
+  return GZ_OK;
+}
+
+gz_status run_forward(gz_net* n, const int8_t* boards, const int8_t* side, int count, float* pi, float* v,
+                      cudaStream_t s) {
+  if (n->kind == GZ_NET_GAT) {
+    if (use_tensor_cores(n))
+      GZ_CUDA(launch_gat_tc(n->game, n->d_tc, n->d_weights, boards, side, count, pi, v, s));
+    else
+      GZ_CUDA(launch_gat_simt(n->game, n->d_weights, n->d_csr, boards, side, count, pi, v, s));
+    return GZ_OK;
+  }
+  return fail(GZ_ERR_UNSUPPORTED, "network kind %d has no kernel in this build", n->kind);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gz_status_string(gz_status s) {
+  switch (s) {
+    case GZ_OK: return "ok";
+    case GZ_ERR_INVALID_ARG: return "invalid argument";
+    case GZ_ERR_CUDA: return "CUDA error";
+    case GZ_ERR_NCCL: return "NCCL error";
+    case GZ_ERR_TIMEOUT: return "timeout";
+    case GZ_ERR_IO: return "I/O error";
+    case GZ_ERR_CAPACITY: return "capacity exceeded";
+    case GZ_ERR_UNSUPPORTED: return "unsupported";
+  }
+  return "unknown status";
+}
+
+const char* gz_last_error(void) { return g_err; }
+const char* gz_version(void) { return "graphzero_b200 0.1 (sm_100a)"; }
+
+gz_status gz_game_shape(int game, int32_t out[9]) {
+  if (!valid_game(game) || !out) return fail(GZ_ERR_INVALID_ARG, "bad game %d", game);
+  GameShape s = game_shape(game);
+  int32_t v[9] = {s.nodes, s.rows, s.cols, s.actions, s.features, s.layers, s.policy_out, s.board_bytes, s.nnz};
+  memcpy(out, v, sizeof v);
+  return GZ_OK;
+}
+
+gz_status gz_game_graph(int game, int32_t* row_ptr, int32_t* col) {
+  if (!valid_game(game) || !row_ptr || !col) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  build_graph_csr(game, row_ptr, col);
+  return GZ_OK;
+}
+
+gz_status gz_game_next_state(int game, const int8_t* board, int player, int action, int8_t* next_board,
+                             int* next_player) {
+  if ((game != kTicTacToe && game != kConnect4) || !board || !next_board || !next_player || (player != 1 && player != -1))
+    return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  GameShape s = game_shape(game);
+  if (action < 0 || action >= s.actions || !action_legal(game, board, action))
+    return fail(GZ_ERR_INVALID_ARG, "illegal action %d", action);
+  memmove(next_board, board, (size_t)s.nodes);
+  apply_action(game, next_board, action, player);
+  *next_player = -player;
+  return GZ_OK;
+}
+
+gz_status gz_game_valid_moves(int game, const int8_t* board, uint8_t* valid) {
+  if ((game != kTicTacToe && game != kConnect4) || !board || !valid) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  GameShape s = game_shape(game);
+  for (int a = 0; a < s.actions; ++a) valid[a] = action_legal(game, board, a) ? 1 : 0;
+  return GZ_OK;
+}
+
+gz_status gz_game_ended(int game, const int8_t* board, int player, int* result) {
+  if ((game != kTicTacToe && game != kConnect4) || !board || !result || (player != 1 && player != -1))
+    return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  GameShape s = game_shape(game);
+  // A win is a line through some stone; check every stone of each player.
+  int won = 0;
+  for (int p = 1; p >= -1 && !won; p -= 2)
+    for (int i = 0; i < s.nodes && !won; ++i)
+      if (board[i] == p) {
+        bool w = game == kConnect4 ? c4_win_through(board, i / 7, i % 7, p) : ttt_line_win(board, p);
+        if (w) won = p;
+      }
+  if (won) {
+    *result = won == player ? 1 : -1;
+    return GZ_OK;
+  }
+  bool full = true;
+  for (int a = 0; a < s.actions; ++a)
+    if (action_legal(game, board, a)) full = false;
+  *result = full ? 2 : 0;
+  return GZ_OK;
+}
+
+size_t gz_weight_count(int game, int kind) {
+  if (kind == GZ_NET_RESNET) return game == kConnect4 ? res_layout().total : 0;
+  if (kind == GZ_NET_GAT && valid_game(game)) return gat_layout(game).total;
+  return 0;
+}
+
+gz_status gz_synth_weights(int game, int kind, uint64_t seed, float bias_scale, int bf16_exact, float* out,
+                           size_t n_floats) {
+  size_t need = gz_weight_count(game, kind);
+  if (!need || !out || n_floats != need) return fail(GZ_ERR_INVALID_ARG, "weight buffer must hold %zu floats", need);
+  WeightOpts o;
+  o.bias_scale = bias_scale;
+  o.bf16_exact = bf16_exact != 0;
+  if (kind == GZ_NET_GAT) make_gat_weights(game, seed, o, out);
+  else make_resnet_weights(seed, o, out);
+  return GZ_OK;
+}
+
+gz_status gz_synth_positions(int game, uint64_t seed, uint64_t first, int n, int8_t* boards, int8_t* side) {
+  if (!valid_game(game) || n < 0 || (n > 0 && (!boards || !side))) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  if (game == kChess) return fail(GZ_ERR_UNSUPPORTED, "chess positions are not generated by this build");
+  GameShape s = game_shape(game);
+  for (int i = 0; i < n; ++i) side[i] = (int8_t)make_position(game, seed, first + (uint64_t)i, boards + (size_t)i * s.board_bytes);
+  return GZ_OK;
+}
+
+gz_status gz_net_create(const gz_net_config* cfg, int device, gz_net** out) {
+  if (!cfg || !out) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  if (!valid_game(cfg->game)) return fail(GZ_ERR_INVALID_ARG, "bad game %d", cfg->game);
+  if (cfg->kind != GZ_NET_GAT && cfg->kind != GZ_NET_RESNET) return fail(GZ_ERR_INVALID_ARG, "bad kind %d", cfg->kind);
+  if (cfg->kind == GZ_NET_RESNET && cfg->game != kConnect4)
+    return fail(GZ_ERR_UNSUPPORTED, "the ResNet tower is built for Connect4 only");
+  if (cfg->precision < GZ_PREC_AUTO || cfg->precision > GZ_PREC_FP16) return fail(GZ_ERR_INVALID_ARG, "bad precision");
+  if (cfg->max_batch < 0) return fail(GZ_ERR_INVALID_ARG, "bad max_batch");
+  int ndev = 0;
+  GZ_CUDA(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return fail(GZ_ERR_INVALID_ARG, "device %d of %d", device, ndev);
+  GZ_DEVICE(device);
+  gz_net* n = new gz_net();
+  n->game = cfg->game;
+  n->kind = cfg->kind;
+  n->precision = cfg->precision;
+  n->device = device;
+  n->max_batch = cfg->max_batch > 0 ? cfg->max_batch : 1;
+  n->weight_count = gz_weight_count(cfg->game, cfg->kind);
+  GameShape s = game_shape(cfg->game);
+  gz_status st = GZ_OK;
+  auto chk = [&](cudaError_t e, const char* what) {
+    if (e != cudaSuccess && st == GZ_OK) st = fail(GZ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  };
+  chk(cudaMalloc(&n->d_weights, n->weight_count * sizeof(float)), "cudaMalloc weights");
+  chk(cudaMemset(n->d_weights, 0, n->weight_count * sizeof(float)), "cudaMemset weights");
+  std::vector<int> csr(s.nodes + 1 + s.nnz);
+  build_graph_csr(cfg->game, csr.data(), csr.data() + s.nodes + 1);
+  chk(cudaMalloc(&n->d_csr, csr.size() * sizeof(int)), "cudaMalloc csr");
+  chk(cudaMemcpy(n->d_csr, csr.data(), csr.size() * sizeof(int), cudaMemcpyHostToDevice), "copy csr");
+  if (use_tensor_cores(n)) {
+    n->tc_bytes = gat_tc_packed_bytes(cfg->game);
+    if (!n->tc_bytes && st == GZ_OK) st = fail(GZ_ERR_UNSUPPORTED, "no tensor-core kernel for game %d", cfg->game);
+    else chk(cudaMalloc(&n->d_tc, n->tc_bytes), "cudaMalloc packed weights");
+  }
+  size_t in_bytes = (size_t)n->max_batch * (s.board_bytes + 1);
+  size_t out_floats = (size_t)n->max_batch * (s.actions + 1);
+  chk(cudaMallocHost(&n->h_in, in_bytes), "cudaMallocHost in");
+  chk(cudaMalloc(&n->d_in, in_bytes), "cudaMalloc in");
+  chk(cudaMallocHost(&n->h_out, out_floats * sizeof(float)), "cudaMallocHost out");
+  chk(cudaMalloc(&n->d_out, out_floats * sizeof(float)), "cudaMalloc out");
+  chk(cudaStreamCreateWithFlags(&n->stream, cudaStreamNonBlocking), "stream");
+  if (st == GZ_OK) {
+    gz_status p = prepare_weights(n, n->stream);
+    if (p != GZ_OK) st = p;
+  }
+  if (st == GZ_OK) chk(cudaStreamSynchronize(n->stream), "sync");
+  if (st != GZ_OK) {
+    gz_net_destroy(n);
+    return st;
+  }
+  *out = n;
+  return GZ_OK;
+}
+
+gz_status gz_net_destroy(gz_net* n) {
+  if (!n) return GZ_OK;
+  DeviceGuard g(n->device);
+  if (n->stream) cudaStreamSynchronize(n->stream);
+  cudaFree(n->d_weights);
+  cudaFree(n->d_csr);
+  cudaFree(n->d_tc);
+  cudaFreeHost(n->h_in);
+  cudaFree(n->d_in);
+  cudaFreeHost(n->h_out);
+  cudaFree(n->d_out);
+  if (n->stream) cudaStreamDestroy(n->stream);
+  delete n;
+  return GZ_OK;
+}
+
+size_t gz_net_weight_count(const gz_net* n) { return n ? n->weight_count : 0; }
+
+const char* gz_net_kernel_name(const gz_net* n) {
+  if (!n) return "";
+  if (n->kind == GZ_NET_RESNET) return "resnet_tc_bf16";
+  if (!use_tensor_cores(n)) return "gat_simt_fp32";
+  return n->precision == GZ_PREC_FP16 ? "gat_tc_fp16" : "gat_tc_bf16";
+}
+
+gz_status gz_net_load_weights(gz_net* n, const float* blob, size_t count) {
+  if (!n || !blob) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  if (count != n->weight_count) return fail(GZ_ERR_INVALID_ARG, "weight blob has %zu floats, expected %zu", count, n->weight_count);
+  GZ_DEVICE(n->device);
+  GZ_CUDA(cudaMemcpyAsync(n->d_weights, blob, count * sizeof(float), cudaMemcpyHostToDevice, n->stream));
+  gz_status p = prepare_weights(n, n->stream);
+  if (p != GZ_OK) return p;
+  GZ_CUDA(cudaStreamSynchronize(n->stream));
+  return GZ_OK;
+}
+
+gz_status gz_net_save_weights(const gz_net* n, float* blob, size_t count) {
+  if (!n || !blob) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  if (count != n->weight_count) return fail(GZ_ERR_INVALID_ARG, "weight blob has %zu floats, expected %zu", count, n->weight_count);
+  GZ_DEVICE(n->device);
+  GZ_CUDA(cudaMemcpyAsync(blob, n->d_weights, count * sizeof(float), cudaMemcpyDeviceToHost, n->stream));
+  GZ_CUDA(cudaStreamSynchronize(n->stream));
+  return GZ_OK;
+}
+
+gz_status gz_net_predict_batch(gz_net* n, const int8_t* boards, const int8_t* side, int count, float* pi, float* v,
+                               void* stream) {
+  if (!n) return fail(GZ_ERR_INVALID_ARG, "null net");
+  if (count < 0) return fail(GZ_ERR_INVALID_ARG, "negative batch");
+  if (count == 0) return GZ_OK;
+  if (!boards || !side || !pi || !v) return fail(GZ_ERR_INVALID_ARG, "null buffer");
+  GZ_DEVICE(n->device);
+  return run_forward(n, boards, side, count, pi, v, (cudaStream_t)stream);
+}
+
+gz_status gz_net_predict_host(gz_net* n, const int8_t* boards, const int8_t* side, int count, float* pi, float* v) {
+  if (!n) return fail(GZ_ERR_INVALID_ARG, "null net");
+  if (count < 0 || count > n->max_batch) return fail(GZ_ERR_INVALID_ARG, "batch %d outside [0, %d]", count, n->max_batch);
+  if (count == 0) return GZ_OK;
+  if (!boards || !side || !pi || !v) return fail(GZ_ERR_INVALID_ARG, "null buffer");
+  GZ_DEVICE(n->device);
+  GameShape s = game_shape(n->game);
+  size_t bb = (size_t)count * s.board_bytes;
+  memcpy(n->h_in, boards, bb);
+  memcpy(n->h_in + bb, side, (size_t)count);
+  GZ_CUDA(cudaMemcpyAsync(n->d_in, n->h_in, bb + count, cudaMemcpyHostToDevice, n->stream));
+  float* d_pi = n->d_out;
+  float* d_v = n->d_out + (size_t)count * s.actions;
+  gz_status st = run_forward(n, n->d_in, n->d_in + bb, count, d_pi, d_v, n->stream);
+  if (st != GZ_OK) return st;
+  size_t outf = (size_t)count * (s.actions + 1);
+  GZ_CUDA(cudaMemcpyAsync(n->h_out, n->d_out, outf * sizeof(float), cudaMemcpyDeviceToHost, n->stream));
+  GZ_CUDA(cudaStreamSynchronize(n->stream));
+  memcpy(pi, n->h_out, (size_t)count * s.actions * sizeof(float));
+  memcpy(v, n->h_out + (size_t)count * s.actions, (size_t)count * sizeof(float));
+  return GZ_OK;
+}
+
+gz_status gz_net_predict(gz_net* n, const float* h_board, float* h_pi, float* h_v) {
+  if (!n || !h_board || !h_pi || !h_v) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  if (n->game == kChess) return fail(GZ_ERR_UNSUPPORTED, "single-position chess boards need the full position record");
+  GameShape s = game_shape(n->game);
+  // Canonical board: own stones +1.  The side to move is the first player
+  // iff both players have placed the same number of stones.
+  int own = 0, opp = 0;
+  for (int i = 0; i < s.nodes; ++i) {
+    float x = h_board[i];
+    if (x != 0.f && x != 1.f && x != -1.f) return fail(GZ_ERR_INVALID_ARG, "board cell %d = %g not in {-1,0,1}", i, x);
+    own += x == 1.f;
+    opp += x == -1.f;
+  }
+  int8_t side = own == opp ? 1 : -1;
+  int8_t b[64];
+  for (int i = 0; i < s.nodes; ++i) b[i] = (int8_t)((int)h_board[i] * side);
+  return gz_net_predict_host(n, b, &side, 1, h_pi, h_v);
+}
+
+gz_status gz_nccl_unique_id(uint8_t out[128]) {
+  Nccl* c = nccl();
+  if (!c) return fail(GZ_ERR_NCCL, "libnccl.so.2 not loadable");
+  if (!out) return fail(GZ_ERR_INVALID_ARG, "null id");
+  ncclUniqueId id;
+  ncclResult_t r = c->getUniqueId(&id);
+  if (r != ncclSuccess) return fail(GZ_ERR_NCCL, "ncclGetUniqueId: %d", (int)r);
+  static_assert(sizeof(id) == 128, "ncclUniqueId size");
+  memcpy(out, &id, 128);
+  return GZ_OK;
+}
+
+gz_status gz_nccl_comm_init(const uint8_t id_bytes[128], int world, int rank, int device, void** comm) {
+  Nccl* c = nccl();
+  if (!c) return fail(GZ_ERR_NCCL, "libnccl.so.2 not loadable");
+  if (!id_bytes || !comm || world <= 0 || rank < 0 || rank >= world) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  GZ_DEVICE(device);
+  ncclUniqueId id;
+  memcpy(&id, id_bytes, 128);
+  ncclComm_t cm = nullptr;
+  ncclResult_t r = c->commInitRank(&cm, world, id, rank);
+  if (r != ncclSuccess) return fail(GZ_ERR_NCCL, "ncclCommInitRank: %s", c->errorString ? c->errorString(r) : "?");
+  *comm = cm;
+  return GZ_OK;
+}
+
+gz_status gz_nccl_comm_destroy(void* comm) {
+  Nccl* c = nccl();
+  if (!c) return fail(GZ_ERR_NCCL, "libnccl.so.2 not loadable");
+  if (comm) c->commDestroy((ncclComm_t)comm);
+  return GZ_OK;
+}
+
+gz_status gz_net_broadcast(gz_net* n, void* comm, int root, void* stream) {
+  if (!n || !comm) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  Nccl* c = nccl();
+  if (!c) return fail(GZ_ERR_NCCL, "libnccl.so.2 not loadable");
+  GZ_DEVICE(n->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  ncclResult_t r = c->broadcast(n->d_weights, n->d_weights, n->weight_count, ncclFloat32, root, (ncclComm_t)comm, s);
+  if (r != ncclSuccess) return fail(GZ_ERR_NCCL, "ncclBroadcast: %s", c->errorString ? c->errorString(r) : "?");
+  return prepare_weights(n, s);
+}
+
+// ---------------------------------------------------------------- search --
+gz_status gz_mcts_create(const gz_mcts_config* cfg, int device, gz_mcts** out) {
+  if (!cfg || !out) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  if (cfg->game != kTicTacToe && cfg->game != kConnect4)
+    return fail(GZ_ERR_UNSUPPORTED, "the batched search supports TicTacToe and Connect4");
+  if (cfg->trees <= 0 || cfg->leaves_per_tree <= 0 || cfg->node_capacity < 2 || cfg->virtual_loss < 0)
+    return fail(GZ_ERR_INVALID_ARG, "bad search sizes");
+  if (!(cfg->c_puct >= 0.f) || !(cfg->dirichlet_eps >= 0.f && cfg->dirichlet_eps <= 1.f) ||
+      (cfg->dirichlet_eps > 0.f && !(cfg->dirichlet_alpha > 0.f)))
+    return fail(GZ_ERR_INVALID_ARG, "bad search constants");
+  int ndev = 0;
+  GZ_CUDA(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return fail(GZ_ERR_INVALID_ARG, "device %d of %d", device, ndev);
+  GZ_DEVICE(device);
+  gz_mcts* m = new gz_mcts();
+  m->device = device;
+  MctsDev& d = m->d;
+  GameShape s = game_shape(cfg->game);
+  d.game = cfg->game;
+  d.trees = cfg->trees;
+  d.leaves = cfg->leaves_per_tree;
+  d.vl_k = cfg->virtual_loss;
+  d.node_cap = cfg->node_capacity;
+  d.edge_cap = cfg->node_capacity * s.actions;
+  d.N = s.nodes;
+  d.A = s.actions;
+  d.c_puct = cfg->c_puct;
+  d.dir_alpha = cfg->dirichlet_alpha;
+  d.dir_eps = cfg->dirichlet_eps;
+  d.seed = cfg->seed;
+  const size_t T = (size_t)d.trees, NC = T * d.node_cap, EC = T * d.edge_cap, L = T * d.leaves;
+  gz_status st = GZ_OK;
+  auto alloc = [&](auto** p, size_t bytes) {
+    if (st != GZ_OK) return;
+    cudaError_t e = cudaMalloc((void**)p, bytes ? bytes : 1);
+    if (e != cudaSuccess) st = fail(GZ_ERR_CUDA, "cudaMalloc %zu bytes: %s", bytes, cudaGetErrorString(e));
+    else m->allocs.push_back((void*)*p);
+  };
+  alloc(&d.n, NC * 4); alloc(&d.vl, NC * 4); alloc(&d.first_edge, NC * 4); alloc(&d.n_edges, NC);
+  alloc(&d.side, NC); alloc(&d.expanded, NC); alloc(&d.terminal, NC); alloc(&d.term_value, NC * 4);
+  alloc(&d.board, NC * kMctsBoardStride);
+  alloc(&d.P, EC * 4); alloc(&d.W, EC * 4); alloc(&d.Nv, EC * 4); alloc(&d.VL, EC * 4); alloc(&d.child, EC * 4);
+  alloc(&d.action, EC);
+  alloc(&d.root, T * 4); alloc(&d.node_count, T * 4); alloc(&d.edge_count, T * 4); alloc(&d.move_no, T * 4);
+  alloc(&d.path_nodes, L * kMctsMaxDepth * 4); alloc(&d.path_edges, L * kMctsMaxDepth * 4); alloc(&d.path_len, L * 4);
+  alloc(&d.leaf_board, L * d.N); alloc(&d.leaf_side, L); alloc(&d.leaf_terminal, L);
+  alloc(&d.err, 4);
+  alloc(&m->d_pi, L * d.A * 4); alloc(&m->d_v, L * 4);
+  alloc(&m->d_tmp, T * 4 * 2);
+  if (st == GZ_OK) {
+    cudaError_t e = cudaMemset(d.err, 0, 4);
+    if (e == cudaSuccess) e = cudaMemset(d.root, 0, T * 4);
+    if (e == cudaSuccess) e = cudaMemset(d.node_count, 0, T * 4);
+    if (e == cudaSuccess) e = cudaMemset(d.expanded, 0, NC);
+    if (e == cudaSuccess) e = cudaMemset(d.path_len, 0, L * 4);
+    if (e == cudaSuccess) e = cudaMemset(d.path_nodes, 0, L * kMctsMaxDepth * 4);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) st = fail(GZ_ERR_CUDA, "init: %s", cudaGetErrorString(e));
+  }
+  if (st != GZ_OK) {
+    gz_mcts_destroy(m);
+    return st;
+  }
+  *out = m;
+  return GZ_OK;
+}
+
+gz_status gz_mcts_destroy(gz_mcts* m) {
+  if (!m) return GZ_OK;
+  DeviceGuard g(m->device);
+  cudaDeviceSynchronize();
+  for (void* p : m->allocs) cudaFree(p);
+  delete m;
+  return GZ_OK;
+}
+
+gz_status gz_mcts_reset_roots(gz_mcts* m, const int8_t* boards, const int8_t* side, void* stream) {
+  if (!m || !boards || !side) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  GZ_DEVICE(m->device);
+  GZ_CUDA(mcts_launch_reset(m->d, boards, side, (cudaStream_t)stream));
+  return GZ_OK;
+}
+
+gz_status gz_mcts_select(gz_mcts* m, void* stream) {
+  if (!m) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  GZ_DEVICE(m->device);
+  GZ_CUDA(mcts_launch_select(m->d, (cudaStream_t)stream));
+  return GZ_OK;
+}
+
+gz_status gz_mcts_leaf_buffers(gz_mcts* m, int8_t** boards, int8_t** side, int8_t** terminal) {
+  if (!m) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  if (boards) *boards = m->d.leaf_board;
+  if (side) *side = m->d.leaf_side;
+  if (terminal) *terminal = m->d.leaf_terminal;
+  return GZ_OK;
+}
+
+gz_status gz_mcts_copy_leaves(gz_mcts* m, int8_t* boards, int8_t* side, int8_t* terminal, void* stream) {
+  if (!m) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  GZ_DEVICE(m->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  size_t L = (size_t)m->d.trees * m->d.leaves;
+  if (boards) GZ_CUDA(cudaMemcpyAsync(boards, m->d.leaf_board, L * m->d.N, cudaMemcpyDeviceToHost, s));
+  if (side) GZ_CUDA(cudaMemcpyAsync(side, m->d.leaf_side, L, cudaMemcpyDeviceToHost, s));
+  if (terminal) GZ_CUDA(cudaMemcpyAsync(terminal, m->d.leaf_terminal, L, cudaMemcpyDeviceToHost, s));
+  GZ_CUDA(cudaStreamSynchronize(s));
+  return GZ_OK;
+}
+
+gz_status gz_mcts_backup(gz_mcts* m, const float* pi, const float* v, void* stream) {
+  if (!m || !pi || !v) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  GZ_DEVICE(m->device);
+  GZ_CUDA(mcts_launch_backup(m->d, pi, v, (cudaStream_t)stream));
+  return GZ_OK;
+}
+
+gz_status gz_mcts_step(gz_mcts* m, gz_net* net, void* stream) {
+  if (!m || !net) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  if (net->game != m->d.game) return fail(GZ_ERR_INVALID_ARG, "net and search play different games");
+  if (net->device != m->device) return fail(GZ_ERR_INVALID_ARG, "net and search live on different devices");
+  GZ_DEVICE(m->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  GZ_CUDA(mcts_launch_select(m->d, s));
+  gz_status st = run_forward(net, m->d.leaf_board, m->d.leaf_side, m->d.trees * m->d.leaves, m->d_pi, m->d_v, s);
+  if (st != GZ_OK) return st;
+  GZ_CUDA(mcts_launch_backup(m->d, m->d_pi, m->d_v, s));
+  return GZ_OK;
+}
+
+gz_status gz_mcts_run(gz_mcts* m, gz_net* net, int sims, void* stream) {
+  if (!m || !net || sims < 0) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  int waves = (sims + m->d.leaves - 1) / m->d.leaves;
+  for (int w = 0; w < waves; ++w) {
+    gz_status st = gz_mcts_step(m, net, stream);
+    if (st != GZ_OK) return st;
+  }
+  return GZ_OK;
+}
+
+gz_status gz_mcts_check(gz_mcts* m) {
+  if (!m) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  GZ_DEVICE(m->device);
+  int err = 0;
+  GZ_CUDA(cudaMemcpy(&err, m->d.err, 4, cudaMemcpyDeviceToHost));
+  if (err == kMctsNodeCap) return fail(GZ_ERR_CAPACITY, "search node pool exhausted (node_capacity %d)", m->d.node_cap);
+  if (err == kMctsEdgeCap) return fail(GZ_ERR_CAPACITY, "search edge pool exhausted");
+  if (err == kMctsDepth) return fail(GZ_ERR_CAPACITY, "search path deeper than %d", kMctsMaxDepth);
+  return GZ_OK;
+}
+
+gz_status gz_mcts_root_stats(gz_mcts* m, int32_t* visits, float* wsum, void* stream) {
+  if (!m || !visits) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  GZ_DEVICE(m->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  size_t cnt = (size_t)m->d.trees * m->d.A;
+  int32_t* dv = nullptr;
+  float* dw = nullptr;
+  GZ_CUDA(cudaMallocAsync((void**)&dv, cnt * 4, s));
+  GZ_CUDA(cudaMallocAsync((void**)&dw, cnt * 4, s));
+  GZ_CUDA(mcts_launch_root_visits(m->d, dv, dw, s));
+  GZ_CUDA(cudaMemcpyAsync(visits, dv, cnt * 4, cudaMemcpyDeviceToHost, s));
+  if (wsum) GZ_CUDA(cudaMemcpyAsync(wsum, dw, cnt * 4, cudaMemcpyDeviceToHost, s));
+  GZ_CUDA(cudaFreeAsync(dv, s));
+  GZ_CUDA(cudaFreeAsync(dw, s));
+  GZ_CUDA(cudaStreamSynchronize(s));
+  return gz_mcts_check(m);
+}
+
+gz_status gz_mcts_tree_sizes(gz_mcts* m, int32_t* nodes, int32_t* edges, void* stream) {
+  if (!m || !nodes || !edges) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  GZ_DEVICE(m->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  GZ_CUDA(mcts_launch_tree_sizes(m->d, m->d_tmp, m->d_tmp + m->d.trees, s));
+  GZ_CUDA(cudaMemcpyAsync(nodes, m->d_tmp, (size_t)m->d.trees * 4, cudaMemcpyDeviceToHost, s));
+  GZ_CUDA(cudaMemcpyAsync(edges, m->d_tmp + m->d.trees, (size_t)m->d.trees * 4, cudaMemcpyDeviceToHost, s));
+  GZ_CUDA(cudaStreamSynchronize(s));
+  return GZ_OK;
+}
+
+gz_status gz_mcts_choose(gz_mcts* m, int temp_moves, int32_t* actions, void* stream) {
+  if (!m || !actions) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  GZ_DEVICE(m->device);
+  GZ_CUDA(mcts_launch_choose(m->d, temp_moves, actions, (cudaStream_t)stream));
+  return GZ_OK;
+}
+
+gz_status gz_mcts_play(gz_mcts* m, const int32_t* actions, int reserve, int8_t* done, void* stream) {
+  if (!m || !actions || reserve < 0) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  GZ_DEVICE(m->device);
+  GZ_CUDA(mcts_launch_play(m->d, actions, reserve, done, (cudaStream_t)stream));
+  return GZ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,26 @@
+// Internal declarations shared by the graphzero_b200 CUDA translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gz_games.h"
+
+namespace gz {
+
+// fp32 SIMT fused GAT forward (all layers + heads, one launch).
+//   boards [n][BOARD] int8, side [n] int8 (+1 / -1),
+//   weights: fp32 blob in gat_layout() order,
+//   csr: row_ptr [N+1] followed by col [nnz] (build_graph_csr order),
+//   pi [n][A] fp32, v [n] fp32.
+cudaError_t launch_gat_simt(int game, const float* d_weights, const int* d_csr, const int8_t* d_boards,
+                            const int8_t* d_side, int n, float* d_pi, float* d_v, cudaStream_t stream);
+
+// bf16 tensor-core (tcgen05) GAT forward for Connect4 and chess.
+// gat_tc_packed_bytes(game) is 0 when the game has no tensor-core kernel.
+size_t gat_tc_packed_bytes(int game);
+// Converts the fp32 blob into the kernel's operand layout (bf16 weight tiles).
+cudaError_t launch_gat_tc_pack(int game, const float* d_weights, void* d_packed, cudaStream_t stream);
+cudaError_t launch_gat_tc(int game, const void* d_packed, const float* d_weights, const int8_t* d_boards,
+                          const int8_t* d_side, int n, float* d_pi, float* d_v, cudaStream_t stream);
+
+}  // namespace gz

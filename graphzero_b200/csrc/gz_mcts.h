@@ -1,0 +1,64 @@
+// Device-side state of the batched PUCT search (structure of arrays).
+//
+// Every tree owns a private pool of nodes and edges; indices are local to the
+// tree (global = tree * cap + local).  A node keeps its position so a leaf can
+// be encoded without replaying the path.  This replaces the reference's
+// MCTSNode with fixed 218-entry child arrays and child pointers
+// (mcts/mcts.cuh:25-36).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gz {
+
+constexpr int kMctsBoardStride = 48;  // bytes per stored position (>= 42, 16-aligned)
+constexpr int kMctsMaxDepth = 48;     // >= longest game (42 plies) + 1
+
+struct MctsDev {
+  int game, trees, leaves, vl_k, node_cap, edge_cap, N, A;
+  float c_puct, dir_alpha, dir_eps;
+  unsigned long long seed;
+  // nodes [trees * node_cap]
+  int* n;           // completed backups through the node
+  int* vl;          // selections in flight through the node
+  int* first_edge;  // local edge index of the first child edge
+  int8_t* n_edges;
+  int8_t* side;     // player to move at the node
+  int8_t* expanded;
+  int8_t* terminal;
+  float* term_value;  // value for the player to move at a terminal node
+  int8_t* board;      // [trees * node_cap][kMctsBoardStride]
+  // edges [trees * edge_cap]
+  float* P;
+  float* W;  // value sum from the perspective of the player to move at the parent
+  int* Nv;   // visit count
+  int* VL;   // virtual visits in flight
+  int* child;
+  int8_t* action;
+  // per tree
+  int* root;
+  int* node_count;
+  int* edge_count;
+  int* move_no;
+  // selection paths [trees][leaves][kMctsMaxDepth]
+  int* path_nodes;
+  int* path_edges;
+  int* path_len;  // [trees][leaves]
+  // leaf batch (network input) [trees * leaves]
+  int8_t* leaf_board;  // [trees * leaves][N]
+  int8_t* leaf_side;
+  int8_t* leaf_terminal;
+  int* err;  // first error code seen by a kernel (0 = none)
+};
+
+enum MctsErr : int { kMctsOk = 0, kMctsNodeCap = 1, kMctsEdgeCap = 2, kMctsDepth = 3 };
+
+cudaError_t mcts_launch_reset(const MctsDev& d, const int8_t* boards, const int8_t* side, cudaStream_t s);
+cudaError_t mcts_launch_select(const MctsDev& d, cudaStream_t s);
+cudaError_t mcts_launch_backup(const MctsDev& d, const float* pi, const float* v, cudaStream_t s);
+cudaError_t mcts_launch_root_visits(const MctsDev& d, int32_t* visits, float* wsum, cudaStream_t s);
+cudaError_t mcts_launch_choose(const MctsDev& d, int temp_moves, int32_t* actions, cudaStream_t s);
+cudaError_t mcts_launch_play(const MctsDev& d, const int32_t* actions, int reserve, int8_t* done, cudaStream_t s);
+cudaError_t mcts_launch_tree_sizes(const MctsDev& d, int32_t* nodes, int32_t* edges, cudaStream_t s);
+
+}  // namespace gz

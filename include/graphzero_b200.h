@@ -1,0 +1,192 @@
+/*
+ * graphzero_b200 — C ABI of the B200 leaf-evaluation and batched PUCT path.
+ *
+ * Drop-in boundary for GraphZero's INeuralNet (networks/neural_network.h:16-27)
+ * and the leaf-evaluation call inside its search (self_play/self_play.cu:617-632).
+ * Plain C types only: device pointers are raw addresses, streams are
+ * cudaStream_t passed as void*, NCCL communicators as void*.
+ *
+ * Errors: every function returns gz_status and never exits the process (the
+ * reference exits through CUDA_CHECK/NCCL_CHECK, networks/gat/gat.cu:16-25).
+ * gz_last_error() returns a message for the calling thread's last failure.
+ *
+ * Threading: one gz_net / gz_mcts handle belongs to one device; calls on one
+ * handle must be serialised by the caller.  Handles on different devices are
+ * independent.
+ *
+ * Position encoding (int8): TicTacToe [9] and Connect4 [42] hold the cells
+ * row-major with +1 for the first player, -1 for the second, 0 empty
+ * (games/connect4/connect4.cu:22-34); chess [66] holds 64 squares with piece
+ * codes +-1..6 = P N B R Q K (white positive, games/chess/chess.cuh:11-21),
+ * a castling-rights byte (bit 0 WK, 1 WQ, 2 BK, 3 BQ) and the en-passant
+ * square (-1 none).  side[i] is the player to move (+1 / -1).
+ */
+#ifndef GRAPHZERO_B200_H
+#define GRAPHZERO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  GZ_OK = 0,
+  GZ_ERR_INVALID_ARG = 1,
+  GZ_ERR_CUDA = 2,
+  GZ_ERR_NCCL = 3,
+  GZ_ERR_TIMEOUT = 4,
+  GZ_ERR_IO = 5,
+  GZ_ERR_CAPACITY = 6,
+  GZ_ERR_UNSUPPORTED = 7
+} gz_status;
+
+typedef enum { GZ_GAME_TICTACTOE = 0, GZ_GAME_CONNECT4 = 1, GZ_GAME_CHESS = 2 } gz_game;
+typedef enum { GZ_NET_GAT = 0, GZ_NET_RESNET = 1 } gz_net_kind;
+
+/* Arithmetic of the forward pass.  AUTO: fp32 SIMT for TicTacToe, bf16
+ * tensor-core operands with fp32 accumulation for Connect4 and chess.
+ * FP16: fp16 tensor-core operands (same speed, 3 more mantissa bits; for
+ * weights whose heads amplify activation rounding).  FP32: SIMT fp32. */
+typedef enum { GZ_PREC_AUTO = 0, GZ_PREC_FP32 = 1, GZ_PREC_BF16 = 2, GZ_PREC_FP16 = 3 } gz_precision;
+
+typedef struct gz_net gz_net;
+typedef struct gz_mcts gz_mcts;
+
+typedef struct {
+  int game;      /* gz_game */
+  int kind;      /* gz_net_kind */
+  int precision; /* gz_precision */
+  int max_batch; /* largest n passed to the host-buffer calls (device staging) */
+} gz_net_config;
+
+typedef struct {
+  int game;               /* GZ_GAME_TICTACTOE or GZ_GAME_CONNECT4 */
+  int trees;              /* concurrent games (one search tree each) */
+  int leaves_per_tree;    /* leaves selected per tree per wave */
+  float c_puct;           /* exploration constant */
+  int virtual_loss;       /* virtual visits (value -1 each) per selection in flight */
+  int node_capacity;      /* node pool per tree */
+  float dirichlet_alpha;  /* root noise concentration */
+  float dirichlet_eps;    /* root noise weight; 0 disables the noise */
+  uint64_t seed;          /* noise and move-sampling seed */
+} gz_mcts_config;
+
+const char* gz_status_string(gz_status s);
+const char* gz_last_error(void);
+/* Library version string. */
+const char* gz_version(void);
+
+/* ---- games ---------------------------------------------------------------
+ * Sizes of a game: nodes, rows, cols, actions, features, gat_layers,
+ * policy_per_node, board_bytes, graph_nnz (9 ints).  Replaces
+ * IGame::get_board_size / get_action_size (games/game.cuh:15-16). */
+gz_status gz_game_shape(int game, int32_t out[9]);
+/* Board-graph CSR: row_ptr[nodes+1], col[nnz]. */
+gz_status gz_game_graph(int game, int32_t* row_ptr, int32_t* col);
+/* IGame rules for TicTacToe / Connect4 on int8 boards (games/game.cuh:17-20;
+ * connect4.cu:22-87, tictactoe.cu:24-66).
+ *   gz_game_next_state: next = board with `action` played by `player`;
+ *                       *next_player = -player.  GZ_ERR_INVALID_ARG if illegal.
+ *   gz_game_valid_moves: valid[actions] = 1 for legal actions.
+ *   gz_game_ended: *result = 1 if `player` has won, -1 if the opponent has,
+ *                  2 for a draw (full board), 0 while the game continues.
+ *                  (The reference returns a draw marker that its int return
+ *                  type truncates to 0, connect4.cu:86.) */
+gz_status gz_game_next_state(int game, const int8_t* board, int player, int action, int8_t* next_board,
+                             int* next_player);
+gz_status gz_game_valid_moves(int game, const int8_t* board, uint8_t* valid);
+gz_status gz_game_ended(int game, const int8_t* board, int player, int* result);
+
+/* ---- synthetic inputs (host) -------------------------------------------- */
+/* Number of floats in the weight blob of (game, kind). */
+size_t gz_weight_count(int game, int kind);
+/* Seeded Glorot-uniform weights; bias_scale > 0 draws biases U(+-bias_scale);
+ * bf16_exact != 0 rounds every value to a bfloat16-representable float. */
+gz_status gz_synth_weights(int game, int kind, uint64_t seed, float bias_scale, int bf16_exact, float* out,
+                           size_t n_floats);
+/* n random legal non-terminal positions (uniform random playouts), indices
+ * first..first+n-1 of the seeded stream.  boards [n][board_bytes], side [n]. */
+gz_status gz_synth_positions(int game, uint64_t seed, uint64_t first, int n, int8_t* boards, int8_t* side);
+
+/* ---- network: INeuralNet replacement ------------------------------------ */
+/* create_gat_model / create_resnet_model / create_neural_net
+ * (networks/gat/gat.cu:681-696, networks/resnet/resnet.cu:259-272,
+ * networks/neural_network.c:6-13). */
+gz_status gz_net_create(const gz_net_config* cfg, int device, gz_net** out);
+/* INeuralNet::destroy (neural_network.h:25). */
+gz_status gz_net_destroy(gz_net* net);
+size_t gz_net_weight_count(const gz_net* net);
+/* Name of the forward kernel this handle launches: "gat_tc_bf16",
+ * "gat_tc_fp16", "gat_simt_fp32" or "resnet_tc_bf16". */
+const char* gz_net_kernel_name(const gz_net* net);
+/* Weights as one fp32 blob in the documented layout (the replacement for the
+ * reference's per-tensor cudaMalloc + cuRAND init, gat.cu:720-789). */
+gz_status gz_net_load_weights(gz_net* net, const float* host_blob, size_t n_floats);
+gz_status gz_net_save_weights(const gz_net* net, float* host_blob, size_t n_floats);
+/* INeuralNet::predict over a batch, all pointers on the device of `net`:
+ * boards [n][board_bytes], side [n], pi [n][actions], v [n]. */
+gz_status gz_net_predict_batch(gz_net* net, const int8_t* d_boards, const int8_t* d_side, int n, float* d_pi,
+                               float* d_v, void* stream);
+/* Same with host buffers: copies in, evaluates, copies out, synchronises.
+ * n <= max_batch. */
+gz_status gz_net_predict_host(gz_net* net, const int8_t* h_boards, const int8_t* h_side, int n, float* h_pi,
+                              float* h_v);
+/* INeuralNet::predict (neural_network.h:22): one position given as the
+ * canonical float board (own stones +1, opponent -1; the reference's
+ * get_canonical_form, connect4.cu:89-93), host pointers. */
+gz_status gz_net_predict(gz_net* net, const float* h_board, float* h_pi, float* h_v);
+/* INeuralNet::broadcast_weights (neural_network.h:27): ncclBroadcast of the
+ * weight blob from `root` over an existing communicator (ncclComm_t). */
+gz_status gz_net_broadcast(gz_net* net, void* nccl_comm, int root, void* stream);
+
+/* ---- NCCL bootstrap without MPI (the reference uses MPI_Bcast of the id,
+ * main.cu:59-61) ---------------------------------------------------------- */
+/* 128-byte ncclUniqueId. */
+gz_status gz_nccl_unique_id(uint8_t out[128]);
+gz_status gz_nccl_comm_init(const uint8_t id[128], int world, int rank, int device, void** comm);
+gz_status gz_nccl_comm_destroy(void* comm);
+
+/* ---- batched PUCT search (mcts/mcts.cu, self_play/self_play.cu:610-758) -- */
+gz_status gz_mcts_create(const gz_mcts_config* cfg, int device, gz_mcts** out);
+gz_status gz_mcts_destroy(gz_mcts* m);
+/* Root positions, device arrays boards [trees][nodes], side [trees]
+ * (replaces mcts_init, mcts/mcts.cu:10). */
+gz_status gz_mcts_reset_roots(gz_mcts* m, const int8_t* d_boards, const int8_t* d_side, void* stream);
+/* One selection pass; fills the leaf batch (trees * leaves_per_tree). */
+gz_status gz_mcts_select(gz_mcts* m, void* stream);
+/* Device pointers of the leaf batch: boards [L][nodes], side [L], terminal [L]. */
+gz_status gz_mcts_leaf_buffers(gz_mcts* m, int8_t** d_boards, int8_t** d_side, int8_t** d_terminal);
+/* Copies the leaf batch to host buffers and synchronises (for callers that
+ * evaluate leaves themselves); any pointer may be NULL. */
+gz_status gz_mcts_copy_leaves(gz_mcts* m, int8_t* h_boards, int8_t* h_side, int8_t* h_terminal, void* stream);
+/* Backup of the current wave with the leaves' evaluations (device arrays
+ * pi [L][actions], v [L]). */
+gz_status gz_mcts_backup(gz_mcts* m, const float* d_pi, const float* d_v, void* stream);
+/* select -> net evaluation of the leaf batch -> backup. */
+gz_status gz_mcts_step(gz_mcts* m, gz_net* net, void* stream);
+/* Waves until every tree has run `sims` more simulations (mcts_run_batch,
+ * mcts/mcts.cu:221-263). */
+gz_status gz_mcts_run(gz_mcts* m, gz_net* net, int sims, void* stream);
+/* Root visit counts [trees][actions] (and optionally value sums) to host;
+ * synchronises and reports any capacity error of earlier kernels. */
+gz_status gz_mcts_root_stats(gz_mcts* m, int32_t* h_visits, float* h_wsum, void* stream);
+/* Node and edge pool use per tree, to host. */
+gz_status gz_mcts_tree_sizes(gz_mcts* m, int32_t* h_nodes, int32_t* h_edges, void* stream);
+/* Actions from root visits (mcts_select_action, mcts/mcts.cu:40-66): sampled
+ * in proportion to N for the first temp_moves moves of a game, then argmax.
+ * d_actions [trees]. */
+gz_status gz_mcts_choose(gz_mcts* m, int temp_moves, int32_t* d_actions, void* stream);
+/* Advance roots (mcts_update_with_move, mcts/mcts.cu:68-103); a subtree is
+ * kept while `reserve` pool nodes remain.  d_done [trees] (may be NULL). */
+gz_status gz_mcts_play(gz_mcts* m, const int32_t* d_actions, int reserve, int8_t* d_done, void* stream);
+/* Sticky device error of the search kernels (0 none, 1 node pool, 2 edge
+ * pool, 3 depth); synchronises. */
+gz_status gz_mcts_check(gz_mcts* m);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GRAPHZERO_B200_H */
