@@ -72,6 +72,7 @@ _SIGS = {
     "gz_net_load_weights": (C.c_int, [_vp, _f32p, C.c_size_t]),
     "gz_net_save_weights": (C.c_int, [_vp, _f32p, C.c_size_t]),
     "gz_net_predict_batch": (C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp, _vp]),
+    "gz_net_check": (C.c_int, [_vp]),
     "gz_net_predict_host": (C.c_int, [_vp, _i8p, _i8p, C.c_int, _f32p, _f32p]),
     "gz_net_predict": (C.c_int, [_vp, _f32p, _f32p, _f32p]),
     "gz_net_broadcast": (C.c_int, [_vp, _vp, C.c_int, _vp]),
@@ -243,6 +244,10 @@ class Net:
         """Device-pointer batch evaluation (torch tensors or raw addresses)."""
         _check(_lib.gz_net_predict_batch(self._h, _dev(d_boards), _dev(d_side), n, _dev(d_pi), _dev(d_v),
                                          _stream(stream)))
+
+    def check(self) -> None:
+        """Raise if a bounded wait inside a forward kernel gave up."""
+        _check(_lib.gz_net_check(self._h))
 
     def predict_host(self, boards: np.ndarray, side: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
         boards = np.ascontiguousarray(boards, np.int8)

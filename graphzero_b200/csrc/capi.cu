@@ -92,8 +92,9 @@ struct gz_net {
   size_t weight_count;
   float* d_weights = nullptr;  // fp32 blob (source of truth on the device)
   int* d_csr = nullptr;        // row_ptr + col
-  void* d_tc = nullptr;        // tensor-core packed weights (bf16 path)
+  void* d_tc = nullptr;        // tensor-core packed weights (bf16 / fp16 path)
   size_t tc_bytes = 0;
+  int* d_err = nullptr;        // sticky device error word of the forward kernels
   // host-call staging
   int8_t *h_in = nullptr, *d_in = nullptr;
   float *h_out = nullptr, *d_out = nullptr;
@@ -119,7 +120,7 @@ bool use_tensor_cores(const gz_net* n) {
 
 gz_status prepare_weights(gz_net* n, cudaStream_t s) {
   if (n->kind == GZ_NET_GAT && use_tensor_cores(n)) {
-    GZ_CUDA(launch_gat_tc_pack(n->game, n->d_weights, n->d_tc, s));
+    GZ_CUDA(launch_gat_tc_pack(n->game, n->precision == GZ_PREC_FP16, n->d_weights, n->d_tc, s));
   }
   return GZ_OK;
 }
@@ -128,7 +129,8 @@ gz_status run_forward(gz_net* n, const int8_t* boards, const int8_t* side, int c
                       cudaStream_t s) {
   if (n->kind == GZ_NET_GAT) {
     if (use_tensor_cores(n))
-      GZ_CUDA(launch_gat_tc(n->game, n->d_tc, n->d_weights, boards, side, count, pi, v, s));
+      GZ_CUDA(launch_gat_tc(n->game, n->precision == GZ_PREC_FP16, n->d_tc, n->d_weights, boards, side, count, pi, v,
+                            n->d_err, s));
     else
       GZ_CUDA(launch_gat_simt(n->game, n->d_weights, n->d_csr, boards, side, count, pi, v, s));
     return GZ_OK;
@@ -270,6 +272,8 @@ gz_status gz_net_create(const gz_net_config* cfg, int device, gz_net** out) {
   std::vector<int> csr(s.nodes + 1 + s.nnz);
   build_graph_csr(cfg->game, csr.data(), csr.data() + s.nodes + 1);
   chk(cudaMalloc(&n->d_csr, csr.size() * sizeof(int)), "cudaMalloc csr");
+  chk(cudaMalloc(&n->d_err, sizeof(int)), "cudaMalloc err");
+  chk(cudaMemset(n->d_err, 0, sizeof(int)), "cudaMemset err");
   chk(cudaMemcpy(n->d_csr, csr.data(), csr.size() * sizeof(int), cudaMemcpyHostToDevice), "copy csr");
   if (use_tensor_cores(n)) {
     n->tc_bytes = gat_tc_packed_bytes(cfg->game);
@@ -303,6 +307,7 @@ gz_status gz_net_destroy(gz_net* n) {
   cudaFree(n->d_weights);
   cudaFree(n->d_csr);
   cudaFree(n->d_tc);
+  cudaFree(n->d_err);
   cudaFreeHost(n->h_in);
   cudaFree(n->d_in);
   cudaFreeHost(n->h_out);
@@ -318,7 +323,7 @@ const char* gz_net_kernel_name(const gz_net* n) {
   if (!n) return "";
   if (n->kind == GZ_NET_RESNET) return "resnet_tc_bf16";
   if (!use_tensor_cores(n)) return "gat_simt_fp32";
-  return n->precision == GZ_PREC_FP16 ? "gat_tc_fp16" : "gat_tc_bf16";
+  return n->precision == GZ_PREC_FP16 ? "gat_tc_fp16" : "gat_tc_bf16";  // gat_tc_c4_kernel
 }
 
 gz_status gz_net_load_weights(gz_net* n, const float* blob, size_t count) {
@@ -351,6 +356,18 @@ gz_status gz_net_predict_batch(gz_net* n, const int8_t* boards, const int8_t* si
   return run_forward(n, boards, side, count, pi, v, (cudaStream_t)stream);
 }
 
+gz_status gz_net_check(gz_net* n) {
+  if (!n) return fail(GZ_ERR_INVALID_ARG, "null net");
+  GZ_DEVICE(n->device);
+  int err = 0;
+  GZ_CUDA(cudaMemcpy(&err, n->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) {
+    GZ_CUDA(cudaMemset(n->d_err, 0, sizeof(int)));
+    return fail(GZ_ERR_TIMEOUT, "a bounded wait inside the forward kernel gave up (outputs of that launch are invalid)");
+  }
+  return GZ_OK;
+}
+
 gz_status gz_net_predict_host(gz_net* n, const int8_t* boards, const int8_t* side, int count, float* pi, float* v) {
   if (!n) return fail(GZ_ERR_INVALID_ARG, "null net");
   if (count < 0 || count > n->max_batch) return fail(GZ_ERR_INVALID_ARG, "batch %d outside [0, %d]", count, n->max_batch);
@@ -369,6 +386,8 @@ gz_status gz_net_predict_host(gz_net* n, const int8_t* boards, const int8_t* sid
   size_t outf = (size_t)count * (s.actions + 1);
   GZ_CUDA(cudaMemcpyAsync(n->h_out, n->d_out, outf * sizeof(float), cudaMemcpyDeviceToHost, n->stream));
   GZ_CUDA(cudaStreamSynchronize(n->stream));
+  gz_status chk_st = gz_net_check(n);
+  if (chk_st != GZ_OK) return chk_st;
   memcpy(pi, n->h_out, (size_t)count * s.actions * sizeof(float));
   memcpy(v, n->h_out + (size_t)count * s.actions, (size_t)count * sizeof(float));
   return GZ_OK;

@@ -18,9 +18,11 @@ cudaError_t launch_gat_simt(int game, const float* d_weights, const int* d_csr, 
 // bf16 tensor-core (tcgen05) GAT forward for Connect4 and chess.
 // gat_tc_packed_bytes(game) is 0 when the game has no tensor-core kernel.
 size_t gat_tc_packed_bytes(int game);
-// Converts the fp32 blob into the kernel's operand layout (bf16 weight tiles).
-cudaError_t launch_gat_tc_pack(int game, const float* d_weights, void* d_packed, cudaStream_t stream);
-cudaError_t launch_gat_tc(int game, const void* d_packed, const float* d_weights, const int8_t* d_boards,
-                          const int8_t* d_side, int n, float* d_pi, float* d_v, cudaStream_t stream);
+// Converts the fp32 blob into the kernel's operand layout (bf16 or fp16
+// weight tiles, 128-byte swizzled).
+cudaError_t launch_gat_tc_pack(int game, int fp16, const float* d_weights, void* d_packed, cudaStream_t stream);
+// d_err: device word set to 1 when a bounded wait inside the kernel gave up.
+cudaError_t launch_gat_tc(int game, int fp16, const void* d_packed, const float* d_weights, const int8_t* d_boards,
+                          const int8_t* d_side, int n, float* d_pi, float* d_v, int* d_err, cudaStream_t stream);
 
 }  // namespace gz

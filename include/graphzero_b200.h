@@ -129,6 +129,9 @@ gz_status gz_net_save_weights(const gz_net* net, float* host_blob, size_t n_floa
  * boards [n][board_bytes], side [n], pi [n][actions], v [n]. */
 gz_status gz_net_predict_batch(gz_net* net, const int8_t* d_boards, const int8_t* d_side, int n, float* d_pi,
                                float* d_v, void* stream);
+/* Synchronises and reports GZ_ERR_TIMEOUT if a bounded wait inside a forward
+ * kernel gave up since the last check (the word is then cleared). */
+gz_status gz_net_check(gz_net* net);
 /* Same with host buffers: copies in, evaluates, copies out, synchronises.
  * n <= max_batch. */
 gz_status gz_net_predict_host(gz_net* net, const int8_t* h_boards, const int8_t* h_side, int n, float* h_pi,

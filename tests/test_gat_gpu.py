@@ -60,6 +60,54 @@ def test_simt_matches_oracle(cuda, game, prec, sharp, tol, sizes):
         assert np.abs(v - ov).max() < tol, (n, np.abs(v - ov).max())
 
 
+TC_CASES = [
+    # precision, sharpened heads, tolerance
+    (gz.PREC_BF16, False, 1e-3),
+    (gz.PREC_FP16, False, 1e-3),
+    (gz.PREC_FP16, True, 1e-3),
+    (gz.PREC_BF16, True, 1e-2),
+]
+
+
+@pytest.mark.parametrize("prec,sharp,tol", TC_CASES)
+def test_tensor_core_matches_oracle(cuda, prec, sharp, tol):
+    game = gz.CONNECT4
+    w = gz.synth_weights(game, seed=17, bias_scale=0.4 if sharp else 0.0)
+    if sharp:
+        w = sharpen(game, w)
+    net = gz.Net(game, precision=prec, max_batch=4096)
+    assert net.kernel_name.startswith("gat_tc_")
+    net.load_weights(w)
+    for n in (1, 2, 3, 4, 7, 300, 1000):
+        boards, side = inputs(game, n, seed=200 + n)
+        pi, v = run(net, boards, side)
+        opi, ov = oracle.gat_forward(game, w, boards, side)
+        assert np.isfinite(pi).all() and np.isfinite(v).all(), n
+        assert np.abs(pi - opi).max() < tol, (n, np.abs(pi - opi).max())
+        assert np.abs(v - ov).max() < tol, (n, np.abs(v - ov).max())
+    net.check()
+
+
+def test_tensor_core_full_batch(cuda):
+    """The benchmark shape: 4096 positions in one launch, every row checked
+    against the oracle, plus run-to-run determinism."""
+    game = gz.CONNECT4
+    w = gz.synth_weights(game, seed=0x6A5A)
+    net = gz.Net(game, max_batch=4096)
+    net.load_weights(w)
+    boards, side = gz.synth_positions(game, 4096, seed=0x6A5A + 1)
+    pi, v = run(net, boards, side)
+    pi2, v2 = run(net, boards, side)
+    assert (pi == pi2).all() and (v == v2).all()
+    opi, ov = oracle.gat_forward(game, w, boards, side)
+    assert np.abs(pi - opi).max() < 1e-3 and np.abs(v - ov).max() < 1e-3
+    assert np.allclose(pi.sum(1), 1, atol=1e-5)
+    # batch composition does not change a position's result
+    pj, vj = run(net, boards[1000:1003], side[1000:1003])
+    assert (pj == pi[1000:1003]).all() and (vj == v[1000:1003]).all()
+    net.check()
+
+
 def test_empty_batch_is_a_no_op(cuda):
     net = gz.Net(gz.CONNECT4, precision=gz.PREC_FP32)
     net.predict_batch(0, 0, 0, 0, 0)
