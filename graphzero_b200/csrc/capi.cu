@@ -363,6 +363,7 @@ gz_status gz_net_check(gz_net* n) {
   GZ_CUDA(cudaMemcpy(&err, n->d_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (err) {
     GZ_CUDA(cudaMemset(n->d_err, 0, sizeof(int)));
+    if (err == 2) return fail(GZ_ERR_CUDA, "forward kernel: dynamic shared memory base not 1024-byte aligned");
     return fail(GZ_ERR_TIMEOUT, "a bounded wait inside the forward kernel gave up (outputs of that launch are invalid)");
   }
   return GZ_OK;

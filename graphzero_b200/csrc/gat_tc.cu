@@ -114,13 +114,14 @@ __device__ __forceinline__ void gather_rows(const float (&wh)[kN], const float4*
 // Shared memory map (bytes).
 constexpr int kSmX = 0;                                  // 4 chunks: X tile, K-major swizzled
 constexpr int kSmW = kSmX + 4 * kChunkBytes;             // weight ring
-constexpr int kWarpScratchFloats = 48 + 48 + 304;        // s_self, s_nbr, alpha
+constexpr int kWarpScratchFloats = 48 + 48 + 48 + 304;   // s_self, s_nbr, 1/z, alpha (16-byte aligned parts)
 constexpr int kSmScratch = kSmW + kSlots * kChunkBytes;
-constexpr int kSmBar = kSmScratch + kEpiWarps * kWarpScratchFloats * 4;
+constexpr int kSmRp = kSmScratch + kEpiWarps * kWarpScratchFloats * 4;  // CSR row pointers [43]
+constexpr int kSmBar = kSmRp + 48 * 4;
 constexpr int kNumBars = 2 * kSlots + 3;                 // full[], empty[], acc_full, x_ready, drain
 constexpr int kSmMisc = kSmBar + kNumBars * 8;           // tmem base, abort flag
 constexpr int kSmemBytes = kSmMisc + 16;
-constexpr int kSmemAlloc = kSmemBytes + 1024;            // slack for 1024-byte alignment
+constexpr int kSmemAlloc = kSmemBytes;                    // base must be 1024-aligned (checked)
 static_assert(kSmemAlloc <= 113 * 1024, "two CTAs per SM");
 
 // Offsets (floats) into the fp32 weight blob for Connect4 (gat_layout order).
@@ -132,7 +133,7 @@ struct C4Off {
   __device__ static constexpr int a(int l) { return b(l) + 256; }
   static constexpr int kHeads = kLayer0 + (kLayers - 1) * kLayerN;
   static constexpr int w_pi = kHeads, b_pi = w_pi + 256, W_v1 = b_pi + 1, b_v1 = W_v1 + 256 * 64;
-  static constexpr int w_v2 = b_v1 + 64, b_v2 = w_v2 + 64, total = b_v2 + 1;
+  static constexpr int w_v2 = b_v1 + 64, b_v2 = w_v2 + 64;
 };
 
 template <typename T> struct OpType;
@@ -214,6 +215,82 @@ __device__ __forceinline__ float dot_scatter16(const float (&x)[NX], float a, in
 __device__ __forceinline__ float lrelu(float x) { return x > 0.f ? x : kLeakySlope * x; }
 __device__ __forceinline__ float elu_fast(float x) { return x > 0.f ? x : __expf(x) - 1.0f; }
 
+template <int OFF>
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
+  asm volatile("st.shared.b16 [%0+%1], %2;" ::"r"(addr), "n"(OFF), "h"(v) : "memory");
+}
+
+template <int I>
+__device__ __forceinline__ float pick4(const float4* a4) {
+  const float4 w4 = a4[I >> 2];
+  return (I & 3) == 0 ? w4.x : (I & 3) == 1 ? w4.y : (I & 3) == 2 ? w4.z : w4.w;
+}
+
+// Epilogue of one position (compile-time slot G_ of the tile) for the head
+// owned by this warp: scores, neighbour softmax, gather, bias + ELU, and
+// either the store of X_{l+1} (feature d of the 42 nodes) or, in the last
+// layer, the pooled sums the heads need.
+template <typename OpT, int G_, bool LAST>
+__device__ __forceinline__ void epilogue_graph(uint32_t tbase, float a_s, float a_n, float bias, float* s_self,
+                                               float* s_nbr, float* inv_z, float* alpha, const int* rp_s,
+                                               const uint32_t (&xs)[8], float& vs, float (&cs)[7], int lane) {
+  float wh[kN];
+#pragma unroll
+  for (int t = 0; t < kN / 2; ++t) tmem_ld_x2(tbase + G_ * kN + 2 * t, wh[2 * t], wh[2 * t + 1]);
+  tmem_ld_wait();
+  // attention scores: reduce-scatter of a . Wh across the 32 feature lanes
+  s_self[lane] = dot_scatter32<0>(wh, a_s, lane);
+  s_nbr[lane] = dot_scatter32<0>(wh, a_n, lane);
+  const float r3 = dot_scatter16<32>(wh, a_s, lane);
+  const float r4 = dot_scatter16<32>(wh, a_n, lane);
+  if (lane < 16) {
+    s_self[32 + lane] = r3;
+    s_nbr[32 + lane] = r4;
+  }
+  __syncwarp();
+  // neighbour softmax over the 3x3 board stencil (the CSR in ascending
+  // order); unnormalised weights in CSR order plus 1/z per node
+  for (int i = lane; i < kN; i += 32) {
+    const int r = i / 7, c = i % 7;
+    const float si = s_self[i];
+    float ev[9];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+      const int dr = k / 3 - 1, dc = k % 3 - 1;
+      const bool in = (unsigned)(r + dr) < 6u && (unsigned)(c + dc) < 7u;
+      ev[k] = in ? lrelu(si + s_nbr[i + 7 * dr + dc]) : -INFINITY;
+      mx = fmaxf(mx, ev[k]);
+    }
+    int e = rp_s[i];
+    float z = 0.f;
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+      if (ev[k] != -INFINITY) {
+        const float pe = __expf(ev[k] - mx);
+        alpha[e++] = pe;
+        z += pe;
+      }
+    }
+    inv_z[i] = 1.0f / z;
+  }
+  __syncwarp();
+  const float4* a4 = (const float4*)alpha;
+  const float4* z4 = (const float4*)inv_z;
+  gather_rows<0>(wh, a4, [&](auto I, float acc) {
+    constexpr int i = decltype(I)::value;
+    const float x = elu_fast(fmaf(acc, pick4<i>(z4), bias));
+    if constexpr (!LAST) {
+      constexpr int j = G_ * kN + i;
+      st_shared_u16<(j >> 3) * 1024 + (j & 7) * 128>(xs[j & 7], OpType<OpT>::bits(x));
+    } else {
+      vs += x;
+      cs[i % 7] += x;
+    }
+  });
+  __syncwarp();
+}
+
 struct TcParams {
   const uint8_t* packed;   // kChunksPerTile chunks in consumption order
   const float* w;          // fp32 blob (biases, attention vectors, heads)
@@ -228,8 +305,12 @@ struct TcParams {
 
 template <typename OpT>
 __global__ void __launch_bounds__(kThreads, 2) gat_tc_c4_kernel(TcParams p) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  extern __shared__ __align__(1024) uint8_t smem[];
+  // The swizzled operand tiles need a 1024-byte aligned base.
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) atomicExch(p.err, 2);
+    return;
+  }
   uint8_t* sX = smem + kSmX;
   uint8_t* sW = smem + kSmW;
   float* scratch = (float*)(smem + kSmScratch);
@@ -245,6 +326,7 @@ __global__ void __launch_bounds__(kThreads, 2) gat_tc_c4_kernel(TcParams p) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  for (int i = threadIdx.x; i <= kN; i += blockDim.x) ((int*)(smem + kSmRp))[i] = c_rp[i];
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(&full[s], 1);
@@ -329,8 +411,16 @@ __global__ void __launch_bounds__(kThreads, 2) gat_tc_c4_kernel(TcParams p) {
     const uint32_t tbase = tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)(m * kTileCols);
     float* s_self = scratch + warp * kWarpScratchFloats;
     float* s_nbr = s_self + 48;
-    float* alpha = s_nbr + 48;
+    float* inv_z = s_nbr + 48;
+    float* alpha = inv_z + 48;
+    const int* rp_s = (const int*)(smem + kSmRp);
     const int chunk_d = d >> 6, kk_d = d & 63;  // where feature d lives in the X tile
+    // shared addresses of feature d in X-tile row r (mod 8) of the 128-byte
+    // swizzle: row base + ((16-byte unit ^ r) << 4) + byte within the unit
+    uint32_t xs[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      xs[r] = smem_u32(sX + chunk_d * kChunkBytes) + ((((kk_d >> 3) ^ r) & 7) << 4) + (kk_d & 7) * 2;
     uint32_t aphase = 0;
     bool ok = true;
 
@@ -367,60 +457,20 @@ __global__ void __launch_bounds__(kThreads, 2) gat_tc_c4_kernel(TcParams p) {
         float* pooled = (float*)(sX + kChunkBytes);       // [3][256]
         float* pol = pooled + kGPT * 256;                 // [3][8 warps][8]
         float* zbuf = pol + kGPT * kEpiWarps * 8;         // [3][64]
+        if (!last) {
+          float vs = 0.f, cs[7];
+          epilogue_graph<OpT, 0, false>(tbase, a_s, a_n, bias, s_self, s_nbr, inv_z, alpha, rp_s, xs, vs, cs, lane);
+          epilogue_graph<OpT, 1, false>(tbase, a_s, a_n, bias, s_self, s_nbr, inv_z, alpha, rp_s, xs, vs, cs, lane);
+          epilogue_graph<OpT, 2, false>(tbase, a_s, a_n, bias, s_self, s_nbr, inv_z, alpha, rp_s, xs, vs, cs, lane);
+        } else {
+          const float wpi = __ldg(p.w + C4Off::w_pi + d);
 #pragma unroll 1
-        for (int g = 0; g < kGPT; ++g) {
-          // Wh for the 42 nodes of position g, this lane's feature.
-          float wh[kN];
-#pragma unroll
-          for (int t = 0; t < kN / 2; ++t) tmem_ld_x2(tbase + g * kN + 2 * t, wh[2 * t], wh[2 * t + 1]);
-          tmem_ld_wait();
-          // attention scores (reduce-scatter across the 32 feature lanes)
-          {
-            s_self[lane] = dot_scatter32<0>(wh, a_s, lane);
-            s_nbr[lane] = dot_scatter32<0>(wh, a_n, lane);
-            const float r3 = dot_scatter16<32>(wh, a_s, lane);
-            const float r4 = dot_scatter16<32>(wh, a_n, lane);
-            if (lane < 16) {
-              s_self[32 + lane] = r3;
-              s_nbr[32 + lane] = r4;
-            }
-          }
-          __syncwarp();
-          // neighbour softmax: lane handles nodes lane and lane + 32
-          for (int i = lane; i < kN; i += 32) {
-            const float si = s_self[i];
-            const int e0 = c_rp[i], e1 = c_rp[i + 1];
-            float mx = -INFINITY;
-            for (int e = e0; e < e1; ++e) mx = fmaxf(mx, lrelu(si + s_nbr[c_col[e]]));
-            float z = 0.f;
-            for (int e = e0; e < e1; ++e) {
-              const float pe = __expf(lrelu(si + s_nbr[c_col[e]]) - mx);
-              alpha[e] = pe;
-              z += pe;
-            }
-            const float inv = 1.0f / z;
-            for (int e = e0; e < e1; ++e) alpha[e] *= inv;
-          }
-          __syncwarp();
-          // aggregation over the static CSR, Wh in registers
-          const float4* a4 = (const float4*)alpha;
-          if (!last) {
-            uint8_t* xcol = sX + chunk_d * kChunkBytes;
-            gather_rows<0>(wh, a4, [&](auto I, float acc) {
-              constexpr int i = decltype(I)::value;
-              const int j = g * kN + i;
-              *(uint16_t*)(xcol + sw128_offset(j, kk_d)) = OpType<OpT>::bits(elu_fast(acc + bias));
-            });
-          } else {
+          for (int g = 0; g < kGPT; ++g) {
             float vs = 0.f, cs[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            gather_rows<0>(wh, a4, [&](auto I, float acc) {
-              constexpr int i = decltype(I)::value;
-              const float x = elu_fast(acc + bias);
-              vs += x;
-              cs[i % 7] += x;
-            });
+            if (g == 0) epilogue_graph<OpT, 0, true>(tbase, a_s, a_n, bias, s_self, s_nbr, inv_z, alpha, rp_s, xs, vs, cs, lane);
+            if (g == 1) epilogue_graph<OpT, 1, true>(tbase, a_s, a_n, bias, s_self, s_nbr, inv_z, alpha, rp_s, xs, vs, cs, lane);
+            if (g == 2) epilogue_graph<OpT, 2, true>(tbase, a_s, a_n, bias, s_self, s_nbr, inv_z, alpha, rp_s, xs, vs, cs, lane);
             pooled[g * 256 + d] = vs * (1.0f / kN);
-            const float wpi = __ldg(p.w + C4Off::w_pi + d);
 #pragma unroll
             for (int c = 0; c < 7; ++c) {
               float t = cs[c] * (1.0f / 6.0f) * wpi;
@@ -429,7 +479,6 @@ __global__ void __launch_bounds__(kThreads, 2) gat_tc_c4_kernel(TcParams p) {
               if (lane == 0) pol[(g * kEpiWarps + warp) * 8 + c] = t;
             }
           }
-          __syncwarp();
         }
         tc_fence_before();
         if (!last) {
@@ -553,15 +602,31 @@ cudaError_t launch_gat_tc(int game, int fp16, const void* d_packed, const float*
   p.n = n;
   p.num_tiles = (n + kGPT - 1) / kGPT;
   auto kern = fp16 ? gat_tc_c4_kernel<__half> : gat_tc_c4_kernel<__nv_bfloat16>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
+  // Per-device launch shape, computed once: persistent grid of
+  // (SMs x resident CTAs per SM, at most two: tensor memory holds two CTAs'
+  // 256-column accumulators).
+  static int cached_grid[64][2];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  int dev = 0, sms = 0, per_sm = 0;
-  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, kSmemAlloc)) != cudaSuccess) return e;
-  if (per_sm < 1) return cudaErrorInvalidConfiguration;
-  per_sm = per_sm > 2 ? 2 : per_sm;  // tensor memory holds two CTAs' accumulators
-  int grid = sms * per_sm;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  int& full_grid = cached_grid[dev][fp16 ? 1 : 0];
+  if (full_grid == 0) {
+    int sms = 0, per_sm = 0, smem_sm = 0, reserved = 0;
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc)) != cudaSuccess) return e;
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev)) != cudaSuccess) return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, kSmemAlloc)) != cudaSuccess) return e;
+    // The occupancy query can under-report here; shared memory (the binding
+    // limit, registers are capped by __launch_bounds__) decides directly.
+    const int by_smem = smem_sm / (kSmemAlloc + reserved);
+    if (by_smem > per_sm) per_sm = by_smem;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    full_grid = sms * (per_sm > 2 ? 2 : per_sm);
+  }
+  int grid = full_grid;
   if (grid > p.num_tiles) grid = p.num_tiles;
   kern<<<grid, kThreads, kSmemAlloc, stream>>>(p);
   return cudaGetLastError();
