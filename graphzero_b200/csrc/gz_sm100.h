@@ -104,6 +104,18 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16.  A is M x K with row m in
+// lane m and two 16-bit K elements per 32-bit column (K = 16 spans 8 columns).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on `bar` once all previously issued MMAs of this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -119,6 +131,30 @@ __device__ __forceinline__ void tmem_ld_x2(uint32_t taddr, float& a, float& b) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 32 lanes x 32 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 lanes x 8 consecutive 32-bit columns from registers.
+__device__ __forceinline__ void tmem_st_x8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Shared-memory matrix descriptor: K-major operand in the 128-byte swizzle
 // layout (rows of 128 bytes, 8-row atoms of 1024 bytes, atoms 1024 bytes
 // apart).  Start address must lie in a 1024-byte aligned atom; advancing
@@ -133,14 +169,30 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor for kind::f16: fp32 accumulator, both operands
-// K-major, of format `fmt` (0 = fp16, 1 = bf16), shape M x N.
-__host__ __device__ constexpr uint32_t idesc_f16(uint32_t fmt, uint32_t M, uint32_t N) {
-  return (1u << 4)            // D format: f32
-         | (fmt << 7)         // A format
-         | (fmt << 10)        // B format
-         | ((N >> 3) << 17)   // N / 8
-         | ((M >> 4) << 24);  // M / 16
+// Shared-memory matrix descriptor without swizzle ("interleaved" core
+// matrices of 8 rows x 16 bytes stored contiguously).  lbo / sbo are the byte
+// strides between core matrices along the leading and the strided dimension;
+// for an MN-major operand the leading dimension is K (8-row K groups) and the
+// strided one MN (8-element groups).
+__device__ __forceinline__ uint64_t noswizzle_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (sm_100); layout type 0 = no swizzle
+  return d;
+}
+
+// Instruction descriptor for kind::f16: fp32 accumulator, operands of format
+// `fmt` (0 = fp16, 1 = bf16), shape M x N; A K-major, B K-major unless
+// b_mn_major (then B is stored N-contiguous).
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t fmt, uint32_t M, uint32_t N, uint32_t b_mn_major = 0) {
+  return (1u << 4)             // D format: f32
+         | (fmt << 7)          // A format
+         | (fmt << 10)         // B format
+         | (b_mn_major << 16)  // B major-ness
+         | ((N >> 3) << 17)    // N / 8
+         | ((M >> 4) << 24);   // M / 16
 }
 
 // Byte offset of element (row, k) inside a K-major 128-byte-swizzled tile
