@@ -76,6 +76,14 @@ _SIGS = {
     "gz_net_predict_host": (C.c_int, [_vp, _i8p, _i8p, C.c_int, _f32p, _f32p]),
     "gz_net_predict": (C.c_int, [_vp, _f32p, _f32p, _f32p]),
     "gz_net_broadcast": (C.c_int, [_vp, _vp, C.c_int, _vp]),
+    "gz_net_save_checkpoint": (C.c_int, [_vp, C.c_char_p]),
+    "gz_net_load_checkpoint": (C.c_int, [_vp, C.c_char_p]),
+    "gz_create_connect4_game": (_vp, []),
+    "gz_create_tictactoe_game": (_vp, []),
+    "gz_game_free": (None, [_vp]),
+    "gz_create_neural_net": (_vp, [C.c_char_p, _vp, C.c_int]),
+    "gz_shim_net": (_vp, [_vp]),
+    "gz_shim_make_ineuralnet": (_vp, [_vp]),
     "gz_nccl_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
     "gz_nccl_comm_init": (C.c_int, [C.POINTER(C.c_uint8), C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
     "gz_nccl_comm_destroy": (C.c_int, [_vp]),
@@ -267,6 +275,12 @@ class Net:
         _check(_lib.gz_net_predict(self._h, _ptr(b, C.c_float), _ptr(pi, C.c_float), _ptr(v, C.c_float)))
         return pi, float(v[0])
 
+    def save_checkpoint(self, path: str) -> None:
+        _check(_lib.gz_net_save_checkpoint(self._h, os.fsencode(path)))
+
+    def load_checkpoint(self, path: str) -> None:
+        _check(_lib.gz_net_load_checkpoint(self._h, os.fsencode(path)))
+
     def broadcast(self, comm: int, root: int = 0, stream=None) -> None:
         _check(_lib.gz_net_broadcast(self._h, comm, root, _stream(stream)))
 
@@ -371,6 +385,68 @@ class Mcts:
 
     def check(self) -> None:
         _check(_lib.gz_mcts_check(self._h))
+
+
+# ---- reference-layout shim (include/graphzero_b200_compat.h) ----
+_fn = C.CFUNCTYPE
+_ip, _fp = C.POINTER(C.c_int), C.POINTER(C.c_float)
+
+
+class IGame(C.Structure):
+    pass
+
+
+IGame._fields_ = [
+    ("init", _fn(None, C.POINTER(IGame))),
+    ("get_init_board", _fn(None, C.POINTER(IGame), _ip)),
+    ("get_board_size", _fn(None, C.POINTER(IGame), _ip, _ip)),
+    ("get_action_size", _fn(C.c_int, C.POINTER(IGame))),
+    ("get_next_state", _fn(None, C.POINTER(IGame), _ip, C.c_int, C.c_int, _ip, _ip)),
+    ("get_valid_moves", _fn(None, C.POINTER(IGame), _ip, C.c_int, C.POINTER(C.c_bool))),
+    ("get_game_ended", _fn(C.c_int, C.POINTER(IGame), _ip, C.c_int)),
+    ("get_canonical_form", _fn(None, C.POINTER(IGame), _ip, C.c_int, _ip)),
+    ("evaluate", _fn(C.c_float, C.POINTER(IGame), _ip, C.c_int)),
+    ("get_symmetries", _fn(None, C.POINTER(IGame), _ip, _fp, C.POINTER(C.c_int * 64), C.POINTER(C.c_float * 64), _ip)),
+    ("string_representation", _fn(None, C.POINTER(IGame), _ip, C.c_char_p, C.c_int)),
+    ("display", _fn(None, C.POINTER(IGame), _ip)),
+]
+
+
+class INeuralNet(C.Structure):
+    pass
+
+
+INeuralNet._fields_ = [
+    ("impl", _vp),
+    ("init", _fn(None, C.POINTER(INeuralNet), C.POINTER(IGame))),
+    ("train", _fn(None, C.POINTER(INeuralNet), _vp, C.c_int)),
+    ("predict", _fn(None, C.POINTER(INeuralNet), _fp, _fp, _fp)),
+    ("save_checkpoint", _fn(None, C.POINTER(INeuralNet), C.c_char_p, C.c_char_p)),
+    ("load_checkpoint", _fn(None, C.POINTER(INeuralNet), C.c_char_p, C.c_char_p)),
+    ("destroy", _fn(None, C.POINTER(INeuralNet))),
+    ("train_distributed", _fn(None, C.POINTER(INeuralNet), _fp, _fp, _fp, C.c_int, C.c_int, C.c_int, _vp, _vp)),
+    ("broadcast_weights", _fn(None, C.POINTER(INeuralNet), C.c_int, C.c_int, _vp, _vp)),
+]
+
+
+def create_igame(name: str):
+    """IGame vtable of `name` ('connect4' or 'tictactoe'); free with free_igame."""
+    h = {"connect4": _lib.gz_create_connect4_game, "tictactoe": _lib.gz_create_tictactoe_game}[name]()
+    if not h:
+        raise GZError(ERR_INVALID_ARG, f"cannot create game {name}")
+    return C.cast(h, C.POINTER(IGame))
+
+
+def free_igame(g) -> None:
+    _lib.gz_game_free(C.cast(g, _vp))
+
+
+def create_ineuralnet(net_type: str, game, device: int = 0):
+    """INeuralNet vtable (create_neural_net, networks/neural_network.c:6-13)."""
+    h = _lib.gz_create_neural_net(net_type.encode(), C.cast(game, _vp), device)
+    if not h:
+        raise GZError(ERR_CUDA, _lib.gz_last_error().decode(errors="replace"))
+    return C.cast(h, C.POINTER(INeuralNet))
 
 
 def loaded_library_path() -> str:

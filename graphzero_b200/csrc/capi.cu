@@ -346,6 +346,65 @@ gz_status gz_net_save_weights(const gz_net* n, float* blob, size_t count) {
   return GZ_OK;
 }
 
+namespace {
+uint64_t fnv1a(const void* data, size_t bytes) {
+  const uint8_t* p = (const uint8_t*)data;
+  uint64_t h = 1469598103934665603ull;
+  for (size_t i = 0; i < bytes; ++i) h = (h ^ p[i]) * 1099511628211ull;
+  return h;
+}
+struct CkptHeader {
+  char magic[8];
+  int32_t version, game, kind, reserved;
+  uint64_t count;
+};
+}  // namespace
+
+gz_status gz_net_save_checkpoint(const gz_net* n, const char* path) {
+  if (!n || !path) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  std::vector<float> w(n->weight_count);
+  gz_status st = gz_net_save_weights(n, w.data(), w.size());
+  if (st != GZ_OK) return st;
+  CkptHeader h{};
+  memcpy(h.magic, "GZB200W1", 8);
+  h.version = 1;
+  h.game = n->game;
+  h.kind = n->kind;
+  h.count = w.size();
+  uint64_t hash = fnv1a(w.data(), w.size() * sizeof(float));
+  FILE* f = fopen(path, "wb");
+  if (!f) return fail(GZ_ERR_IO, "cannot open %s for writing", path);
+  bool ok = fwrite(&h, sizeof h, 1, f) == 1 && fwrite(w.data(), sizeof(float), w.size(), f) == w.size() &&
+            fwrite(&hash, sizeof hash, 1, f) == 1;
+  ok = (fclose(f) == 0) && ok;
+  return ok ? GZ_OK : fail(GZ_ERR_IO, "short write to %s", path);
+}
+
+gz_status gz_net_load_checkpoint(gz_net* n, const char* path) {
+  if (!n || !path) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  FILE* f = fopen(path, "rb");
+  if (!f) return fail(GZ_ERR_IO, "cannot open %s", path);
+  CkptHeader h{};
+  std::vector<float> w;
+  uint64_t hash = 0;
+  gz_status st = GZ_OK;
+  if (fread(&h, sizeof h, 1, f) != 1 || memcmp(h.magic, "GZB200W1", 8) != 0 || h.version != 1) {
+    st = fail(GZ_ERR_IO, "%s: not a graphzero_b200 checkpoint", path);
+  } else if (h.game != n->game || h.kind != n->kind || h.count != n->weight_count) {
+    st = fail(GZ_ERR_IO, "%s: checkpoint for game %d kind %d (%llu weights) does not fit this net", path, h.game,
+              h.kind, (unsigned long long)h.count);
+  } else {
+    w.resize(h.count);
+    if (fread(w.data(), sizeof(float), w.size(), f) != w.size() || fread(&hash, sizeof hash, 1, f) != 1)
+      st = fail(GZ_ERR_IO, "%s: truncated checkpoint", path);
+    else if (hash != fnv1a(w.data(), w.size() * sizeof(float)))
+      st = fail(GZ_ERR_IO, "%s: checksum mismatch", path);
+  }
+  fclose(f);
+  if (st != GZ_OK) return st;
+  return gz_net_load_weights(n, w.data(), w.size());
+}
+
 gz_status gz_net_predict_batch(gz_net* n, const int8_t* boards, const int8_t* side, int count, float* pi, float* v,
                                void* stream) {
   if (!n) return fail(GZ_ERR_INVALID_ARG, "null net");

@@ -140,6 +140,14 @@ gz_status gz_net_predict_host(gz_net* net, const int8_t* h_boards, const int8_t*
  * canonical float board (own stones +1, opponent -1; the reference's
  * get_canonical_form, connect4.cu:89-93), host pointers. */
 gz_status gz_net_predict(gz_net* net, const float* h_board, float* h_pi, float* h_v);
+/* INeuralNet::save_checkpoint / load_checkpoint (neural_network.h:23-24; the
+ * reference writes a libtorch archive, networks/gat/gat.cu:201-337).  File:
+ * "GZB200W1" magic, then int32 version, game, kind, reserved, uint64 count,
+ * count fp32 weights (little endian, the weight-blob layout), uint64 FNV-1a
+ * hash of the weight bytes.  Load checks game, kind, count and hash
+ * (GZ_ERR_IO on any mismatch or short file). */
+gz_status gz_net_save_checkpoint(const gz_net* net, const char* path);
+gz_status gz_net_load_checkpoint(gz_net* net, const char* path);
 /* INeuralNet::broadcast_weights (neural_network.h:27): ncclBroadcast of the
  * weight blob from `root` over an existing communicator (ncclComm_t). */
 gz_status gz_net_broadcast(gz_net* net, void* nccl_comm, int root, void* stream);
