@@ -101,6 +101,7 @@ _SIGS = {
     "gz_mcts_choose": (C.c_int, [_vp, C.c_int, _vp, _vp]),
     "gz_mcts_play": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
     "gz_mcts_check": (C.c_int, [_vp]),
+    "gz_selftest_wait_timeout": (C.c_int, [C.c_int, C.c_int]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _f = getattr(_lib, _name)
@@ -133,6 +134,12 @@ def _stream(s) -> int | None:
         except Exception:  # noqa: BLE001
             return None
     return s if isinstance(s, int) else s.cuda_stream
+
+
+def selftest_wait_timeout(device: int = 0, limit_us: int = 20000) -> int:
+    """Status of a kernel whose bounded wait on a never-arriving barrier runs
+    out (GZ_ERR_TIMEOUT expected; the context stays usable)."""
+    return int(_lib.gz_selftest_wait_timeout(device, limit_us))
 
 
 def version() -> str:

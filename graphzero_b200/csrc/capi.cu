@@ -15,6 +15,7 @@
 #include "gz_games.h"
 #include "gz_internal.h"
 #include "gz_mcts.h"
+#include "gz_sm100.h"
 #include "gz_synth.h"
 
 using namespace gz;
@@ -514,6 +515,44 @@ gz_status gz_net_broadcast(gz_net* n, void* comm, int root, void* stream) {
   ncclResult_t r = c->broadcast(n->d_weights, n->d_weights, n->weight_count, ncclFloat32, root, (ncclComm_t)comm, s);
   if (r != ncclSuccess) return fail(GZ_ERR_NCCL, "ncclBroadcast: %s", c->errorString ? c->errorString(r) : "?");
   return prepare_weights(n, s);
+}
+
+// ------------------------------------------------------ failure detection --
+namespace {
+// Waits on an mbarrier nothing arrives at; reports through *status:
+// 1 = the bounded wait gave up (expected), 0 = it completed.
+__global__ void wait_timeout_kernel(int* status, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    gz::sm100::mbar_init(&bar, 1);
+    abort_flag = 0;
+    gz::sm100::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = gz::sm100::mbar_wait(&bar, 0, (volatile int*)&abort_flag, limit_ns);
+    *status = ok ? 0 : 1;
+  }
+}
+}  // namespace
+
+gz_status gz_selftest_wait_timeout(int device, int limit_us) {
+  if (limit_us <= 0 || limit_us > 10000000) return fail(GZ_ERR_INVALID_ARG, "limit_us out of range");
+  GZ_DEVICE(device);
+  int* d = nullptr;
+  GZ_CUDA(cudaMalloc(&d, sizeof(int)));
+  GZ_CUDA(cudaMemset(d, 0xFF, sizeof(int)));
+  wait_timeout_kernel<<<1, 32>>>(d, (unsigned long long)limit_us * 1000ull);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  int st = -1;
+  if (e == cudaSuccess) e = cudaMemcpy(&st, d, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (e != cudaSuccess) return fail(GZ_ERR_CUDA, "selftest: %s", cudaGetErrorString(e));
+  if (st == 1) return fail(GZ_ERR_TIMEOUT, "bounded wait gave up after %d us (expected)", limit_us);
+  if (st == 0) return GZ_OK;
+  return fail(GZ_ERR_CUDA, "selftest kernel did not report");
 }
 
 // ---------------------------------------------------------------- search --

@@ -196,6 +196,15 @@ gz_status gz_mcts_play(gz_mcts* m, const int32_t* d_actions, int reserve, int8_t
  * pool, 3 depth); synchronises. */
 gz_status gz_mcts_check(gz_mcts* m);
 
+/* ---- failure detection ---------------------------------------------------
+ * Runs, on `device`, a one-block kernel whose thread waits on an mbarrier
+ * that nothing ever arrives at, through the same bounded wait every kernel of
+ * this library uses, with a limit of `limit_us`.  Returns GZ_ERR_TIMEOUT when
+ * the wait gave up and the kernel exited cleanly (the expected outcome),
+ * GZ_OK if it somehow completed, GZ_ERR_CUDA on a launch error.  The CUDA
+ * context stays usable afterwards. */
+gz_status gz_selftest_wait_timeout(int device, int limit_us);
+
 #ifdef __cplusplus
 }
 #endif

@@ -147,3 +147,14 @@ def test_weights_round_trip(cuda):
     assert (net.save_weights() == w).all()
     with pytest.raises(gz.GZError):
         net.load_weights(w[:-1])
+
+
+def test_bounded_wait_reports_timeout_and_context_survives(cuda):
+    """Failure detection on the GPU without a fault: a wait on a barrier that
+    nothing arrives at gives up after its limit, the kernel exits, the host
+    reads GZ_ERR_TIMEOUT, and the device keeps working."""
+    assert gz.selftest_wait_timeout(0, 20000) == gz.ERR_TIMEOUT
+    net = gz.Net(gz.CONNECT4, precision=gz.PREC_FP32, max_batch=2)
+    boards, side = gz.synth_positions(gz.CONNECT4, 2, seed=3)
+    pi, v = net.predict_host(boards, side)
+    assert np.isfinite(pi).all() and np.isfinite(v).all()
