@@ -43,7 +43,20 @@ CONFIGS = {
     "c1": dict(index=1, game=gz.CONNECT4, kind=gz.GAT, batch=4096, precision=gz.PREC_AUTO, dtype="bf16",
                workload="Connect4 GAT leaf evaluation, 6 layers 8x32 heads, bf16 operands fp32 accumulate, "
                         "batch 4096 per GPU"),
+    "c2": dict(index=2, game=gz.CONNECT4, kind=gz.RESNET, batch=4096, precision=gz.PREC_AUTO, dtype="bf16",
+               workload="Connect4 ResNet leaf evaluation, 3x3 stem + 10 residual blocks of 128 channels, "
+                        "bf16 operands fp32 accumulate, batch 4096 per GPU"),
 }
+
+
+def resnet_gemm_flops() -> float:
+    """Algorithmic FLOPs per position of the ResNet tower (implicit-GEMM
+    convolutions + heads)."""
+    conv = 2.0 * 42 * 128 * 128 * 9
+    f = 20 * conv + 2.0 * 42 * 128 * 27       # blocks + stem
+    f += 2.0 * 42 * 128 * 3                    # 1x1 head convolutions
+    f += 2.0 * 84 * 7 + 2.0 * 42 * 128 + 2.0 * 128
+    return f
 
 
 def gat_gemm_flops(game: int) -> float:
@@ -145,7 +158,10 @@ def cpu_baseline(cfg: dict, w: np.ndarray, seconds: float = 10.0) -> dict:
     done, t0, i = 0, time.perf_counter(), 0
     while True:
         boards, side = gz.synth_positions(game, chunk, seed=gzd.shard_seed(cfg["index"], 0) + 77, first=i * chunk)
-        oracle.gat_forward(game, w, boards, side, threads=threads, native=True)
+        if cfg["kind"] == gz.GAT:
+            oracle.gat_forward(game, w, boards, side, threads=threads, native=True)
+        else:
+            oracle.resnet_forward(w, boards, side, threads=threads, native=True)
         done += chunk
         i += 1
         el = time.perf_counter() - t0
@@ -164,27 +180,30 @@ def reference_arm(args, cfg: dict) -> None:
 
     threads = oracle.cpu_threads()
     game = cfg["game"]
-    w = gz.synth_weights(game, seed=gzd.shard_seed(cfg["index"], 0))
+    w = gz.synth_weights(game, cfg["kind"], seed=gzd.shard_seed(cfg["index"], 0))
+    fwd = (lambda b, s: oracle.gat_forward(game, w, b, s, threads=threads, native=True)) if cfg["kind"] == gz.GAT \
+        else (lambda b, s: oracle.resnet_forward(w, b, s, threads=threads, native=True))
     # size one step so the whole run stays within a couple of minutes
     probe_n = 4 * threads
     b, s = gz.synth_positions(game, probe_n, seed=1)
     t0 = time.perf_counter()
-    oracle.gat_forward(game, w, b, s, threads=threads, native=True)
+    fwd(b, s)
     rate = probe_n / (time.perf_counter() - t0)
     per_step = int(max(threads, min(cfg["batch"], rate * min(2.0, 100.0 / max(1, args.steps + args.warmup)))))
     boards, side = gz.synth_positions(game, per_step * (args.steps + args.warmup),
                                       seed=gzd.shard_seed(cfg["index"], 0))
     for k in range(args.warmup):
         sl = slice(k * per_step, (k + 1) * per_step)
-        oracle.gat_forward(game, w, boards[sl], side[sl], threads=threads, native=True)
+        fwd(boards[sl], side[sl])
     t0 = time.perf_counter()
     for k in range(args.warmup, args.warmup + args.steps):
         sl = slice(k * per_step, (k + 1) * per_step)
-        oracle.gat_forward(game, w, boards[sl], side[sl], threads=threads, native=True)
+        fwd(boards[sl], side[sl])
     el = time.perf_counter() - t0
     value = per_step * args.steps / el
     line = {
-        "impl": "reference", "metric": "leaf evals/sec (Connect4 GAT, b=4096)" if game == gz.CONNECT4 else
+        "impl": "reference", "metric": ("leaf evals/sec (Connect4 GAT, b=4096)" if cfg["kind"] == gz.GAT else
+                                        "leaf evals/sec (Connect4 ResNet, b=4096)") if game == gz.CONNECT4 else
         "leaf evals/sec", "value": value, "unit": "leaf evals/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -252,6 +271,7 @@ def ours(args, cfg: dict) -> None:
     net = gz.Net(game, cfg["kind"], device=dev, precision=cfg["precision"], max_batch=B)
     w = gz.synth_weights(game, cfg["kind"], seed=gzd.shard_seed(cfg["index"], 0))
     comm = None
+    assert net.weight_count() == w.size
     if multi:
         if info.rank == 0:
             net.load_weights(w)
@@ -321,20 +341,21 @@ def ours(args, cfg: dict) -> None:
 
     # ---- batched search throughput (secondary metric) ----
     mcts = None
-    if game == gz.CONNECT4 and args.mcts_moves > 0:
+    if game == gz.CONNECT4 and cfg["kind"] == gz.GAT and args.mcts_moves > 0:
         mcts = mcts_bench(net, dev, game, trees=1024, sims=800, leaves=4, moves=args.mcts_moves,
                           seed=seed)
 
     if comm is not None:
         gz.nccl_comm_destroy(comm)
     if info.rank == 0:
-        flops = gat_gemm_flops(game) * B
+        flops = (gat_gemm_flops(game) if cfg["kind"] == gz.GAT else resnet_gemm_flops()) * B
         peak, peak_src = measured_peak()
         achieved = flops / kernel_s / 1e12
         kernel_name = net.kernel_name
         traffic = ncu_traffic(kernel_name, f"batch{B}")
         line = {
-            "metric": "leaf evals/sec (Connect4 GAT, b=4096)" if game == gz.CONNECT4 else "leaf evals/sec",
+            "metric": ("leaf evals/sec (Connect4 GAT, b=4096)" if cfg["kind"] == gz.GAT else
+                       "leaf evals/sec (Connect4 ResNet, b=4096)") if game == gz.CONNECT4 else "leaf evals/sec",
             "value": value, "unit": "leaf evals/s", "n_gpus": info.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": kernel_name.rsplit("_", 1)[-1].replace("fp", "f"),

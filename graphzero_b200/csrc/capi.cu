@@ -120,7 +120,9 @@ bool use_tensor_cores(const gz_net* n) {
 }
 
 gz_status prepare_weights(gz_net* n, cudaStream_t s) {
-  if (n->kind == GZ_NET_GAT && use_tensor_cores(n)) {
+  if (n->kind == GZ_NET_RESNET) {
+    GZ_CUDA(launch_resnet_tc_pack(n->precision == GZ_PREC_FP16, n->d_weights, n->d_tc, s));
+  } else if (n->kind == GZ_NET_GAT && use_tensor_cores(n)) {
     GZ_CUDA(launch_gat_tc_pack(n->game, n->precision == GZ_PREC_FP16, n->d_weights, n->d_tc, s));
   }
   return GZ_OK;
@@ -136,7 +138,8 @@ gz_status run_forward(gz_net* n, const int8_t* boards, const int8_t* side, int c
       GZ_CUDA(launch_gat_simt(n->game, n->d_weights, n->d_csr, boards, side, count, pi, v, s));
     return GZ_OK;
   }
-  return fail(GZ_ERR_UNSUPPORTED, "network kind %d has no kernel in this build", n->kind);
+  GZ_CUDA(launch_resnet_tc(n->precision == GZ_PREC_FP16, n->d_tc, n->d_weights, boards, side, count, pi, v, n->d_err, s));
+  return GZ_OK;
 }
 
 }  // namespace
@@ -250,6 +253,8 @@ gz_status gz_net_create(const gz_net_config* cfg, int device, gz_net** out) {
   if (cfg->kind != GZ_NET_GAT && cfg->kind != GZ_NET_RESNET) return fail(GZ_ERR_INVALID_ARG, "bad kind %d", cfg->kind);
   if (cfg->kind == GZ_NET_RESNET && cfg->game != kConnect4)
     return fail(GZ_ERR_UNSUPPORTED, "the ResNet tower is built for Connect4 only");
+  if (cfg->kind == GZ_NET_RESNET && cfg->precision == GZ_PREC_FP32)
+    return fail(GZ_ERR_UNSUPPORTED, "the ResNet tower runs on tensor cores (bf16 or fp16 operands)");
   if (cfg->precision < GZ_PREC_AUTO || cfg->precision > GZ_PREC_FP16) return fail(GZ_ERR_INVALID_ARG, "bad precision");
   if (cfg->max_batch < 0) return fail(GZ_ERR_INVALID_ARG, "bad max_batch");
   int ndev = 0;
@@ -276,7 +281,10 @@ gz_status gz_net_create(const gz_net_config* cfg, int device, gz_net** out) {
   chk(cudaMalloc(&n->d_err, sizeof(int)), "cudaMalloc err");
   chk(cudaMemset(n->d_err, 0, sizeof(int)), "cudaMemset err");
   chk(cudaMemcpy(n->d_csr, csr.data(), csr.size() * sizeof(int), cudaMemcpyHostToDevice), "copy csr");
-  if (use_tensor_cores(n)) {
+  if (cfg->kind == GZ_NET_RESNET) {
+    n->tc_bytes = resnet_tc_packed_bytes();
+    chk(cudaMalloc(&n->d_tc, n->tc_bytes), "cudaMalloc packed weights");
+  } else if (use_tensor_cores(n)) {
     n->tc_bytes = gat_tc_packed_bytes(cfg->game);
     if (!n->tc_bytes && st == GZ_OK) st = fail(GZ_ERR_UNSUPPORTED, "no tensor-core kernel for game %d", cfg->game);
     else chk(cudaMalloc(&n->d_tc, n->tc_bytes), "cudaMalloc packed weights");
@@ -322,7 +330,7 @@ size_t gz_net_weight_count(const gz_net* n) { return n ? n->weight_count : 0; }
 
 const char* gz_net_kernel_name(const gz_net* n) {
   if (!n) return "";
-  if (n->kind == GZ_NET_RESNET) return "resnet_tc_bf16";
+  if (n->kind == GZ_NET_RESNET) return n->precision == GZ_PREC_FP16 ? "resnet_tc_fp16" : "resnet_tc_bf16";
   if (!use_tensor_cores(n)) return "gat_simt_fp32";
   return n->precision == GZ_PREC_FP16 ? "gat_tc_fp16" : "gat_tc_bf16";  // gat_tc_c4_kernel
 }

@@ -183,6 +183,26 @@ __device__ __forceinline__ uint64_t noswizzle_desc(uint32_t smem_addr, uint32_t 
   return d;
 }
 
+// 128-byte-swizzle K-major descriptor of a row-shifted view of a tile: the
+// start address may lie anywhere in a 1024-byte swizzle atom (rows are 128
+// bytes apart).  The swizzle is applied to the absolute address bits, so the
+// descriptor is the plain one with base offset 0 (measured on B200: setting
+// the base-offset field to the row phase shifts the pattern twice).
+__device__ __forceinline__ uint64_t sw128_desc_shifted(uint32_t smem_addr) { return sw128_desc(smem_addr); }
+
+// D[tmem] (+)= A[smem] * B[smem] with output rows (lanes) whose bit is set in
+// the 128-bit mask left unchanged (cta_group::1, M = 128: lane i <-> bit
+// i % 32 of word i / 32).
+__device__ __forceinline__ void mma_f16_ss_masked(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate, const uint32_t (&mask)[4]) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(mask[0]), "r"(mask[1]), "r"(mask[2]), "r"(mask[3])
+      : "memory");
+}
+
 // Instruction descriptor for kind::f16: fp32 accumulator, operands of format
 // `fmt` (0 = fp16, 1 = bf16), shape M x N; A K-major, B K-major unless
 // b_mn_major (then B is stored N-contiguous).
