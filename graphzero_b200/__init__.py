@@ -102,6 +102,9 @@ _SIGS = {
     "gz_mcts_play": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
     "gz_mcts_check": (C.c_int, [_vp]),
     "gz_selftest_wait_timeout": (C.c_int, [C.c_int, C.c_int]),
+    "gz_gat_c4_predict_noalloc": (C.c_int, [C.c_int, _f32p, C.c_size_t, _i8p, _i8p, C.c_int, _f32p, _f32p]),
+    "gz_gat_c4_noalloc_scratch_bytes": (C.c_size_t, []),
+    "gz_gat_c4_noalloc_max_batch": (C.c_int, []),
 }
 for _name, (_res, _args) in _SIGS.items():
     _f = getattr(_lib, _name)
@@ -134,6 +137,29 @@ def _stream(s) -> int | None:
         except Exception:  # noqa: BLE001
             return None
     return s if isinstance(s, int) else s.cuda_stream
+
+
+def gat_c4_noalloc_max_batch() -> int:
+    return _lib.gz_gat_c4_noalloc_max_batch()
+
+
+def gat_c4_noalloc_scratch_bytes() -> int:
+    return _lib.gz_gat_c4_noalloc_scratch_bytes()
+
+
+def gat_c4_predict_noalloc(weights: np.ndarray, boards: np.ndarray, side: np.ndarray,
+                           device: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """Connect4 GAT evaluation that allocates no device memory (host buffers
+    in and out, staging in a fixed device array; n <= 4096 per call)."""
+    w = np.ascontiguousarray(weights, np.float32)
+    b = np.ascontiguousarray(boards, np.int8)
+    s = np.ascontiguousarray(side, np.int8)
+    n = s.shape[0]
+    pi = np.empty((n, 7), np.float32)
+    v = np.empty(n, np.float32)
+    _check(_lib.gz_gat_c4_predict_noalloc(device, _ptr(w, C.c_float), w.size, _ptr(b, C.c_int8), _ptr(s, C.c_int8), n,
+                                          _ptr(pi, C.c_float), _ptr(v, C.c_float)))
+    return pi, v
 
 
 def selftest_wait_timeout(device: int = 0, limit_us: int = 20000) -> int:

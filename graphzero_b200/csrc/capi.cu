@@ -32,6 +32,18 @@ gz_status fail(gz_status s, const char* fmt, ...) {
   return s;
 }
 
+}  // namespace
+
+gz_status gz::set_last_error(gz_status s, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return s;
+}
+
+namespace {
+
 #define GZ_CUDA(call)                                                                                  \
   do {                                                                                                 \
     cudaError_t e_ = (call);                                                                           \

@@ -5,7 +5,13 @@
 
 #include "gz_games.h"
 
+#include "../../include/graphzero_b200.h"
+
 namespace gz {
+
+// Records a printf-style message for gz_last_error() of the calling thread
+// and returns `s`.
+gz_status set_last_error(gz_status s, const char* fmt, ...);
 
 // fp32 SIMT fused GAT forward (all layers + heads, one launch).
 //   boards [n][BOARD] int8, side [n] int8 (+1 / -1),

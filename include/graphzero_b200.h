@@ -196,6 +196,27 @@ gz_status gz_mcts_play(gz_mcts* m, const int32_t* d_actions, int reserve, int8_t
  * pool, 3 depth); synchronises. */
 gz_status gz_mcts_check(gz_mcts* m);
 
+/* ---- allocation-free leaf evaluation --------------------------------------
+ * No counterpart in the reference.  For callers that may not allocate device
+ * memory (a plugin inside a host application that fixes the device-memory
+ * budget at start-up; a latency-critical loop that cannot pay for
+ * cudaMalloc/cudaFree, which synchronise the device): Connect4 GAT leaf
+ * evaluation (bf16 tensor-core kernel) from host weights (the Connect4 GAT
+ * blob), host positions int8 [n][42] + side [n], into host pi [n][7], v [n].
+ * It calls no cudaMalloc/cudaFree: all device staging lives in one static
+ * device array of gz_gat_c4_noalloc_scratch_bytes() (about 2.3 MB), reserved
+ * on every GPU that loads the library until the process exits.  n is limited
+ * to gz_gat_c4_noalloc_max_batch() (4096); larger n returns
+ * GZ_ERR_INVALID_ARG.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current, so make that first
+ * call before any stream capture.  All calls share the array: calls that
+ * overlap in time on one device race and must be serialised by the caller.
+ * Synchronous (returns when the outputs are in host memory). */
+gz_status gz_gat_c4_predict_noalloc(int device, const float* h_weights, size_t n_weights, const int8_t* h_boards,
+                                    const int8_t* h_side, int n, float* h_pi, float* h_v);
+size_t gz_gat_c4_noalloc_scratch_bytes(void);
+int gz_gat_c4_noalloc_max_batch(void);
+
 /* ---- failure detection ---------------------------------------------------
  * Runs, on `device`, a one-block kernel whose thread waits on an mbarrier
  * that nothing ever arrives at, through the same bounded wait every kernel of
