@@ -5,26 +5,31 @@
 // layer:
 //   1. projection   Wh[128 x 256] = X[128 x K] . W[K x 256]       (tcgen05.mma,
 //      bf16/fp16 operands from shared memory, fp32 accumulator in tensor
-//      memory: lane = node, column = feature)
+//      memory: lane = node, column = feature), and beside it the attention
+//      scores S[128 x 32] = X . (W a): the per-head dot products
+//      s_i = a_self . Wh_i^h and t_i = a_nbr . Wh_i^h come out of the same
+//      MMA, because a . (x W) = x . (W a).  W a is folded into the packed
+//      weights as a bf16 high part and a bf16 remainder (two columns each),
+//      so the scores keep fp32-level accuracy in the weights.
 //   2. per head h (8 heads, two groups of four run by two warpgroups):
-//      scores   s_i = a_self . Wh_i^h, t_i = a_nbr . Wh_i^h      (in-thread)
-//      softmax  alpha_ij = softmax_j LeakyReLU_0.2(s_i + t_j) over the
-//               8-neighbourhood + self of node i (the Connect4 board graph)
-//      gather   out^h = alpha^h . Wh^h   as a second tcgen05.mma: alpha^h
-//               (128 x 128, fp16, block-diagonal, zero outside each node's
-//               3x3 stencil) is the A operand in tensor memory, Wh^h (fp16)
-//               the B operand in shared memory; the result overwrites the
-//               head's accumulator columns
-//   3. bias + ELU, stored as the next layer's X tile (128-byte swizzled,
-//      K-major) -- or, after the last layer, mean-pooled into the value head
-//      (256->64 ReLU, 64->1 tanh) and column-pooled into the policy head
-//      (256->1 per column, softmax over 7), in fp32.
-// Weights W_l^T are pre-packed on the device into 32 KB chunks (256 feature
-// rows x 64 K, swizzled) and streamed into a two-slot shared-memory ring by
-// one producer thread with 1-D bulk async copies (TMA engine); one thread
-// issues every MMA.  Every wait is bounded (%globaltimer); on a timeout the
-// CTA drains its copies and MMAs, frees tensor memory and reports through
-// the error word.
+//      softmax  e_ij = exp(LeakyReLU_0.2(s_i + t_j) - max_j), z_i = sum_j e_ij
+//               over the 8-neighbourhood + self of node i (the Connect4 board
+//               graph); e (fp16, unnormalised) goes into tensor memory
+//      gather   out^h = e^h . Wh^h   as a second tcgen05.mma: e^h (128 x 128,
+//               block-diagonal, zero outside each node's 3x3 stencil) is the
+//               A operand in tensor memory, Wh^h (fp16) the B operand in
+//               shared memory; the result overwrites the head's accumulator
+//               columns
+//   3. out / z + bias, ELU, stored as the next layer's X tile (128-byte
+//      swizzled, K-major) -- or, after the last layer, mean-pooled into the
+//      value head (256->64 ReLU, 64->1 tanh) and column-pooled into the policy
+//      head (256->1 per column, softmax over 7), in fp32.
+// Weights are pre-packed on the device into 36 KB chunks (256 projection rows
+// + 32 score rows, 64 K each, swizzled) and streamed into a two-slot
+// shared-memory ring by one producer thread with 1-D bulk async copies (TMA
+// engine); one thread issues every MMA.  Every wait is bounded
+// (%globaltimer); on a timeout the CTA drains its copies and MMAs, frees
+// tensor memory and reports through the error word.
 //
 // Reference: networks/gat/gat.cu:836-870 (forward_gat_layer), 916-948
 // (compute_output), 995-1038 (softmax, tanh); the math is the standard GAT
@@ -51,26 +56,34 @@ constexpr int kEpiWarps = 8;        // two warpgroups: heads 0-3 and 4-7
 constexpr int kThreads = (kEpiWarps + 2) * 32;
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
-constexpr int kWChunk = 32768;      // 256 feature rows x 64 K x 2 B
+constexpr int kWRows = 256 + 32;    // projection rows + score rows (16 high parts, 16 remainders)
+constexpr int kWChunk = kWRows * 128;  // 64 K x 2 B per row
+constexpr int kWScoreOff = 256 * 128;  // byte offset of the score rows in a chunk
 constexpr int kWSlots = 2;
 constexpr int kChunksPerTile = 1 + (kLayers - 1) * 4;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAlphaCol = 256;  // alpha buffers: 256 + (2 * group + buffer) * 64
+constexpr uint32_t kAlphaCol = 256;  // e buffers: 256 + (2 * group + buffer) * 64
+// Score accumulator: 32 columns that alias e buffer (group 0, buffer 1)
+// columns 0..31; read at the start of a layer, then re-zeroed by group 0.
+constexpr uint32_t kScoreCol = kAlphaCol + 64;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s per wait
+constexpr float kLog2e = 1.4426950408889634f;
 
 // Shared memory map (bytes).
-constexpr int kSmX = 0;                                // X tile: 4 x 16 KB (K-major, 128 rows)
-constexpr int kSmW = kSmX + 4 * 16384;                 // weight ring
-constexpr int kSmB2 = kSmW + kWSlots * kWChunk;        // Wh^h operand: [group][buffer] 8 KB each
-constexpr int kSmStage = kSmB2 + 4 * 8192;             // alpha staging: [group][24 words][128 nodes]
-constexpr int kSmScore = kSmStage + 2 * 24 * 128 * 4;  // [group][buffer][128][2] floats
-constexpr int kSmVec = kSmScore + 2 * 2 * 128 * 2 * 4; // per layer: a[8][2][32], bias[256]; x2 (layer parity)
-constexpr int kVecFloats = 8 * 2 * 32 + 256;
+constexpr int kStageStride = 112;                       // bytes per staging row (24 used words + pad)
+constexpr int kSmX = 0;                                 // X tile: 4 x 16 KB (K-major, 128 rows)
+constexpr int kSmW = kSmX + 4 * 16384;                  // weight ring
+constexpr int kSmB2 = kSmW + kWSlots * kWChunk;         // Wh^h operand: [group][buffer] 8 KB each
+constexpr int kSmStage = kSmB2 + 4 * 8192;              // e staging: [group][128 rows][kStageStride]
+constexpr int kSmTsc = kSmStage + 2 * 128 * kStageStride;  // t scores: [group][129][4 heads] floats
+constexpr int kSmVec = kSmTsc + 2 * 129 * 16;           // per layer bias[256]; x2 (layer parity)
+constexpr int kVecFloats = 256;
 constexpr int kSmBar = kSmVec + 2 * kVecFloats * 4;
 constexpr int kNumBars = 2 * kWSlots + 1 + 1 + 4 + 4 + 1;  // full, empty, acc_full, x_ready, req[2][2], done2[2][2], drain
 constexpr int kSmMisc = kSmBar + kNumBars * 8;
 constexpr int kSmemBytes = kSmMisc + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+static_assert(kSmW % 1024 == 0 && kWChunk % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 // last-layer head scratch inside the (then unused) X tile
 constexpr int kHeadRowStride = 33;                      // floats, padded
 constexpr int kSmHeadRows = kSmX;                       // [group][128][33] floats
@@ -84,9 +97,9 @@ static_assert(kSmLogit + kGPT * 8 * 4 <= kSmW, "head scratch fits in the X tile"
 struct C4Off {
   static constexpr int kLayer0 = 4 * 256 + 256 + 512;
   static constexpr int kLayerN = 256 * 256 + 256 + 512;
-  __device__ static constexpr int W(int l) { return l == 0 ? 0 : kLayer0 + (l - 1) * kLayerN; }
-  __device__ static constexpr int b(int l) { return W(l) + (l == 0 ? 4 : 256) * 256; }
-  __device__ static constexpr int a(int l) { return b(l) + 256; }
+  __host__ __device__ static constexpr int W(int l) { return l == 0 ? 0 : kLayer0 + (l - 1) * kLayerN; }
+  __host__ __device__ static constexpr int b(int l) { return W(l) + (l == 0 ? 4 : 256) * 256; }
+  __host__ __device__ static constexpr int a(int l) { return b(l) + 256; }
   static constexpr int kHeads = kLayer0 + (kLayers - 1) * kLayerN;
   static constexpr int w_pi = kHeads, b_pi = w_pi + 256, W_v1 = b_pi + 1, b_v1 = W_v1 + 256 * 64;
   static constexpr int w_v2 = b_v1 + 64, b_v2 = w_v2 + 64;
@@ -96,17 +109,31 @@ template <typename T> struct OpType;
 template <> struct OpType<__nv_bfloat16> {
   static constexpr uint32_t fmt = 1;
   static __device__ __forceinline__ uint16_t bits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+  static __device__ __forceinline__ float round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
+  }
+  // stochastic rounding: the low element rounds up when rbits[15:0] plus its
+  // discarded 16 bits carry, the high element likewise with rbits[31:16]
+  static __device__ __forceinline__ uint32_t pack_sr(float lo, float hi, uint32_t rbits) {
+    uint32_t d;
+    asm("cvt.rs.satfinite.bf16x2.f32 %0, %1, %2, %3;" : "=r"(d) : "f"(hi), "f"(lo), "r"(rbits));
+    return d;
   }
 };
 template <> struct OpType<__half> {
   static constexpr uint32_t fmt = 0;
   static __device__ __forceinline__ uint16_t bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
+  static __device__ __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
+  }
+  static __device__ __forceinline__ uint32_t pack_sr(float lo, float hi, uint32_t rbits) {
+    uint32_t d;
+    asm("cvt.rs.satfinite.f16x2.f32 %0, %1, %2, %3;" : "=r"(d) : "f"(hi), "f"(lo), "r"(rbits));
+    return d;
   }
 };
 
@@ -129,8 +156,33 @@ __device__ __forceinline__ bool epilogue_all(bool ok) {
   return r != 0;
 }
 
-__device__ __forceinline__ float lrelu(float x) { return x > 0.f ? x : kLeakySlope * x; }
-__device__ __forceinline__ float elu_fast(float x) { return x > 0.f ? x : __expf(x) - 1.0f; }
+// Random bits for rounding the activations of node `li` (index inside its
+// position, so a position rounds the same way in any batch slot), layer l,
+// head h.  Identical nodes of one position then round independently, and
+// their rounding errors average out in the neighbour gather and the pooling
+// instead of adding up (round-to-nearest gives every node of a uniform board
+// the same error).
+__device__ __forceinline__ uint32_t round_seed(int li, int l, int h) {
+  uint32_t x = (uint32_t)li * 0x9E3779B1u + (uint32_t)(l * 8 + h + 1) * 0x85EBCA77u;
+  x ^= x >> 15;
+  x *= 0x2C1B3C6Du;
+  x ^= x >> 12;
+  return x;
+}
+// per feature pair m of a head: seed ^ kPairMix[m] (odd Weyl steps)
+__host__ __device__ constexpr uint32_t pair_mix(int m) { return (uint32_t)(m + 1) * 0x9E3779B9u ^ 0x7F4A7C15u; }
+
+__device__ __forceinline__ float comp(const float4& v, int k) {
+  return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
+}
+
+// ELU of two values: max(2^(-|y| log2 e) - 1, y) equals y for y > 0 and
+// e^y - 1 otherwise (e^y - 1 >= y everywhere), with no select.
+__device__ __forceinline__ float2 elu2(float2 y) {
+  const float2 zl = __fmul2_rn(y, make_float2(kLog2e, kLog2e));
+  const float2 em = __fadd2_rn(make_float2(ex2_approx(-fabsf(zl.x)), ex2_approx(-fabsf(zl.y))), make_float2(-1.f, -1.f));
+  return make_float2(fmaxf(em.x, y.x), fmaxf(em.y, y.y));
+}
 
 // First node of the 48-node window that covers every neighbour of the 32
 // nodes owned by lane quarter q (nodes 32q .. 32q+31 have neighbours within
@@ -139,7 +191,7 @@ __device__ __forceinline__ int window_start(int q) { return q == 0 ? 0 : q == 3 
 
 struct TcParams {
   const uint8_t* packed;  // kChunksPerTile chunks in consumption order
-  const float* w;         // fp32 blob (biases, attention vectors, heads)
+  const float* w;         // fp32 blob (biases, heads)
   const int8_t* boards;
   const int8_t* side;
   float* pi;
@@ -175,8 +227,10 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // zero the alpha staging (its zero pattern is static) and init barriers
-  for (int i = threadIdx.x; i < 2 * 24 * 128; i += blockDim.x) ((uint32_t*)(smem + kSmStage))[i] = 0u;
+  // zero the e staging (its zero pattern is static), fill the t-score rows
+  // of the "no neighbour" node (index 128) with -inf, init barriers
+  for (int i = threadIdx.x; i < 2 * 128 * kStageStride / 4; i += blockDim.x) ((uint32_t*)(smem + kSmStage))[i] = 0u;
+  if (threadIdx.x < 8) ((float*)(smem + kSmTsc))[(threadIdx.x >> 2) * 129 * 4 + 128 * 4 + (threadIdx.x & 3)] = -INFINITY;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kWSlots; ++s) {
       mbar_init(&full[s], 1);
@@ -223,6 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc1 = idesc_f16(OpType<OpT>::fmt, 128, 256);
+      constexpr uint32_t idesc_s = idesc_f16(OpType<OpT>::fmt, 128, 32);
       constexpr uint32_t idesc2 = idesc_f16(0 /* fp16 */, 128, 32, 1 /* B N-contiguous */);
       const uint32_t xs = smem_u32(sX);
       const uint32_t b2s = smem_u32(smem + kSmB2);
@@ -242,8 +297,11 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
             if (!ok) break;
             tc_fence_after();
             const uint32_t ws = smem_u32(sW + s * kWChunk);
-            for (int kk = 0; kk < ksteps; ++kk)
-              mma_f16_ss(tmem, sw128_desc(xs + c * 16384 + kk * 32), sw128_desc(ws + kk * 32), idesc1, (c | kk) != 0);
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const uint64_t adesc = sw128_desc(xs + c * 16384 + kk * 32);
+              mma_f16_ss(tmem, adesc, sw128_desc(ws + kk * 32), idesc1, (c | kk) != 0);
+              mma_f16_ss(tmem + kScoreCol, adesc, sw128_desc(ws + kWScoreOff + kk * 32), idesc_s, (c | kk) != 0);
+            }
             mma_commit(&empty[s]);
           }
           if (!ok) break;
@@ -290,24 +348,27 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
     const int li = i % kN, rr = li / 7, cc = li % 7;
     const bool real = i < kGPT * kN;
     const int jw0 = window_start(qd);
-    uint32_t* stage = (uint32_t*)(smem + kSmStage) + g * 24 * 128;
-    // node i's 3x3 stencil: validity bits and the staging address of each
-    // neighbour's alpha (word (j - jw0) / 2 of column i, half (j - jw0) % 2)
-    uint32_t nmask = 0, saddr[9];
+    uint8_t* srow = smem + kSmStage + (g * 128 + i) * kStageStride;
+    const float4* tsc = (const float4*)(smem + kSmTsc) + g * 129;
+    // node i's 3x3 stencil: the t-score row of each neighbour (128 = none,
+    // whose scores are -inf) and the staging address of its e (half-word
+    // j - jw0 of row i; absent neighbours write a pad half-word).  Padding
+    // rows attend to themselves only.
+    int nidx[9];
+    uint32_t saddr[9];
 #pragma unroll
     for (int k = 0; k < 9; ++k) {
       const int dr = k / 3 - 1, dc = k % 3 - 1;
-      const bool in = real && (unsigned)(rr + dr) < 6u && (unsigned)(cc + dc) < 7u;
-      nmask |= (uint32_t)in << k;
-      const int wpos = in ? i + 7 * dr + dc - jw0 : 0;  // 0..47
-      saddr[k] = smem_u32(stage + (wpos >> 1) * 128 + i) + (wpos & 1) * 2;
+      const bool in = real ? ((unsigned)(rr + dr) < 6u && (unsigned)(cc + dc) < 7u) : k == 4;
+      nidx[k] = in ? i + 7 * dr + dc : 128;
+      saddr[k] = smem_u32(srow) + 2 * (in ? i + 7 * dr + dc - jw0 : 48);
     }
-    float* score = (float*)(smem + kSmScore) + g * 2 * 128 * 2;
     const int gbar = 3 + g;
     uint32_t aph = 0, dph[2] = {0, 0};
-    bool ok = true;
+    bool ok = true;    // collective: changes only through epilogue_all
+    bool wok = true;   // this thread's waits inside a layer; folded into the next vote
 
-    // zero this warp's lanes of both alpha buffers of its group (static background)
+    // zero this warp's lanes of both e buffers of its group (static background)
     {
       uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       for (int b = 0; b < 2; ++b)
@@ -336,52 +397,81 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
 
       for (int l = 0; l < kLayers && ok; ++l) {
         const bool last = l == kLayers - 1;
-        // per-layer vectors (attention a, bias) into shared memory, by layer parity
+        // per-layer bias into shared memory, by layer parity
         float* vec = (float*)(smem + kSmVec) + (l & 1) * kVecFloats;
-        for (int t = threadIdx.x; t < kVecFloats; t += kEpiWarps * 32)
-          vec[t] = t < 512 ? __ldg(p.w + C4Off::a(l) + t) : __ldg(p.w + C4Off::b(l) + t - 512);
-        ok = epilogue_all(mbar_wait(acc_full, aph & 1, abort_flag, kWaitLimitNs));  // also publishes vec
+        vec[threadIdx.x] = __ldg(p.w + C4Off::b(l) + threadIdx.x);
+        wok = mbar_wait(acc_full, aph & 1, abort_flag, kWaitLimitNs) && wok;
+        ok = epilogue_all(wok);  // also publishes vec
         ++aph;
         if (!ok) break;
         tc_fence_after();
 
+        // ---- scores of this group's heads: high part + remainder ----
+        float s[4];
+        {
+          float hi[8], lo[8];
+          tmem_ld_x8(tlane + kScoreCol + 8 * g, hi);
+          tmem_ld_x8(tlane + kScoreCol + 16 + 8 * g, lo);
+          tmem_ld_wait();
+#pragma unroll
+          for (int t = 0; t < 4; ++t) s[t] = hi[2 * t] + lo[2 * t];
+          ((float4*)(smem + kSmTsc))[g * 129 + i] =
+              make_float4(hi[1] + lo[1], hi[3] + lo[3], hi[5] + lo[5], hi[7] + lo[7]);
+        }
+        tc_fence_before();
+        named_bar_sync(1, kEpiWarps * 32);  // t scores visible; score columns read by everyone
+        tc_fence_after();
+        if (g == 0) {  // restore the zero background of e buffer (0, 1) under the score columns
+          uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) tmem_st_x8(tlane + kScoreCol + c, z);
+          tmem_st_wait();
+        }
+        float4 tn[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) tn[k] = tsc[nidx[k]];
+
         float* hrow = (float*)(smem + kSmHeadRows) + g * 128 * kHeadRowStride;
         float* pcol = (float*)(smem + kSmPcol);
         float* pooled = (float*)(smem + kSmPooled);
+        float inv[4] = {0.f, 0.f, 0.f, 0.f};
 
-        // P3: result of head t -> bias, ELU -> next X (or head pooling)
+        // P3: result of head t -> / z, + bias, ELU -> next X (or head pooling)
         auto finish_head = [&](int t) {
           const int h = 4 * g + t, b = t & 1;
-          ok = mbar_wait(&done2[2 * g + b], dph[b] & 1, abort_flag, kWaitLimitNs) && ok;
+          wok = mbar_wait(&done2[2 * g + b], dph[b] & 1, abort_flag, kWaitLimitNs) && wok;
           ++dph[b];
           tc_fence_after();
           float o[32];
           tmem_ld_x32(tlane + (uint32_t)(32 * h), o);
           tmem_ld_wait();
-          const float4* bias4 = (const float4*)(vec + 512 + 32 * h);
-          if (!last) {
-            uint32_t w[16];
+          const float4* bias4 = (const float4*)(vec + 32 * h);
+          const float2 iv = make_float2(inv[t], inv[t]);
+          float2 y[16];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const float4 bv = bias4[k];
-              w[2 * k] = OpType<OpT>::pack(elu_fast(o[4 * k] + bv.x), elu_fast(o[4 * k + 1] + bv.y));
-              w[2 * k + 1] = OpType<OpT>::pack(elu_fast(o[4 * k + 2] + bv.z), elu_fast(o[4 * k + 3] + bv.w));
-            }
+          for (int k = 0; k < 8; ++k) {
+            const float4 bv = bias4[k];
+            y[2 * k] = elu2(__ffma2_rn(make_float2(o[4 * k], o[4 * k + 1]), iv, make_float2(bv.x, bv.y)));
+            y[2 * k + 1] = elu2(__ffma2_rn(make_float2(o[4 * k + 2], o[4 * k + 3]), iv, make_float2(bv.z, bv.w)));
+          }
+          if (!last) {
+            // the next layer's operand, stochastically rounded (see round_seed)
+            const uint32_t seed = round_seed(li, l, h);
             uint8_t* xrow = sX + (h >> 1) * 16384 + (i >> 3) * 1024 + (i & 7) * 128;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const int unit = (4 * (h & 1) + u) ^ (i & 7);
-              *(uint4*)(xrow + unit * 16) = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+              uint32_t q[4];
+#pragma unroll
+              for (int m = 0; m < 4; ++m) q[m] = OpType<OpT>::pack_sr(y[4 * u + m].x, y[4 * u + m].y, seed ^ pair_mix(4 * u + m));
+              *(uint4*)(xrow + unit * 16) = make_uint4(q[0], q[1], q[2], q[3]);
             }
           } else {
             // fp32 rows of this head into scratch, then per-position pooling
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const float4 bv = bias4[k];
-              hrow[i * kHeadRowStride + 4 * k + 0] = elu_fast(o[4 * k + 0] + bv.x);
-              hrow[i * kHeadRowStride + 4 * k + 1] = elu_fast(o[4 * k + 1] + bv.y);
-              hrow[i * kHeadRowStride + 4 * k + 2] = elu_fast(o[4 * k + 2] + bv.z);
-              hrow[i * kHeadRowStride + 4 * k + 3] = elu_fast(o[4 * k + 3] + bv.w);
+            for (int k = 0; k < 16; ++k) {
+              hrow[i * kHeadRowStride + 2 * k + 0] = y[k].x;
+              hrow[i * kHeadRowStride + 2 * k + 1] = y[k].y;
             }
             named_bar_sync(gbar, 128);
             const int tid = threadIdx.x & 127;
@@ -406,30 +496,17 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
 
         // The head loop always runs to the end (waits return at once after an
         // abort), so every thread meets every named barrier; the decision to
-        // stop is collective, at the end of the layer.
+        // stop is collective, at the next layer's start.
+#pragma unroll
         for (int t = 0; t < 4; ++t) {
           const int h = 4 * g + t, b = t & 1;
-          // ---- P1: Wh^h (fp32) -> scores, fp16 copy as the gather's B operand ----
-          float wh[32];
-          tmem_ld_x32(tlane + (uint32_t)(32 * h), wh);
-          tmem_ld_wait();
-          const float4* as4 = (const float4*)(vec + (h * 2 + 0) * 32);
-          const float4* an4 = (const float4*)(vec + (h * 2 + 1) * 32);
-          // four independent partial sums per score (short dependency chains)
-          float sp[4] = {0.f, 0.f, 0.f, 0.f}, tp[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const float4 a1 = as4[k], a2 = an4[k];
-            sp[0] = fmaf(a1.x, wh[4 * k], sp[0]); sp[1] = fmaf(a1.y, wh[4 * k + 1], sp[1]);
-            sp[2] = fmaf(a1.z, wh[4 * k + 2], sp[2]); sp[3] = fmaf(a1.w, wh[4 * k + 3], sp[3]);
-            tp[0] = fmaf(a2.x, wh[4 * k], tp[0]); tp[1] = fmaf(a2.y, wh[4 * k + 1], tp[1]);
-            tp[2] = fmaf(a2.z, wh[4 * k + 2], tp[2]); tp[3] = fmaf(a2.w, wh[4 * k + 3], tp[3]);
-          }
-          const float si = (sp[0] + sp[1]) + (sp[2] + sp[3]);
-          const float ti = (tp[0] + tp[1]) + (tp[2] + tp[3]);
-          // Wh^h (fp16) as the gather's B operand, N-contiguous without swizzle:
-          // node i's 8-feature group ng at ng * 128 + (i / 8) * 512 + (i % 8) * 16
+          // ---- P1: Wh^h (fp32) -> fp16 copy as the gather's B operand ----
           {
+            float wh[32];
+            tmem_ld_x32(tlane + (uint32_t)(32 * h), wh);
+            tmem_ld_wait();
+            // N-contiguous without swizzle: node i's 8-feature group ng at
+            // ng * 128 + (i / 8) * 512 + (i % 8) * 16
             uint8_t* b2 = smem + kSmB2 + (2 * g + b) * 8192 + (i >> 3) * 512 + (i & 7) * 16;
 #pragma unroll
             for (int ng = 0; ng < 4; ++ng)
@@ -437,41 +514,44 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
                   make_uint4(OpType<__half>::pack(wh[8 * ng + 0], wh[8 * ng + 1]), OpType<__half>::pack(wh[8 * ng + 2], wh[8 * ng + 3]),
                              OpType<__half>::pack(wh[8 * ng + 4], wh[8 * ng + 5]), OpType<__half>::pack(wh[8 * ng + 6], wh[8 * ng + 7]));
           }
-          ((float2*)score)[b * 128 + i] = make_float2(si, ti);
-          fence_proxy_async_smem();
-          tc_fence_before();
-          named_bar_sync(gbar, 128);  // scores of every node of the head are visible
-          // ---- P2: neighbour softmax of node i -> alpha row (fp16) in tensor memory ----
+          // ---- P2: neighbour softmax numerators of node i -> e row (fp16) in tensor memory ----
           {
-            const float2* sc = (const float2*)score + b * 128;
-            float ev[9];
+            float lg[9];
             float mx = -INFINITY;
 #pragma unroll
             for (int k = 0; k < 9; ++k) {
-              const int dr = k / 3 - 1, dc = k % 3 - 1;
-              ev[k] = (nmask >> k) & 1u ? lrelu(si + sc[i + 7 * dr + dc].y) : -INFINITY;
-              mx = fmaxf(mx, ev[k]);
+              const float x = s[t] + comp(tn[k], t);
+              lg[k] = fmaxf(x, kLeakySlope * x);
+              mx = fmaxf(mx, lg[k]);
             }
+            const float c = -mx * kLog2e;
+            // z sums the fp16 values the gather multiplies, so the weights
+            // e / z form an exact convex combination (a uniform neighbourhood
+            // reproduces Wh exactly instead of drifting by the rounding of z)
             float z = 0.f;
 #pragma unroll
             for (int k = 0; k < 9; ++k) {
-              ev[k] = ev[k] == -INFINITY ? 0.f : __expf(ev[k] - mx);
-              z += ev[k];
+              const __half e = __float2half_rn(ex2_approx(fmaf(lg[k], kLog2e, c)));
+              z += __half2float(e);
+              asm volatile("st.shared.b16 [%0], %1;" ::"r"(saddr[k]), "h"(__half_as_ushort(e)) : "memory");
             }
-            const float inv = real ? 1.0f / z : 0.f;
-#pragma unroll
-            for (int k = 0; k < 9; ++k)
-              if ((nmask >> k) & 1u)
-                asm volatile("st.shared.b16 [%0], %1;" ::"r"(saddr[k]), "h"(OpType<__half>::bits(ev[k] * inv)) : "memory");
+            inv[t] = __frcp_rn(z);
             uint32_t a[24];
 #pragma unroll
-            for (int k = 0; k < 24; ++k) a[k] = stage[k * 128 + i];
+            for (int k = 0; k < 6; ++k) {
+              const uint4 v = *(const uint4*)(srow + 16 * k);
+              a[4 * k] = v.x;
+              a[4 * k + 1] = v.y;
+              a[4 * k + 2] = v.z;
+              a[4 * k + 3] = v.w;
+            }
             const uint32_t acol = tlane + kAlphaCol + (uint32_t)((2 * g + b) * 64 + (jw0 >> 1));
             tmem_st_x8(acol, *(const uint32_t(*)[8])(a));
             tmem_st_x8(acol + 8, *(const uint32_t(*)[8])(a + 8));
             tmem_st_x8(acol + 16, *(const uint32_t(*)[8])(a + 16));
             tmem_st_wait();
           }
+          fence_proxy_async_smem();  // B2 writes -> the MMA's async proxy
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&req[2 * g + b]);
@@ -479,8 +559,6 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           if (t >= 1) finish_head(t - 1);
         }
         finish_head(3);
-        ok = epilogue_all(ok);
-        if (!ok) break;
         if (!last) {
           fence_proxy_async_smem();
           tc_fence_before();
@@ -491,6 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           float* zbuf = (float*)(smem + kSmZ);
           float* logit = (float*)(smem + kSmLogit);
           const int tid = threadIdx.x;  // 0..255
+          named_bar_sync(1, kEpiWarps * 32);  // pooled sums of both groups visible
           if (tid < kGPT * 64) {
             const int pg = tid / 64, u = tid % 64;
             float acc = __ldg(p.w + C4Off::b_v1 + u);
@@ -538,21 +617,35 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
   }
 }
 
-// ---- weight packing: W_l^T into swizzled 32 KB chunks [256 features][64 K] ----
+// ---- weight packing: 36 KB chunks [288 rows][64 K], 128-byte swizzled ----
+// Rows 0..255: W_l^T (feature f, K).  Rows 256..287: the attention-score
+// weights W_l a_l^h: row 256 + 2h + v holds the bf16/fp16 rounding of
+// sum_f W_l[k][32h + f] a_l[h][v][f] (v = 0 self, 1 neighbour), row 272 + 2h + v
+// the rounding of what is left over.
 template <typename OpT>
 __global__ void pack_c4_kernel(const float* __restrict__ w, uint8_t* __restrict__ out) {
   const int chunk = blockIdx.x;  // 0 .. kChunksPerTile-1
   const int layer = chunk == 0 ? 0 : 1 + (chunk - 1) / 4;
   const int c = chunk == 0 ? 0 : (chunk - 1) % 4;
   const int fin = layer == 0 ? 4 : 256;
-  const int w_off = layer == 0 ? 0 : C4Off::kLayer0 + (layer - 1) * C4Off::kLayerN;
-  const float* W = w + w_off;
+  const float* W = w + C4Off::W(layer);
+  const float* A = w + C4Off::a(layer);
   uint8_t* dst = out + (size_t)chunk * kWChunk;
   for (int t = threadIdx.x; t < 256 * 64; t += blockDim.x) {
     const int f = t / 64, kk = t % 64;  // feature row, K within chunk
     const int k = c * 64 + kk;
     const float x = k < fin ? W[(size_t)k * kHidden + f] : 0.f;
-    *(uint16_t*)(dst + (f >> 7) * 16384 + sw128_offset(f & 127, kk)) = OpType<OpT>::bits(x);
+    *(uint16_t*)(dst + sw128_offset(f, kk)) = OpType<OpT>::bits(x);
+  }
+  for (int t = threadIdx.x; t < 16 * 64; t += blockDim.x) {
+    const int j = t / 64, kk = t % 64;  // score column j = 2h + v
+    const int k = c * 64 + kk, h = j >> 1, v = j & 1;
+    float acc = 0.f;
+    if (k < fin)
+      for (int f = 0; f < 32; ++f) acc = fmaf(W[(size_t)k * kHidden + 32 * h + f], A[(2 * h + v) * 32 + f], acc);
+    const float hi = OpType<OpT>::round(acc);
+    *(uint16_t*)(dst + sw128_offset(256 + j, kk)) = OpType<OpT>::bits(hi);
+    *(uint16_t*)(dst + sw128_offset(272 + j, kk)) = OpType<OpT>::bits(acc - hi);
   }
 }
 

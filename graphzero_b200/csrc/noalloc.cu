@@ -40,7 +40,7 @@ constexpr size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 constexpr size_t kWeightsFloats = 350082;  // Connect4 GAT blob (gat_layout), checked at run time
 constexpr size_t kOffWeights = 0;
 constexpr size_t kOffPacked = align256(kOffWeights + kWeightsFloats * sizeof(float));
-constexpr size_t kPackedBytes = 21 * 32768;  // checked against gat_tc_packed_bytes at run time
+constexpr size_t kPackedBytes = 21 * 36864;  // checked against gat_tc_packed_bytes at run time
 constexpr size_t kOffBoards = align256(kOffPacked + kPackedBytes);
 constexpr size_t kOffSide = align256(kOffBoards + (size_t)kNoAllocMaxBatch * kC4Board);
 constexpr size_t kOffPi = align256(kOffSide + kNoAllocMaxBatch);
