@@ -39,6 +39,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "gz_games.h"
 #include "gz_internal.h"
 #include "gz_sm100.h"
@@ -87,11 +89,11 @@ static_assert(kSmW % 1024 == 0 && kWChunk % 1024 == 0, "swizzled tiles need 1024
 // last-layer head scratch inside the (then unused) X tile
 constexpr int kHeadRowStride = 33;                      // floats, padded
 constexpr int kSmHeadRows = kSmX;                       // [group][128][33] floats
-constexpr int kSmPooled = kSmHeadRows + 2 * 128 * kHeadRowStride * 4;  // [3][256]
-constexpr int kSmPcol = kSmPooled + kGPT * 256 * 4;     // [3][7][256] column means
-constexpr int kSmZ = kSmPcol + kGPT * 7 * 256 * 4;      // [3][64]
-constexpr int kSmLogit = kSmZ + kGPT * 64 * 4;          // [3][8]
-static_assert(kSmLogit + kGPT * 8 * 4 <= kSmW, "head scratch fits in the X tile");
+constexpr int kSmPooled = kSmHeadRows + 2 * 128 * kHeadRowStride * 4;  // [group][3][32] one head's node means
+constexpr int kSmZ = kSmPooled + 2 * kGPT * 32 * 4;     // [group][half][3][64] value-head partial sums
+constexpr int kSmLogit = kSmZ + 2 * 2 * kGPT * 64 * 4;  // [group][3][8] policy-logit partial sums
+constexpr int kSmLgAcc = kSmLogit + 2 * kGPT * 8 * 4;   // [group][96 pooling lanes][7] running sums
+static_assert(kSmLgAcc + 2 * kGPT * 32 * 7 * 4 <= kSmW, "head scratch fits in the X tile");
 
 // Offsets (floats) into the fp32 weight blob for Connect4 (gat_layout order).
 struct C4Off {
@@ -189,6 +191,7 @@ __device__ __forceinline__ float2 elu2(float2 y) {
 // +-8); clamped to [0, 80] so the window stays inside the 128 columns.
 __device__ __forceinline__ int window_start(int q) { return q == 0 ? 0 : q == 3 ? 80 : 32 * q - 8; }
 
+
 struct TcParams {
   const uint8_t* packed;  // kChunksPerTile chunks in consumption order
   const float* w;         // fp32 blob (biases, heads)
@@ -275,12 +278,17 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
+    // One thread issues every MMA; its own instruction stream is on the
+    // critical path of the small gather MMAs, so descriptors are built once
+    // and advanced by adding (byte offset >> 4) to the start-address field
+    // (no carry out of the 14-bit field: shared addresses stay below 2^18).
     if (lane == 0) {
       constexpr uint32_t idesc1 = idesc_f16(OpType<OpT>::fmt, 128, 256);
       constexpr uint32_t idesc_s = idesc_f16(OpType<OpT>::fmt, 128, 32);
       constexpr uint32_t idesc2 = idesc_f16(0 /* fp16 */, 128, 32, 1 /* B N-contiguous */);
-      const uint32_t xs = smem_u32(sX);
-      const uint32_t b2s = smem_u32(smem + kSmB2);
+      const uint64_t xdesc = sw128_desc(smem_u32(sX));
+      const uint64_t wdesc0 = sw128_desc(smem_u32(sW));
+      const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
       uint32_t q = 0, xph = 0, rph[4] = {0, 0, 0, 0};
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
@@ -289,42 +297,49 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           ++xph;
           if (!ok) break;
           tc_fence_after();
-          const int nchunk = l == 0 ? 1 : 4;  // K chunks of 64
-          const int ksteps = l == 0 ? 1 : 4;  // K = 16 per MMA (layer 0: 4 features -> one step)
+          const int nchunk = l == 0 ? 1 : 4;  // K chunks of 64 (layer 0: 4 features -> one K = 16 step)
           for (int c = 0; c < nchunk && ok; ++c, ++q) {
             const int s = q % kWSlots;
             ok = mbar_wait(&full[s], (q / kWSlots) & 1, abort_flag, kWaitLimitNs);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t ws = smem_u32(sW + s * kWChunk);
-            for (int kk = 0; kk < ksteps; ++kk) {
-              const uint64_t adesc = sw128_desc(xs + c * 16384 + kk * 32);
-              mma_f16_ss(tmem, adesc, sw128_desc(ws + kk * 32), idesc1, (c | kk) != 0);
-              mma_f16_ss(tmem + kScoreCol, adesc, sw128_desc(ws + kWScoreOff + kk * 32), idesc_s, (c | kk) != 0);
+            const uint64_t xd = xdesc + (uint64_t)(c * (16384 >> 4)), wd = wdesc0 + (uint64_t)(s * (kWChunk >> 4));
+            mma_f16_ss(tmem, xd, wd, idesc1, c != 0);
+            mma_f16_ss(tmem + kScoreCol, xd, wd + (kWScoreOff >> 4), idesc_s, c != 0);
+            if (l != 0) {
+#pragma unroll
+              for (int kk = 1; kk < 4; ++kk) {  // K = 16 per MMA: 32 bytes along the swizzled row
+                mma_f16_ss(tmem, xd + kk * 2, wd + kk * 2, idesc1, 1);
+                mma_f16_ss(tmem + kScoreCol, xd + kk * 2, wd + (kWScoreOff >> 4) + kk * 2, idesc_s, 1);
+              }
             }
             mma_commit(&empty[s]);
           }
           if (!ok) break;
           mma_commit(acc_full);
-          // gathers: serve whichever group's next head is ready (each group's
-          // heads in order), eight per layer
+          // gathers: serve whichever group's next head is ready (each
+          // group's heads in order), eight per layer; polling never blocks
+          // on one group's barrier
           int next_t[2] = {0, 0};
           uint64_t t0 = global_timer_ns();
           while (ok && (next_t[0] < 4 || next_t[1] < 4)) {
             bool issued = false;
+#pragma unroll
             for (int g = 0; g < 2; ++g) {
               if (next_t[g] >= 4) continue;
-              const int t = next_t[g], b = t & 1, h = 4 * g + t;
-              if (!mbar_try_wait(&req[2 * g + b], rph[2 * g + b] & 1)) continue;
-              ++rph[2 * g + b];
+              const int t = next_t[g], ab = 2 * g + (t & 1);
+              if (!mbar_test_wait(&req[ab], rph[ab] & 1)) continue;
+              ++rph[ab];
               ++next_t[g];
               tc_fence_after();
-              const uint32_t a_col = tmem + kAlphaCol + (uint32_t)((2 * g + b) * 64);
-              const uint32_t bb = b2s + (uint32_t)((2 * g + b) * 8192);
-              for (int kk = 0; kk < 8; ++kk)  // K = 16 nodes = two 8-row core-matrix groups per step
-                mma_f16_ts(tmem + (uint32_t)(32 * h), a_col + kk * 8, noswizzle_desc(bb + kk * 1024, 512, 128), idesc2,
-                           kk != 0);
-              mma_commit(&done2[2 * g + b]);
+              const uint32_t d = tmem + (uint32_t)(32 * (4 * g + t));
+              const uint32_t a_col = tmem + kAlphaCol + (uint32_t)(ab * 64);
+              const uint64_t bd = b2desc0 + (uint64_t)(ab * (8192 >> 4));
+              mma_f16_ts(d, a_col, bd, idesc2, 0);
+#pragma unroll
+              for (int kk = 1; kk < 8; ++kk)  // K = 16 nodes: 8 columns of e, two 8-row core-matrix groups of Wh
+                mma_f16_ts(d, a_col + kk * 8, bd + kk * (1024 >> 4), idesc2, 1);
+              mma_commit(&done2[ab]);
               issued = true;
             }
             if (issued) {
@@ -395,15 +410,17 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
       __syncwarp();
       if (lane == 0) mbar_arrive(x_ready);
 
-      for (int l = 0; l < kLayers && ok; ++l) {
-        const bool last = l == kLayers - 1;
+      // One layer.  `last` is a compile-time flag, so the last layer's head
+      // code does not share registers with the head loop of the others.
+      auto layer = [&](int l, auto last_tag) -> bool {
+        constexpr bool last = decltype(last_tag)::value;
         // per-layer bias into shared memory, by layer parity
         float* vec = (float*)(smem + kSmVec) + (l & 1) * kVecFloats;
         vec[threadIdx.x] = __ldg(p.w + C4Off::b(l) + threadIdx.x);
         wok = mbar_wait(acc_full, aph & 1, abort_flag, kWaitLimitNs) && wok;
         ok = epilogue_all(wok);  // also publishes vec
         ++aph;
-        if (!ok) break;
+        if (!ok) return false;
         tc_fence_after();
 
         // ---- scores of this group's heads: high part + remainder ----
@@ -432,9 +449,16 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
         for (int k = 0; k < 9; ++k) tn[k] = tsc[nidx[k]];
 
         float* hrow = (float*)(smem + kSmHeadRows) + g * 128 * kHeadRowStride;
-        float* pcol = (float*)(smem + kSmPcol);
-        float* pooled = (float*)(smem + kSmPooled);
+        float* pooled = (float*)(smem + kSmPooled) + g * kGPT * 32;
         float inv[4] = {0.f, 0.f, 0.f, 0.f};
+        // last layer: the heads are accumulated head by head.  Value head:
+        // thread (u, half) of the group sums pooled[c] W_v1[c][u] over the 16
+        // features c of its half of each head; policy head: the pooling lanes
+        // sum column-mean x w_pi over their feature.
+        // The running sums live in thread-private shared-memory slots.
+        const int gt = threadIdx.x & 127, vu = gt & 63, vhalf = gt >> 6;
+        float* zacc = (float*)(smem + kSmZ) + (g * 2 + vhalf) * kGPT * 64 + vu;  // [pg * 64]
+        float* lgacc = (float*)(smem + kSmLgAcc) + (g * kGPT * 32 + gt) * 7;     // pooling lanes only
 
         // P3: result of head t -> / z, + bias, ELU -> next X (or head pooling)
         auto finish_head = [&](int t) {
@@ -454,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
             y[2 * k] = elu2(__ffma2_rn(make_float2(o[4 * k], o[4 * k + 1]), iv, make_float2(bv.x, bv.y)));
             y[2 * k + 1] = elu2(__ffma2_rn(make_float2(o[4 * k + 2], o[4 * k + 3]), iv, make_float2(bv.z, bv.w)));
           }
-          if (!last) {
+          if constexpr (!last) {
             // the next layer's operand, stochastically rounded (see round_seed)
             const uint32_t seed = round_seed(li, l, h);
             uint8_t* xrow = sX + (h >> 1) * 16384 + (i >> 3) * 1024 + (i & 7) * 128;
@@ -473,10 +497,13 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
               hrow[i * kHeadRowStride + 2 * k + 0] = y[k].x;
               hrow[i * kHeadRowStride + 2 * k + 1] = y[k].y;
             }
+            // this thread's W_v1 slice for the head (lands during the pooling)
+            float wv[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) wv[j] = __ldg(p.w + C4Off::W_v1 + (32 * h + 16 * vhalf + j) * 64 + vu);
             named_bar_sync(gbar, 128);
-            const int tid = threadIdx.x & 127;
-            if (tid < kGPT * 32) {
-              const int pg = tid >> 5, d = tid & 31;
+            if (gt < kGPT * 32) {
+              const int pg = gt >> 5, d = gt & 31;
               float cs[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, tot = 0.f;
 #pragma unroll
               for (int r = 0; r < 6; ++r)
@@ -486,11 +513,19 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
                   cs[c] += x;
                   tot += x;
                 }
-              pooled[pg * 256 + 32 * h + d] = tot * (1.0f / kN);
+              pooled[pg * 32 + d] = tot * (1.0f / kN);
+              const float wp = __ldg(p.w + C4Off::w_pi + 32 * h + d) * (1.0f / 6.0f);
 #pragma unroll
-              for (int c = 0; c < 7; ++c) pcol[(pg * 7 + c) * 256 + 32 * h + d] = cs[c] * (1.0f / 6.0f);
+              for (int c = 0; c < 7; ++c) lgacc[c] = fmaf(cs[c], wp, t == 0 ? 0.f : lgacc[c]);
             }
-            named_bar_sync(gbar, 128);  // scratch reused by the next head
+            named_bar_sync(gbar, 128);  // node means visible; scratch reused by the next head
+#pragma unroll
+            for (int pg = 0; pg < kGPT; ++pg) {
+              float acc = t == 0 ? 0.f : zacc[pg * 64];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) acc = fmaf(pooled[pg * 32 + 16 * vhalf + j], wv[j], acc);
+              zacc[pg * 64] = acc;
+            }
           }
         };
 
@@ -559,36 +594,38 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           if (t >= 1) finish_head(t - 1);
         }
         finish_head(3);
-        if (!last) {
+        if constexpr (!last) {
           fence_proxy_async_smem();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(x_ready);
         } else {
           // ---------------- heads (fp32) ----------------
-          float* zbuf = (float*)(smem + kSmZ);
-          float* logit = (float*)(smem + kSmLogit);
-          const int tid = threadIdx.x;  // 0..255
-          named_bar_sync(1, kEpiWarps * 32);  // pooled sums of both groups visible
-          if (tid < kGPT * 64) {
-            const int pg = tid / 64, u = tid % 64;
-            float acc = __ldg(p.w + C4Off::b_v1 + u);
-            for (int c = 0; c < 256; ++c) acc = fmaf(pooled[pg * 256 + c], __ldg(p.w + C4Off::W_v1 + c * 64 + u), acc);
-            zbuf[pg * 64 + u] = fmaxf(acc, 0.f);
-          } else if (tid < kGPT * 64 + kGPT * 7) {
-            const int k = tid - kGPT * 64, pg = k / 7, c = k % 7;
-            float acc = __ldg(p.w + C4Off::b_pi);
-            for (int f = 0; f < 256; ++f) acc = fmaf(pcol[(pg * 7 + c) * 256 + f], __ldg(p.w + C4Off::w_pi + f), acc);
-            logit[pg * 8 + c] = acc;
+          float* zpart = (float*)(smem + kSmZ);
+          float* lgpart = (float*)(smem + kSmLogit);
+          if (gt < kGPT * 32) {
+#pragma unroll
+            for (int c = 0; c < 7; ++c) {
+              float x = lgacc[c];
+#pragma unroll
+              for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+              if (lane == 0) lgpart[(g * kGPT + (gt >> 5)) * 8 + c] = x;
+            }
           }
-          named_bar_sync(1, kEpiWarps * 32);
+          named_bar_sync(1, kEpiWarps * 32);  // partial sums of both groups visible
           if (warp < kGPT) {
             const int pg = warp, pos = tile * kGPT + pg;
-            float vv = zbuf[pg * 64 + lane] * __ldg(p.w + C4Off::w_v2 + lane) +
-                       zbuf[pg * 64 + 32 + lane] * __ldg(p.w + C4Off::w_v2 + 32 + lane);
+            float z0 = __ldg(p.w + C4Off::b_v1 + lane), z1 = __ldg(p.w + C4Off::b_v1 + 32 + lane);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              z0 += zpart[(q * kGPT + pg) * 64 + lane];
+              z1 += zpart[(q * kGPT + pg) * 64 + 32 + lane];
+            }
+            float vv = fmaxf(z0, 0.f) * __ldg(p.w + C4Off::w_v2 + lane) + fmaxf(z1, 0.f) * __ldg(p.w + C4Off::w_v2 + 32 + lane);
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) vv += __shfl_xor_sync(0xffffffffu, vv, o);
-            const float lg = lane < 7 ? logit[pg * 8 + lane] : -INFINITY;
+            const float lg = lane < 7 ? __ldg(p.w + C4Off::b_pi) + lgpart[pg * 8 + lane] + lgpart[(kGPT + pg) * 8 + lane]
+                                      : -INFINITY;
             float mx = lg;
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -603,6 +640,11 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           }
           named_bar_sync(1, kEpiWarps * 32);  // head scratch (X tile) free for the next encode
         }
+        return true;
+      };
+      for (int l = 0; l < kLayers && ok; ++l) {
+        const bool cont = l < kLayers - 1 ? layer(l, std::false_type{}) : layer(l, std::true_type{});
+        if (!cont) break;
       }
     }
   }
