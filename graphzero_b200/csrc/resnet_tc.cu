@@ -81,6 +81,23 @@ constexpr size_t kPackedBytes = kPackedW + (size_t)kConvs * 2 * kC * 4;
 __host__ __device__ constexpr int tap_dy(int t) { return t == 0 ? 0 : ((t <= 4 ? t - 1 : t) / 3) - 1; }
 __host__ __device__ constexpr int tap_dx(int t) { return t == 0 ? 0 : ((t <= 4 ? t - 1 : t) % 3) - 1; }
 
+// Per-tap row masks (bit set = row skipped): rows whose tap leaves the board,
+// and the two padding rows.  Identical for every tile; built at compile time
+// so the MMA loop reads them as immediates.
+struct TapMasks {
+  uint32_t m[9][4];
+};
+__host__ __device__ constexpr TapMasks tap_masks() {
+  TapMasks k{};
+  for (int t = 0; t < 9; ++t)
+    for (int r = 0; r < kRows; ++r) {
+      const int li = r % kN, rr = li / 7 + tap_dy(t), cc = li % 7 + tap_dx(t);
+      const bool live = r < kGPT * kN && rr >= 0 && rr < 6 && cc >= 0 && cc < 7;
+      if (!live) k.m[t][r >> 5] |= 1u << (r & 31);
+    }
+  return k;
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -197,17 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
     __syncwarp();
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
-      // Per-tap row masks (bit set = row skipped): rows whose tap leaves the
-      // board, and the two padding rows.  Identical for every tile.
-      uint32_t mask[9][4];
-      for (int t = 0; t < 9; ++t) {
-        for (int w = 0; w < 4; ++w) mask[t][w] = 0;
-        for (int r = 0; r < kRows; ++r) {
-          const int li = r % kN, rr = li / 7 + tap_dy(t), cc = li % 7 + tap_dx(t);
-          const bool live = r < kGPT * kN && rr >= 0 && rr < 6 && cc >= 0 && cc < 7;
-          if (!live) mask[t][r >> 5] |= 1u << (r & 31);
-        }
-      }
+      constexpr TapMasks kMask = tap_masks();
       constexpr uint32_t idesc = idesc_f16(ResOp<OpT>::fmt, 128, 128);
       uint32_t q = 0, aph = 0;
       bool ok = true;
@@ -219,19 +226,28 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
           tc_fence_after();
           // input buffer: stem reads A1 (input planes), block conv1 reads A0, conv2 reads A1
           const uint32_t in = smem_u32(smem + ((cv == 0 || (cv & 1) == 0) ? kSmA1 : kSmA0));
-          const int nchunk = cv == 0 ? 1 : 2, ksteps = cv == 0 ? 1 : 4;
-          for (int t = 0; t < 9 && ok; ++t) {
-            const int shift = 7 * tap_dy(t) + tap_dx(t);
+          const int nchunk = cv == 0 ? 1 : 2;
+          // One thread issues every MMA, so its own instruction stream bounds
+          // the MMA rate: the taps are unrolled (masks stay in registers) and
+          // descriptors advance by adding (byte offset >> 4) to the start
+          // address field (shared addresses stay below 2^18: no carry).
+          const uint64_t in_desc = sw128_desc_shifted(in + kGuard * 128);
+          const uint64_t w_desc = sw128_desc(smem_u32(smem + kSmW));
+#pragma unroll
+          for (int t = 0; t < 9; ++t) {
+            const int shift = 7 * tap_dy(t) + tap_dx(t);  // rows; x 128 bytes
             for (int c = 0; c < nchunk && ok; ++c, ++q) {
               const int s = q % kWSlots;
               ok = mbar_wait(&full[s], (q / kWSlots) & 1, abort_flag, kWaitLimitNs);
               if (!ok) break;
               tc_fence_after();
-              const uint32_t ws = smem_u32(smem + kSmW + s * kWChunk);
-              const uint32_t a0 = in + c * kActChunk + (kGuard + shift) * 128;
-              for (int kk = 0; kk < ksteps; ++kk)
-                mma_f16_ss_masked(tmem, sw128_desc_shifted(a0 + kk * 32), sw128_desc(ws + kk * 32), idesc,
-                                  (t | c | kk) != 0, mask[t]);
+              const uint64_t wd = w_desc + (uint64_t)(s * (kWChunk >> 4));
+              const uint64_t ad = in_desc + (uint64_t)((c * kActChunk + shift * 128) >> 4);
+              mma_f16_ss_masked(tmem, ad, wd, idesc, (t | c) != 0, kMask.m[t]);
+              if (cv != 0) {
+#pragma unroll
+                for (int kk = 1; kk < 4; ++kk) mma_f16_ss_masked(tmem, ad + kk * 2, wd + kk * 2, idesc, 1, kMask.m[t]);
+              }
               mma_commit(&empty[s]);
             }
           }
