@@ -69,6 +69,7 @@ constexpr uint32_t kAlphaCol = 256;  // e buffers: 256 + (2 * group + buffer) * 
 // columns 0..31; read at the start of a layer, then re-zeroed by group 0.
 constexpr uint32_t kScoreCol = kAlphaCol + 64;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s per wait
+constexpr long long kWaitLimitCycles = 8000000000ll;  // 4 s at 2 GHz (longer at lower clocks; always bounded)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Shared memory map (bytes).
@@ -321,7 +322,9 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           // group's heads in order), eight per layer; polling never blocks
           // on one group's barrier
           int next_t[2] = {0, 0};
-          uint64_t t0 = global_timer_ns();
+          // (the idle limit counts SM cycles: %globaltimer is slow to read
+          // and this loop is on the critical path of every gather)
+          long long c0 = clock64();
           while (ok && (next_t[0] < 4 || next_t[1] < 4)) {
             bool issued = false;
 #pragma unroll
@@ -343,8 +346,8 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
               issued = true;
             }
             if (issued) {
-              t0 = global_timer_ns();
-            } else if (*abort_flag || global_timer_ns() - t0 > kWaitLimitNs) {
+              c0 = clock64();
+            } else if (*abort_flag || clock64() - c0 > kWaitLimitCycles) {
               *abort_flag = 1;
               ok = false;
             }
