@@ -55,9 +55,10 @@ constexpr int kGPT = 3;             // positions per tile
 constexpr int kRows = 128;          // MMA M (node rows per tile)
 constexpr int kLayers = 6;
 constexpr int kEpiWarps = 8;        // two warpgroups: heads 0-3 and 4-7
-constexpr int kThreads = (kEpiWarps + 2) * 32;
+constexpr int kThreads = (kEpiWarps + 3) * 32;
 constexpr int kProducerWarp = kEpiWarps;
-constexpr int kMmaWarp = kEpiWarps + 1;
+constexpr int kMmaWarp = kEpiWarps + 1;     // projection MMAs + group 0's gathers
+constexpr int kGatherWarp = kEpiWarps + 2;  // group 1's gathers (a second issuing thread)
 constexpr int kWRows = 256 + 32;    // projection rows + score rows (16 high parts, 16 remainders)
 constexpr int kWChunk = kWRows * 128;  // 64 K x 2 B per row
 constexpr int kWScoreOff = 256 * 128;  // byte offset of the score rows in a chunk
@@ -69,7 +70,6 @@ constexpr uint32_t kAlphaCol = 256;  // e buffers: 256 + (2 * group + buffer) * 
 // columns 0..31; read at the start of a layer, then re-zeroed by group 0.
 constexpr uint32_t kScoreCol = kAlphaCol + 64;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s per wait
-constexpr long long kWaitLimitCycles = 8000000000ll;  // 4 s at 2 GHz (longer at lower clocks; always bounded)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Shared memory map (bytes).
@@ -82,7 +82,7 @@ constexpr int kSmTsc = kSmStage + 2 * 128 * kStageStride;  // t scores: [group][
 constexpr int kSmVec = kSmTsc + 2 * 129 * 16;           // per layer bias[256]; x2 (layer parity)
 constexpr int kVecFloats = 256;
 constexpr int kSmBar = kSmVec + 2 * kVecFloats * 4;
-constexpr int kNumBars = 2 * kWSlots + 1 + 1 + 4 + 4 + 1;  // full, empty, acc_full, x_ready, req[2][2], done2[2][2], drain
+constexpr int kNumBars = 2 * kWSlots + 1 + 1 + 4 + 4 + 2;  // full, empty, acc_full, x_ready, req[2][2], done2[2][2], drain[2]
 constexpr int kSmMisc = kSmBar + kNumBars * 8;
 constexpr int kSmemBytes = kSmMisc + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -193,6 +193,30 @@ __device__ __forceinline__ float2 elu2(float2 y) {
 __device__ __forceinline__ int window_start(int q) { return q == 0 ? 0 : q == 3 ? 80 : 32 * q - 8; }
 
 
+// One group's four gathers of a layer, in head order: wait for head t's
+// request (e buffer and Wh^h staged), issue its eight K = 16 steps (8 columns
+// of e, two 8-row core-matrix groups of Wh), commit to done2.  Returns false
+// after an abort or a timed-out wait.
+__device__ __forceinline__ bool serve_gathers(int g, uint32_t tmem, uint64_t b2desc0, uint64_t* req, uint64_t* done2,
+                                              uint32_t (&rph)[2], volatile int* abort_flag) {
+  constexpr uint32_t idesc2 = idesc_f16(0 /* fp16 */, 128, 32, 1 /* B N-contiguous */);
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const int b = t & 1, ab = 2 * g + b;
+    if (!mbar_wait(&req[ab], rph[b] & 1, abort_flag, kWaitLimitNs)) return false;
+    ++rph[b];
+    tc_fence_after();
+    const uint32_t d = tmem + (uint32_t)(32 * (4 * g + t));
+    const uint32_t a_col = tmem + kAlphaCol + (uint32_t)(ab * 64);
+    const uint64_t bd = b2desc0 + (uint64_t)(ab * (8192 >> 4));
+    mma_f16_ts(d, a_col, bd, idesc2, 0);
+#pragma unroll
+    for (int kk = 1; kk < 8; ++kk) mma_f16_ts(d, a_col + kk * 8, bd + kk * (1024 >> 4), idesc2, 1);
+    mma_commit(&done2[ab]);
+  }
+  return true;
+}
+
 struct TcParams {
   const uint8_t* packed;  // kChunksPerTile chunks in consumption order
   const float* w;         // fp32 blob (biases, heads)
@@ -224,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
   // phase ahead of its consumer.
   uint64_t* req = acc_full + 2;     // [2 groups][2 buffers]
   uint64_t* done2 = acc_full + 6;   // [2 groups][2 buffers]
-  uint64_t* drain = acc_full + 10;
+  uint64_t* drain = acc_full + 10;  // [issuing thread]
   uint32_t* tmem_slot = (uint32_t*)(smem + kSmMisc);
   volatile int* abort_flag = (volatile int*)(smem + kSmMisc + 4);
 
@@ -246,7 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
       mbar_init(&req[i], 4);
       mbar_init(&done2[i], 1);
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -286,11 +311,10 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
     if (lane == 0) {
       constexpr uint32_t idesc1 = idesc_f16(OpType<OpT>::fmt, 128, 256);
       constexpr uint32_t idesc_s = idesc_f16(OpType<OpT>::fmt, 128, 32);
-      constexpr uint32_t idesc2 = idesc_f16(0 /* fp16 */, 128, 32, 1 /* B N-contiguous */);
       const uint64_t xdesc = sw128_desc(smem_u32(sX));
       const uint64_t wdesc0 = sw128_desc(smem_u32(sW));
       const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
-      uint32_t q = 0, xph = 0, rph[4] = {0, 0, 0, 0};
+      uint32_t q = 0, xph = 0, rph[2] = {0, 0};
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         for (int l = 0; l < kLayers && ok; ++l) {
@@ -318,44 +342,25 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           }
           if (!ok) break;
           mma_commit(acc_full);
-          // gathers: serve whichever group's next head is ready (each
-          // group's heads in order), eight per layer; polling never blocks
-          // on one group's barrier
-          int next_t[2] = {0, 0};
-          // (the idle limit counts SM cycles: %globaltimer is slow to read
-          // and this loop is on the critical path of every gather)
-          long long c0 = clock64();
-          while (ok && (next_t[0] < 4 || next_t[1] < 4)) {
-            bool issued = false;
-#pragma unroll
-            for (int g = 0; g < 2; ++g) {
-              if (next_t[g] >= 4) continue;
-              const int t = next_t[g], ab = 2 * g + (t & 1);
-              if (!mbar_test_wait(&req[ab], rph[ab] & 1)) continue;
-              ++rph[ab];
-              ++next_t[g];
-              tc_fence_after();
-              const uint32_t d = tmem + (uint32_t)(32 * (4 * g + t));
-              const uint32_t a_col = tmem + kAlphaCol + (uint32_t)(ab * 64);
-              const uint64_t bd = b2desc0 + (uint64_t)(ab * (8192 >> 4));
-              mma_f16_ts(d, a_col, bd, idesc2, 0);
-#pragma unroll
-              for (int kk = 1; kk < 8; ++kk)  // K = 16 nodes: 8 columns of e, two 8-row core-matrix groups of Wh
-                mma_f16_ts(d, a_col + kk * 8, bd + kk * (1024 >> 4), idesc2, 1);
-              mma_commit(&done2[ab]);
-              issued = true;
-            }
-            if (issued) {
-              c0 = clock64();
-            } else if (*abort_flag || clock64() - c0 > kWaitLimitCycles) {
-              *abort_flag = 1;
-              ok = false;
-            }
-          }
+          ok = serve_gathers(0, tmem, b2desc0, req, done2, rph, abort_flag);
         }
       }
-      mma_commit(drain);
-      mbar_wait(drain, 0, abort_flag, kWaitLimitNs);
+      mma_commit(&drain[0]);
+      mbar_wait(&drain[0], 0, abort_flag, kWaitLimitNs);
+    }
+    __syncwarp();
+  } else if (warp == kGatherWarp) {
+    // ---------------- group 1's gathers ----------------
+    // A second issuing thread, so the two groups' gather chains overlap in
+    // the tensor pipe (each chain is bound by one thread's issue rate).
+    if (lane == 0) {
+      const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
+      uint32_t rph[2] = {0, 0};
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x)
+        for (int l = 0; l < kLayers && ok; ++l) ok = serve_gathers(1, tmem, b2desc0, req, done2, rph, abort_flag);
+      mma_commit(&drain[1]);
+      mbar_wait(&drain[1], 0, abort_flag, kWaitLimitNs);
     }
     __syncwarp();
   } else {
