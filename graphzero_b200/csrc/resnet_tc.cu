@@ -47,8 +47,15 @@ constexpr int kThreads = (kEpiWarps + 2) * 32;
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
 constexpr int kWChunk = 16384;              // 128 co rows x 64 ci x 2 B
-constexpr int kWSlots = 4;
 constexpr int kChunksPerTile = 9 + (kConvs - 1) * 18;
+// The ring moves one tap per copy: both 64-channel chunks of a block conv's
+// tap (adjacent in the packed weights, 32 KB), or the stem's one chunk.  A
+// 32 KB bulk copy moves about 1.7x the bytes per cycle of a 16 KB one from
+// L2 (measured on B200 with every SM streaming), and the weights are
+// re-streamed for every tile.
+constexpr int kWSlot = 2 * kWChunk;
+constexpr int kWSlots = 4;
+constexpr int kUnitsPerTile = 9 * kConvs;
 constexpr uint32_t kTmemCols = 128;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
 constexpr int kGuard = 8;                   // guard rows before and after
@@ -60,7 +67,7 @@ constexpr int kActBytes = 2 * kActChunk;    // 128 channels
 constexpr int kSmA0 = 0;                          // block input / residual
 constexpr int kSmA1 = kSmA0 + kActBytes;          // intermediate (and the stem input)
 constexpr int kSmW = kSmA1 + kActBytes;           // weight ring
-constexpr int kSmBn = kSmW + kWSlots * kWChunk;   // [2 parity][scale 128, shift 128]
+constexpr int kSmBn = kSmW + kWSlots * kWSlot;    // [2 parity][scale 128, shift 128]
 constexpr int kSmHead = kSmBn + 2 * 2 * kC * 4;   // [2 halves][128 rows][3] partial head dots
 constexpr int kSmFeat = kSmHead + 2 * kRows * 3 * 4;  // [3 pos][84 policy + 42 value] features
 constexpr int kSmHid = kSmFeat + kGPT * 128 * 4;  // [3][128] value hidden
@@ -201,12 +208,15 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
       uint32_t q = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x)
-        for (int c = 0; c < kChunksPerTile && ok; ++c, ++q) {
+        for (int u = 0; u < kUnitsPerTile && ok; ++u, ++q) {
           const int s = q % kWSlots;
+          // unit u: stem tap u (one chunk), else conv 1 + (u - 9) / 9, tap (u - 9) % 9 (two chunks)
+          const int c = u < 9 ? u : 9 + 2 * (u - 9);
+          const uint32_t bytes = u < 9 ? kWChunk : kWSlot;
           ok = mbar_wait(&empty[s], ((q / kWSlots) & 1) ^ 1, abort_flag, kWaitLimitNs);
           if (!ok) break;
-          mbar_arrive_expect_tx(&full[s], kWChunk);
-          bulk_g2s(smem + kSmW + s * kWChunk, p.packed + (size_t)c * kWChunk, kWChunk, &full[s]);
+          mbar_arrive_expect_tx(&full[s], bytes);
+          bulk_g2s(smem + kSmW + s * kWSlot, p.packed + (size_t)c * kWChunk, bytes, &full[s]);
         }
       for (uint32_t k = (q > kWSlots ? q - kWSlots : 0); k < q; ++k)
         mbar_wait(&full[k % kWSlots], (k / kWSlots) & 1, abort_flag, kWaitLimitNs);
@@ -236,20 +246,22 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
 #pragma unroll
           for (int t = 0; t < 9; ++t) {
             const int shift = 7 * tap_dy(t) + tap_dx(t);  // rows; x 128 bytes
-            for (int c = 0; c < nchunk && ok; ++c, ++q) {
-              const int s = q % kWSlots;
-              ok = mbar_wait(&full[s], (q / kWSlots) & 1, abort_flag, kWaitLimitNs);
-              if (!ok) break;
-              tc_fence_after();
-              const uint64_t wd = w_desc + (uint64_t)(s * (kWChunk >> 4));
+            if (!ok) break;
+            const int s = q % kWSlots;
+            ok = mbar_wait(&full[s], (q / kWSlots) & 1, abort_flag, kWaitLimitNs);
+            ++q;
+            if (!ok) break;
+            tc_fence_after();
+            for (int c = 0; c < nchunk; ++c) {  // 64-channel K chunks of this tap's slot
+              const uint64_t wd = w_desc + (uint64_t)((s * kWSlot + c * kWChunk) >> 4);
               const uint64_t ad = in_desc + (uint64_t)((c * kActChunk + shift * 128) >> 4);
               mma_f16_ss_masked(tmem, ad, wd, idesc, (t | c) != 0, kMask.m[t]);
               if (cv != 0) {
 #pragma unroll
                 for (int kk = 1; kk < 4; ++kk) mma_f16_ss_masked(tmem, ad + kk * 2, wd + kk * 2, idesc, 1, kMask.m[t]);
               }
-              mma_commit(&empty[s]);
             }
+            mma_commit(&empty[s]);
           }
           if (ok) mma_commit(acc_full);
         }
