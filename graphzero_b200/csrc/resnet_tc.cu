@@ -20,6 +20,11 @@
 // head convolutions, and the heads (FC 84->7 softmax, FC 42->128 ReLU ->1
 // tanh) finish in fp32.
 //
+// Two tiles are in flight per CTA (slots A and B, each with its own
+// activations and tensor-memory accumulator): the MMAs of one slot's
+// convolution run while the epilogue warps finish the other slot's, so the
+// tensor pipe does not idle during the epilogues.
+//
 // Reference: networks/resnet/resnet.cu:506-667 (forward_resnet; the
 // reference's residual "add" overwrites, resnet.cu:588-591, and its BN runs
 // in training mode; here BN is in inference form and the add is real).
@@ -54,26 +59,26 @@ constexpr int kChunksPerTile = 9 + (kConvs - 1) * 18;
 // L2 (measured on B200 with every SM streaming), and the weights are
 // re-streamed for every tile.
 constexpr int kWSlot = 2 * kWChunk;
-constexpr int kWSlots = 4;
-constexpr int kUnitsPerTile = 9 * kConvs;
-constexpr uint32_t kTmemCols = 128;
+constexpr int kWSlots = 2;
+constexpr uint32_t kTmemCols = 256;         // slot s accumulates in columns [128 s, 128 s + 128)
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
 constexpr int kGuard = 8;                   // guard rows before and after
 constexpr int kChunkRows = kRows + 2 * kGuard;
 constexpr int kActChunk = kChunkRows * 128; // one 64-channel K chunk, 18 KB
 constexpr int kActBytes = 2 * kActChunk;    // 128 channels
 
-// Shared memory map.
+// Shared memory map.  Slot s's activations start at s * kSlotBytes.
 constexpr int kSmA0 = 0;                          // block input / residual
 constexpr int kSmA1 = kSmA0 + kActBytes;          // intermediate (and the stem input)
-constexpr int kSmW = kSmA1 + kActBytes;           // weight ring
+constexpr int kSlotBytes = 2 * kActBytes;
+constexpr int kSmW = 2 * kSlotBytes;              // weight ring
 constexpr int kSmBn = kSmW + kWSlots * kWSlot;    // [2 parity][scale 128, shift 128]
 constexpr int kSmHead = kSmBn + 2 * 2 * kC * 4;   // [2 halves][128 rows][3] partial head dots
 constexpr int kSmFeat = kSmHead + 2 * kRows * 3 * 4;  // [3 pos][84 policy + 42 value] features
 constexpr int kSmHid = kSmFeat + kGPT * 128 * 4;  // [3][128] value hidden
 constexpr int kSmLogit = kSmHid + kGPT * 128 * 4; // [3][8]
 constexpr int kSmBar = kSmLogit + kGPT * 8 * 4;
-constexpr int kNumBars = 2 * kWSlots + 3;         // full, empty, acc_full, act_ready, drain
+constexpr int kNumBars = 2 * kWSlots + 5;         // full, empty, acc_full[2], act_ready[2], drain
 constexpr int kSmMisc = kSmBar + kNumBars * 8;
 constexpr int kSmemBytes = kSmMisc + 16;
 static_assert(kSmA1 % 1024 == 0 && kSmW % 1024 == 0 && kActChunk % 1024 == 0, "swizzle alignment");
@@ -169,17 +174,17 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
   uint64_t* bars = (uint64_t*)(smem + kSmBar);
   uint64_t* full = bars;
   uint64_t* empty = bars + kWSlots;
-  uint64_t* acc_full = bars + 2 * kWSlots;
-  uint64_t* act_ready = acc_full + 1;
-  uint64_t* drain = acc_full + 2;
+  uint64_t* acc_full = bars + 2 * kWSlots;  // [slot]
+  uint64_t* act_ready = acc_full + 2;       // [slot]
+  uint64_t* drain = acc_full + 4;
   uint32_t* tmem_slot = (uint32_t*)(smem + kSmMisc);
   volatile int* abort_flag = (volatile int*)(smem + kSmMisc + 4);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const ResLayout RL = res_layout();
 
-  // Guard rows of both activation buffers hold finite values (zeros).
-  for (int i = threadIdx.x; i < 2 * kActBytes / 16; i += blockDim.x) {
+  // Guard rows of the activation buffers hold finite values (zeros).
+  for (int i = threadIdx.x; i < 4 * kActBytes / 16; i += blockDim.x) {
     const int byte = i * 16, row = (byte % kActChunk) / 128;
     if (row < kGuard || row >= kGuard + kRows) *(uint4*)(smem + byte) = make_uint4(0, 0, 0, 0);
   }
@@ -188,8 +193,10 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(act_ready, kEpiWarps);
+    for (int sl = 0; sl < 2; ++sl) {
+      mbar_init(&acc_full[sl], 1);
+      mbar_init(&act_ready[sl], kEpiWarps);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -207,12 +214,14 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
     if (lane == 0) {
       uint32_t q = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x)
-        for (int u = 0; u < kUnitsPerTile && ok; ++u, ++q) {
+      // consumption order: per tile pair, per conv, slot A's nine taps then slot B's
+      for (int ta = blockIdx.x; ta < p.num_tiles && ok; ta += 2 * gridDim.x)
+        for (int u = 0; u < 18 * kConvs && ok; ++u, ++q) {
           const int s = q % kWSlots;
-          // unit u: stem tap u (one chunk), else conv 1 + (u - 9) / 9, tap (u - 9) % 9 (two chunks)
-          const int c = u < 9 ? u : 9 + 2 * (u - 9);
-          const uint32_t bytes = u < 9 ? kWChunk : kWSlot;
+          const int cv = u / 18, t = u % 9;
+          // stem tap: one chunk; block conv tap: its two adjacent chunks
+          const int c = cv == 0 ? t : 9 + (cv - 1) * 18 + 2 * t;
+          const uint32_t bytes = cv == 0 ? kWChunk : kWSlot;
           ok = mbar_wait(&empty[s], ((q / kWSlots) & 1) ^ 1, abort_flag, kWaitLimitNs);
           if (!ok) break;
           mbar_arrive_expect_tx(&full[s], bytes);
@@ -226,16 +235,18 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
     if (lane == 0) {
       constexpr TapMasks kMask = tap_masks();
       constexpr uint32_t idesc = idesc_f16(ResOp<OpT>::fmt, 128, 128);
-      uint32_t q = 0, aph = 0;
+      uint32_t q = 0, aph[2] = {0, 0};
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        for (int cv = 0; cv < kConvs && ok; ++cv) {
-          ok = mbar_wait(act_ready, aph & 1, abort_flag, kWaitLimitNs);
-          ++aph;
+      for (int ta = blockIdx.x; ta < p.num_tiles && ok; ta += 2 * gridDim.x) {
+        for (int u = 0; u < 2 * kConvs && ok; ++u) {
+          const int cv = u >> 1, sl = u & 1;
+          ok = mbar_wait(&act_ready[sl], aph[sl] & 1, abort_flag, kWaitLimitNs);
+          ++aph[sl];
           if (!ok) break;
           tc_fence_after();
+          const uint32_t dt = tmem + (uint32_t)(128 * sl);
           // input buffer: stem reads A1 (input planes), block conv1 reads A0, conv2 reads A1
-          const uint32_t in = smem_u32(smem + ((cv == 0 || (cv & 1) == 0) ? kSmA1 : kSmA0));
+          const uint32_t in = smem_u32(smem + sl * kSlotBytes + ((cv == 0 || (cv & 1) == 0) ? kSmA1 : kSmA0));
           const int nchunk = cv == 0 ? 1 : 2;
           // One thread issues every MMA, so its own instruction stream bounds
           // the MMA rate: the taps are unrolled (masks stay in registers) and
@@ -255,15 +266,15 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
             for (int c = 0; c < nchunk; ++c) {  // 64-channel K chunks of this tap's slot
               const uint64_t wd = w_desc + (uint64_t)((s * kWSlot + c * kWChunk) >> 4);
               const uint64_t ad = in_desc + (uint64_t)((c * kActChunk + shift * 128) >> 4);
-              mma_f16_ss_masked(tmem, ad, wd, idesc, (t | c) != 0, kMask.m[t]);
+              mma_f16_ss_masked(dt, ad, wd, idesc, (t | c) != 0, kMask.m[t]);
               if (cv != 0) {
 #pragma unroll
-                for (int kk = 1; kk < 4; ++kk) mma_f16_ss_masked(tmem, ad + kk * 2, wd + kk * 2, idesc, 1, kMask.m[t]);
+                for (int kk = 1; kk < 4; ++kk) mma_f16_ss_masked(dt, ad + kk * 2, wd + kk * 2, idesc, 1, kMask.m[t]);
               }
             }
             mma_commit(&empty[s]);
           }
-          if (ok) mma_commit(acc_full);
+          if (ok) mma_commit(&acc_full[sl]);
         }
       }
       mma_commit(drain);
@@ -276,11 +287,14 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
     const int r = 32 * qd + lane;  // tile row of this thread
     const uint32_t tlane = tmem + ((uint32_t)(32 * qd) << 16);
     const float* bnp = (const float*)(p.packed + kPackedW);
-    uint32_t accph = 0;
+    uint32_t accph[2] = {0, 0};
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-      // -- stem input: 3 planes (own, opponent, first-player-to-move) in A1 chunk 0 --
-      {
+    for (int ta = blockIdx.x; ta < p.num_tiles && ok; ta += 2 * gridDim.x) {
+      // slot sl holds tile ta + sl * gridDim.x (past the last tile: zero
+      // inputs, outputs never written since its positions are >= n)
+      for (int sl = 0; sl < 2; ++sl) {
+        const int tile = ta + sl * (int)gridDim.x;
+        // -- stem input: 3 planes (own, opponent, first-player-to-move) in A1 chunk 0 --
         const int g = r / kN, li = r % kN, pos = tile * kGPT + g;
         float f0 = 0.f, f1 = 0.f, f2 = 0.f;
         if (g < kGPT && pos < p.n) {
@@ -290,34 +304,38 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
           f2 = sd == 1 ? 1.f : 0.f;
         }
         if (hf == 0) {
-          uint8_t* row = smem + kSmA1 + (kGuard + r) * 128;
+          uint8_t* row = smem + sl * kSlotBytes + kSmA1 + (kGuard + r) * 128;
           const int rs = (kGuard + r) & 7;
           *(uint4*)(row + ((0 ^ rs) << 4)) = make_uint4(ResOp<OpT>::pack(f0, f1), ResOp<OpT>::pack(f2, 0.f), 0u, 0u);
           *(uint4*)(row + ((1 ^ rs) << 4)) = make_uint4(0u, 0u, 0u, 0u);
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&act_ready[sl]);
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(act_ready);
 
-      for (int cv = 0; cv < kConvs && ok; ++cv) {
-        // folded BN of this conv into shared memory (by parity)
+      for (int u = 0; u < 2 * kConvs && ok; ++u) {
+        const int cv = u >> 1, sl = u & 1, tile = ta + sl * (int)gridDim.x;
+        // folded BN of this conv into shared memory (by parity; both slots use it)
         float* bn = (float*)(smem + kSmBn) + (cv & 1) * 2 * kC;
-        for (int t = threadIdx.x; t < 2 * kC; t += kEpiWarps * 32) bn[t] = __ldg(bnp + (size_t)cv * 2 * kC + t);
-        ok = epilogue_all(mbar_wait(acc_full, accph & 1, abort_flag, kWaitLimitNs));
-        ++accph;
+        if (sl == 0)
+          for (int t = threadIdx.x; t < 2 * kC; t += kEpiWarps * 32) bn[t] = __ldg(bnp + (size_t)cv * 2 * kC + t);
+        ok = epilogue_all(mbar_wait(&acc_full[sl], accph[sl] & 1, abort_flag, kWaitLimitNs));
+        ++accph[sl];
         if (!ok) break;
         tc_fence_after();
+        uint8_t* const sbase = smem + sl * kSlotBytes;
+        const uint32_t tslot = tlane + (uint32_t)(128 * sl);
         const bool second = cv > 0 && (cv & 1) == 0;  // second conv of a block: residual add
         const bool last = cv == kConvs - 1;
         // output: stem and conv2 -> A0, conv1 -> A1
-        uint8_t* outb = smem + ((cv == 0 || second) ? kSmA0 : kSmA1);
+        uint8_t* outb = sbase + ((cv == 0 || second) ? kSmA0 : kSmA1);
         float hp0 = 0.f, hp1 = 0.f, hv = 0.f;  // partial 1x1 head convolutions (last conv)
 #pragma unroll 1
         for (int cb = 0; cb < 2; ++cb) {  // 32-channel blocks of this half
           const int c0 = 64 * hf + 32 * cb;
           float acc[32];
-          tmem_ld_x32(tlane + (uint32_t)c0, acc);
+          tmem_ld_x32(tslot + (uint32_t)c0, acc);
           tmem_ld_wait();
           const float4* sc4 = (const float4*)(bn + c0);
           const float4* sh4 = (const float4*)(bn + kC + c0);
@@ -333,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
           // row r, channels c0..c0+31: K chunk c0/64, 16-byte units (c0%64)/8 + u
           const int rs = (kGuard + r) & 7;
           uint8_t* orow = outb + (c0 >> 6) * kActChunk + (kGuard + r) * 128;
-          const uint8_t* rrow = smem + kSmA0 + (c0 >> 6) * kActChunk + (kGuard + r) * 128;
+          const uint8_t* rrow = sbase + kSmA0 + (c0 >> 6) * kActChunk + (kGuard + r) * 128;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int unit = ((((c0 & 63) >> 3) + u) ^ rs) << 4;
@@ -367,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
           fence_proxy_async_smem();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(act_ready);
+          if (lane == 0) mbar_arrive(&act_ready[sl]);
           continue;
         }
         // ---------------- heads (fp32) ----------------
