@@ -65,6 +65,8 @@ _SIGS = {
     "gz_weight_count": (C.c_size_t, [C.c_int, C.c_int]),
     "gz_synth_weights": (C.c_int, [C.c_int, C.c_int, C.c_uint64, C.c_float, C.c_int, _f32p, C.c_size_t]),
     "gz_synth_positions": (C.c_int, [C.c_int, C.c_uint64, C.c_uint64, C.c_int, _i8p, _i8p]),
+    "gz_chess_legal_count": (C.c_int, [_i8p, C.c_int, C.POINTER(C.c_int)]),
+    "gz_chess_perft": (C.c_int, [_i8p, C.c_int, C.c_int, C.POINTER(C.c_uint64)]),
     "gz_net_create": (C.c_int, [C.POINTER(NetConfig), C.c_int, C.POINTER(_vp)]),
     "gz_net_destroy": (C.c_int, [_vp]),
     "gz_net_weight_count": (C.c_size_t, [_vp]),
@@ -228,6 +230,20 @@ def synth_weights(game: int, kind: int = GAT, seed: int = 0x6A5A, bias_scale: fl
     w = np.empty(n, np.float32)
     _check(_lib.gz_synth_weights(game, kind, seed, bias_scale, int(bf16_exact), _ptr(w, C.c_float), n))
     return w
+
+
+def chess_legal_count(board: np.ndarray, side: int) -> int:
+    b = np.ascontiguousarray(board, np.int8)
+    r = C.c_int()
+    _check(_lib.gz_chess_legal_count(_ptr(b, C.c_int8), side, C.byref(r)))
+    return r.value
+
+
+def chess_perft(board: np.ndarray, side: int, depth: int) -> int:
+    b = np.ascontiguousarray(board, np.int8)
+    r = C.c_uint64()
+    _check(_lib.gz_chess_perft(_ptr(b, C.c_int8), side, depth, C.byref(r)))
+    return r.value
 
 
 def synth_positions(game: int, n: int, seed: int = 0x6A5A, first: int = 0) -> tuple[np.ndarray, np.ndarray]:

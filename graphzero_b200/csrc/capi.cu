@@ -17,6 +17,7 @@
 #include "gz_mcts.h"
 #include "gz_sm100.h"
 #include "gz_synth.h"
+#include "gz_chess.h"
 
 using namespace gz;
 
@@ -252,9 +253,28 @@ gz_status gz_synth_weights(int game, int kind, uint64_t seed, float bias_scale, 
 
 gz_status gz_synth_positions(int game, uint64_t seed, uint64_t first, int n, int8_t* boards, int8_t* side) {
   if (!valid_game(game) || n < 0 || (n > 0 && (!boards || !side))) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
-  if (game == kChess) return fail(GZ_ERR_UNSUPPORTED, "chess positions are not generated by this build");
   GameShape s = game_shape(game);
-  for (int i = 0; i < n; ++i) side[i] = (int8_t)make_position(game, seed, first + (uint64_t)i, boards + (size_t)i * s.board_bytes);
+  for (int i = 0; i < n; ++i)
+    side[i] = (int8_t)(game == kChess ? chess::make_position(seed, first + (uint64_t)i, boards + (size_t)i * s.board_bytes)
+                                      : make_position(game, seed, first + (uint64_t)i, boards + (size_t)i * s.board_bytes));
+  return GZ_OK;
+}
+
+gz_status gz_chess_legal_count(const int8_t* board, int side, int* count) {
+  if (!board || !count || (side != 1 && side != -1)) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  chess::Pos p;
+  chess::from_record(board, side, p);
+  chess::Move ms[256];
+  *count = chess::legal_moves(p, ms);
+  return GZ_OK;
+}
+
+gz_status gz_chess_perft(const int8_t* board, int side, int depth, uint64_t* nodes) {
+  if (!board || !nodes || (side != 1 && side != -1) || depth < 0 || depth > 6)
+    return fail(GZ_ERR_INVALID_ARG, "bad arguments (depth 0..6)");
+  chess::Pos p;
+  chess::from_record(board, side, p);
+  *nodes = chess::perft(p, depth);
   return GZ_OK;
 }
 

@@ -107,8 +107,20 @@ size_t gz_weight_count(int game, int kind);
 gz_status gz_synth_weights(int game, int kind, uint64_t seed, float bias_scale, int bf16_exact, float* out,
                            size_t n_floats);
 /* n random legal non-terminal positions (uniform random playouts), indices
- * first..first+n-1 of the seeded stream.  boards [n][board_bytes], side [n]. */
+ * first..first+n-1 of the seeded stream.  boards [n][board_bytes], side [n].
+ * Chess: k ~ U{0..120} random legal plies from the initial position, 66-byte
+ * records (64 squares, castling rights, en-passant square). */
 gz_status gz_synth_positions(int game, uint64_t seed, uint64_t first, int n, int8_t* boards, int8_t* side);
+
+/* ---- chess rules (host) ---------------------------------------------------
+ * Replace the move generation of games/chess/chess.cu:677-1071 (which does
+ * not compile) for the position generator: a legal generator with castling,
+ * en passant and promotions over the 66-byte record and side (+1 white). */
+/* Number of legal moves of `side`. */
+gz_status gz_chess_legal_count(const int8_t* board, int side, int* count);
+/* Leaf count of the legal move tree to `depth` (0..6): the rules'
+ * known-answer check against published perft counts. */
+gz_status gz_chess_perft(const int8_t* board, int side, int depth, uint64_t* nodes);
 
 /* ---- network: INeuralNet replacement ------------------------------------ */
 /* create_gat_model / create_resnet_model / create_neural_net
