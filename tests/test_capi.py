@@ -56,9 +56,13 @@ def test_invalid_arguments_are_reported():
     assert e.value.status == gz.ERR_INVALID_ARG and "bad game" in str(e.value)
     with pytest.raises(gz.GZError):
         gz.synth_weights(gz.TICTACTOE, gz.RESNET)
+    b, s = gz.synth_positions(gz.CHESS, 2)
     with pytest.raises(gz.GZError) as e:
-        gz.synth_positions(gz.CHESS, 4)
-    assert e.value.status == gz.ERR_UNSUPPORTED
+        gz.chess_perft(b[0], int(s[0]), 7)
+    assert e.value.status == gz.ERR_INVALID_ARG
+    with pytest.raises(gz.GZError) as e:
+        gz.chess_legal_count(b[0], 0)
+    assert e.value.status == gz.ERR_INVALID_ARG
     lib = C.CDLL(str(gz.LIB_PATH))
     assert gz._lib.gz_net_predict_batch(None, None, None, 4, None, None, None) == gz.ERR_INVALID_ARG
     assert gz._lib.gz_mcts_select(None, None) == gz.ERR_INVALID_ARG
