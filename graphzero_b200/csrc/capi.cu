@@ -9,6 +9,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "../../include/graphzero_b200.h"
@@ -254,9 +255,26 @@ gz_status gz_synth_weights(int game, int kind, uint64_t seed, float bias_scale, 
 gz_status gz_synth_positions(int game, uint64_t seed, uint64_t first, int n, int8_t* boards, int8_t* side) {
   if (!valid_game(game) || n < 0 || (n > 0 && (!boards || !side))) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
   GameShape s = game_shape(game);
-  for (int i = 0; i < n; ++i)
-    side[i] = (int8_t)(game == kChess ? chess::make_position(seed, first + (uint64_t)i, boards + (size_t)i * s.board_bytes)
-                                      : make_position(game, seed, first + (uint64_t)i, boards + (size_t)i * s.board_bytes));
+  if (game != kChess) {
+    for (int i = 0; i < n; ++i)
+      side[i] = (int8_t)make_position(game, seed, first + (uint64_t)i, boards + (size_t)i * s.board_bytes);
+    return GZ_OK;
+  }
+  // Chess playouts cost ~0.3 ms each: positions are independent (each is a
+  // function of its stream index), so host threads split the range.
+  auto run = [&](int lo, int hi) {
+    for (int i = lo; i < hi; ++i)
+      side[i] = (int8_t)chess::make_position(seed, first + (uint64_t)i, boards + (size_t)i * s.board_bytes);
+  };
+  int threads = (int)std::thread::hardware_concurrency();
+  threads = threads < 1 ? 1 : threads > 64 ? 64 : threads;
+  if (n < 64 || threads == 1) {
+    run(0, n);
+    return GZ_OK;
+  }
+  std::vector<std::thread> pool;
+  for (int t = 0; t < threads; ++t) pool.emplace_back(run, (int)((int64_t)n * t / threads), (int)((int64_t)n * (t + 1) / threads));
+  for (auto& th : pool) th.join();
   return GZ_OK;
 }
 

@@ -701,9 +701,12 @@ __global__ void pack_c4_kernel(const float* __restrict__ w, uint8_t* __restrict_
 
 }  // namespace
 
-size_t gat_tc_packed_bytes(int game) { return game == kConnect4 ? (size_t)kChunksPerTile * kWChunk : 0; }
+size_t gat_tc_packed_bytes(int game) {
+  return game == kConnect4 ? (size_t)kChunksPerTile * kWChunk : game == kChess ? chess_tc_packed_bytes() : 0;
+}
 
 cudaError_t launch_gat_tc_pack(int game, int fp16, const float* d_weights, void* d_packed, cudaStream_t stream) {
+  if (game == kChess) return launch_chess_tc_pack(fp16, d_weights, d_packed, stream);
   if (game != kConnect4) return cudaErrorNotSupported;
   if (fp16) pack_c4_kernel<__half><<<kChunksPerTile, 256, 0, stream>>>(d_weights, (uint8_t*)d_packed);
   else pack_c4_kernel<__nv_bfloat16><<<kChunksPerTile, 256, 0, stream>>>(d_weights, (uint8_t*)d_packed);
@@ -712,6 +715,7 @@ cudaError_t launch_gat_tc_pack(int game, int fp16, const float* d_weights, void*
 
 cudaError_t launch_gat_tc(int game, int fp16, const void* d_packed, const float* d_weights, const int8_t* d_boards,
                           const int8_t* d_side, int n, float* d_pi, float* d_v, int* d_err, cudaStream_t stream) {
+  if (game == kChess) return launch_chess_tc(fp16, d_packed, d_weights, d_boards, d_side, n, d_pi, d_v, d_err, stream);
   if (game != kConnect4) return cudaErrorNotSupported;
   if (n <= 0) return cudaSuccess;
   TcParams p;

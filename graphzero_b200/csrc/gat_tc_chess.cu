@@ -1,0 +1,771 @@
+// Tensor-core (tcgen05) GAT forward for chess: all eight layers, the
+// 4672-way policy and the value head in one persistent launch, one CTA per
+// SM.  Same machinery as the Connect4 kernel (gat_tc.cu); what differs:
+//
+//   * a tile is 128 node rows = 2 positions x 64 squares;
+//   * the graph is the static queen-line + knight + self geometry (up to 36
+//     neighbours per square, 1856 edges per position), held as a neighbour
+//     table in shared memory; each row's attention weights span its
+//     position's 64 squares, i.e. 32 tensor-memory columns of the e buffer
+//     (lane quarters 0-1: columns 0-31, quarters 2-3: 32-63);
+//   * layer 0 has 18 input features (K padded to 32);
+//   * policy: logits[square][73] = X_8[square] . W_pi + b_pi as one more MMA
+//     (N = 80, K = 256) on the last layer's activations, softmax over the
+//     position's 4672 logits, staged in shared memory and written with one
+//     bulk copy per position;
+//   * value: mean-pool over the 64 squares (warp reduce-scatter), then the
+//     256 -> 64 ReLU -> 1 tanh head in fp32.
+//
+// Reference: networks/gat/gat.cu:836-870 (forward_gat_layer), 916-948
+// (compute_output: per-node 256 -> 73 policy for chess), 995-1038
+// (softmax, tanh); action index square * 73 + type (games/chess/chess.cu:96-135).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#include "gz_games.h"
+#include "gz_internal.h"
+#include "gz_sm100.h"
+
+namespace gz {
+namespace {
+
+using namespace sm100;
+
+constexpr int kN = 64;              // squares
+constexpr int kGPT = 2;             // positions per tile
+constexpr int kRows = 128;          // MMA M
+constexpr int kLayers = 8;
+constexpr int kF = 18;              // input features
+constexpr int kP = 73;              // policy outputs per square
+constexpr int kPN = 80;             // policy MMA N (73 padded to a multiple of 16)
+constexpr int kA = kN * kP;         // 4672 actions
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = (kEpiWarps + 3) * 32;
+constexpr int kProducerWarp = kEpiWarps;
+constexpr int kMmaWarp = kEpiWarps + 1;     // projection + policy MMAs + group 0's gathers
+constexpr int kGatherWarp = kEpiWarps + 2;  // group 1's gathers
+constexpr int kWRows = 256 + 32;            // projection rows + score rows
+constexpr int kWChunk = kWRows * 128;       // 36 KB: 288 rows x 64 K x 2 B
+constexpr int kWScoreOff = 256 * 128;
+constexpr int kPolChunk = kPN * 128;        // 10 KB: 80 rows x 64 K x 2 B
+constexpr int kWSlots = 2;
+constexpr int kLayerChunks = 1 + (kLayers - 1) * 4;     // 29
+constexpr int kChunksPerTile = kLayerChunks + 4;        // + 4 policy chunks
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAlphaCol = 256;
+constexpr uint32_t kScoreCol = kAlphaCol + 64;          // aliases e buffer (0, 1) columns 0..31
+constexpr uint32_t kPolCol = kAlphaCol;                 // policy accumulator, after the last gathers
+constexpr uint64_t kWaitLimitNs = 4000000000ull;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMaxDeg = 36;                             // queen lines (27 max) + knights (8) + self
+
+// chess graph degree of a square (queen lines + knight + self), host/device
+__host__ __device__ constexpr int chess_degree(int s) {
+  int d = 0;
+  for (int j = 0; j < 64; ++j) {
+    const int dr = (j >> 3) - (s >> 3), dc = (j & 7) - (s & 7);
+    const int ar = dr < 0 ? -dr : dr, ac = dc < 0 ? -dc : dc;
+    if (j == s || dr == 0 || dc == 0 || ar == ac || (ar == 1 && ac == 2) || (ar == 2 && ac == 1)) ++d;
+  }
+  return d;
+}
+__host__ __device__ constexpr int chess_max_degree() {
+  int m = 0;
+  for (int s = 0; s < 64; ++s) m = chess_degree(s) > m ? chess_degree(s) : m;
+  return m;
+}
+static_assert(chess_max_degree() <= kMaxDeg, "neighbour table width");
+
+// Shared memory map (bytes).
+constexpr int kStageStride = 144;                       // 32 used words + pad (conflict-free 16 B reads)
+constexpr int kSmX = 0;                                 // X tile 64 KB; after the policy MMA: pi staging
+constexpr int kSmW = kSmX + 4 * 16384;
+constexpr int kSmB2 = kSmW + kWSlots * kWChunk;
+constexpr int kSmStage = kSmB2 + 4 * 8192;
+constexpr int kSmTsc = kSmStage + 2 * 128 * kStageStride;
+constexpr int kSmVec = kSmTsc + 2 * 129 * 16;
+constexpr int kVecFloats = 256;
+constexpr int kSmNbr = kSmVec + 2 * kVecFloats * 4;     // [64 squares][kMaxDeg] neighbour squares, 255 = none
+constexpr int kSmDeg = kSmNbr + 64 * kMaxDeg;           // [64]
+constexpr int kSmPool = kSmDeg + 64;                    // [2 groups][4 quarters][32] node sums of one head
+constexpr int kSmZ = kSmPool + 2 * 4 * 32 * 4;          // [2 groups][2 halves][2 pos][64] value partial sums
+constexpr int kSmRed = kSmZ + 2 * 2 * kGPT * 64 * 4;    // [4 quarters][2] policy max / sum exchange
+constexpr int kSmBar = (kSmRed + 4 * 2 * 4 + 7) & ~7;
+constexpr int kNumBars = 2 * kWSlots + 1 + 1 + 4 + 4 + 2 + 1;  // full, empty, acc_full, x_ready, req, done2, drain[2], pol_full
+constexpr int kSmMisc = kSmBar + kNumBars * 8;
+constexpr int kSmemBytes = kSmMisc + 16;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+static_assert(kSmW % 1024 == 0 && kWChunk % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+static_assert(kGPT * kA * 4 <= kSmW, "policy staging fits in the X tile");
+
+// Offsets (floats) into the fp32 weight blob for chess (gat_layout order).
+struct ChOff {
+  static constexpr int kLayer0 = kF * 256 + 256 + 512;
+  static constexpr int kLayerN = 256 * 256 + 256 + 512;
+  __host__ __device__ static constexpr int W(int l) { return l == 0 ? 0 : kLayer0 + (l - 1) * kLayerN; }
+  __host__ __device__ static constexpr int b(int l) { return W(l) + (l == 0 ? kF : 256) * 256; }
+  __host__ __device__ static constexpr int a(int l) { return b(l) + 256; }
+  static constexpr int kHeads = kLayer0 + (kLayers - 1) * kLayerN;
+  static constexpr int w_pi = kHeads, b_pi = w_pi + 256 * kP, W_v1 = b_pi + kP, b_v1 = W_v1 + 256 * 64;
+  static constexpr int w_v2 = b_v1 + 64, b_v2 = w_v2 + 64;
+};
+
+template <typename T> struct OpType;
+template <> struct OpType<__nv_bfloat16> {
+  static constexpr uint32_t fmt = 1;
+  static __device__ __forceinline__ uint16_t bits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+  static __device__ __forceinline__ float round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  static __device__ __forceinline__ uint32_t pack_sr(float lo, float hi, uint32_t rbits) {
+    uint32_t d;
+    asm("cvt.rs.satfinite.bf16x2.f32 %0, %1, %2, %3;" : "=r"(d) : "f"(hi), "f"(lo), "r"(rbits));
+    return d;
+  }
+};
+template <> struct OpType<__half> {
+  static constexpr uint32_t fmt = 0;
+  static __device__ __forceinline__ uint16_t bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
+  static __device__ __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  static __device__ __forceinline__ uint32_t pack_sr(float lo, float hi, uint32_t rbits) {
+    uint32_t d;
+    asm("cvt.rs.satfinite.f16x2.f32 %0, %1, %2, %3;" : "=r"(d) : "f"(hi), "f"(lo), "r"(rbits));
+    return d;
+  }
+};
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ bool epilogue_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 2, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok), "r"(kEpiWarps * 32)
+      : "memory");
+  return r != 0;
+}
+
+// Random bits for stochastically rounding node `li` (square, so a position
+// rounds the same way in any batch slot), layer l, head h; see gat_tc.cu.
+__device__ __forceinline__ uint32_t round_seed(int li, int l, int h) {
+  uint32_t x = (uint32_t)li * 0x9E3779B1u + (uint32_t)(l * 8 + h + 1) * 0x85EBCA77u;
+  x ^= x >> 15;
+  x *= 0x2C1B3C6Du;
+  x ^= x >> 12;
+  return x;
+}
+__host__ __device__ constexpr uint32_t pair_mix(int m) { return (uint32_t)(m + 1) * 0x9E3779B9u ^ 0x7F4A7C15u; }
+
+__device__ __forceinline__ float comp(const float4& v, int k) {
+  return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
+}
+
+__device__ __forceinline__ float2 elu2(float2 y) {
+  const float2 zl = __fmul2_rn(y, make_float2(kLog2e, kLog2e));
+  const float2 em = __fadd2_rn(make_float2(ex2_approx(-fabsf(zl.x)), ex2_approx(-fabsf(zl.y))), make_float2(-1.f, -1.f));
+  return make_float2(fmaxf(em.x, y.x), fmaxf(em.y, y.y));
+}
+
+// Sum of v[0..31] over the 32 lanes, scattered: lane d returns the sum of
+// element d (recursive halving: 16 + 8 + 4 + 2 + 1 shuffles).
+__device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool upper = (lane & w) != 0;
+#pragma unroll
+    for (int k = 0; k < w; ++k) {
+      // keep the half this lane owns, send the other half
+      const float send = upper ? v[k] : v[k + w];
+      const float keep = upper ? v[k + w] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+    }
+  }
+  return v[0];  // each halving keeps the half selected by one lane bit: lane L ends with element L
+}
+
+// One group's four gathers of a layer (see gat_tc.cu): wait for head t's
+// request, issue its eight K = 16 steps, commit to done2.
+__device__ __forceinline__ bool serve_gathers(int g, uint32_t tmem, uint64_t b2desc0, uint64_t* req, uint64_t* done2,
+                                              uint32_t (&rph)[2], volatile int* abort_flag) {
+  constexpr uint32_t idesc2 = idesc_f16(0 /* fp16 */, 128, 32, 1 /* B N-contiguous */);
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const int b = t & 1, ab = 2 * g + b;
+    if (!mbar_wait(&req[ab], rph[b] & 1, abort_flag, kWaitLimitNs)) return false;
+    ++rph[b];
+    tc_fence_after();
+    const uint32_t d = tmem + (uint32_t)(32 * (4 * g + t));
+    const uint32_t a_col = tmem + kAlphaCol + (uint32_t)(ab * 64);
+    const uint64_t bd = b2desc0 + (uint64_t)(ab * (8192 >> 4));
+    mma_f16_ts(d, a_col, bd, idesc2, 0);
+#pragma unroll
+    for (int kk = 1; kk < 8; ++kk) mma_f16_ts(d, a_col + kk * 8, bd + kk * (1024 >> 4), idesc2, 1);
+    mma_commit(&done2[ab]);
+  }
+  return true;
+}
+
+// 1-D bulk copy shared -> global (TMA engine), tracked by the issuing
+// thread's bulk group.
+__device__ __forceinline__ void bulk_s2g(void* dst_gmem, const void* src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_gmem), "r"(smem_u32(src_smem)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the committed bulk copies have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until the committed bulk copies are complete (writes visible).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+struct TcParams {
+  const uint8_t* packed;
+  const float* w;
+  const int8_t* boards;
+  const int8_t* side;
+  float* pi;
+  float* v;
+  int* err;
+  int n;
+  int num_tiles;
+};
+
+template <typename OpT>
+__global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) atomicExch(p.err, 2);
+    return;
+  }
+  uint8_t* sX = smem + kSmX;
+  uint8_t* sW = smem + kSmW;
+  uint64_t* bars = (uint64_t*)(smem + kSmBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kWSlots;
+  uint64_t* acc_full = bars + 2 * kWSlots;
+  uint64_t* x_ready = acc_full + 1;
+  uint64_t* req = acc_full + 2;     // [2 groups][2 buffers]
+  uint64_t* done2 = acc_full + 6;   // [2 groups][2 buffers]
+  uint64_t* drain = acc_full + 10;  // [issuing thread]
+  uint64_t* pol_full = acc_full + 12;
+  uint32_t* tmem_slot = (uint32_t*)(smem + kSmMisc);
+  volatile int* abort_flag = (volatile int*)(smem + kSmMisc + 4);
+  uint8_t* nbr = smem + kSmNbr;
+  uint8_t* deg = smem + kSmDeg;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  for (int i = threadIdx.x; i < 2 * 128 * kStageStride / 4; i += blockDim.x) ((uint32_t*)(smem + kSmStage))[i] = 0u;
+  if (threadIdx.x < 8) ((float*)(smem + kSmTsc))[(threadIdx.x >> 2) * 129 * 4 + 128 * 4 + (threadIdx.x & 3)] = -INFINITY;
+  if (threadIdx.x < 64) {  // neighbour table of square s (the chess board graph, build_graph_csr order)
+    const int s = threadIdx.x;
+    int d = 0;
+    for (int j = 0; j < 64; ++j)
+      if (graph_adjacent(kChess, 8, 8, s, j)) nbr[s * kMaxDeg + d++] = (uint8_t)j;
+    deg[s] = (uint8_t)d;
+    for (int k = d; k < kMaxDeg; ++k) nbr[s * kMaxDeg + k] = 255;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWSlots; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(x_ready, kEpiWarps);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&req[i], 4);
+      mbar_init(&done2[i], 1);
+    }
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
+    mbar_init(pol_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kProducerWarp) {
+    // ---------------- weight producer ----------------
+    if (lane == 0) {
+      uint32_t q = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        for (int c = 0; c < kChunksPerTile && ok; ++c, ++q) {
+          const int s = q % kWSlots;
+          const uint32_t bytes = c < kLayerChunks ? kWChunk : kPolChunk;
+          const size_t off = c < kLayerChunks ? (size_t)c * kWChunk
+                                              : (size_t)kLayerChunks * kWChunk + (size_t)(c - kLayerChunks) * kPolChunk;
+          ok = mbar_wait(&empty[s], ((q / kWSlots) & 1) ^ 1, abort_flag, kWaitLimitNs);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&full[s], bytes);
+          bulk_g2s(sW + s * kWChunk, p.packed + off, bytes, &full[s]);
+        }
+      }
+      for (uint32_t k = (q > kWSlots ? q - kWSlots : 0); k < q; ++k)
+        mbar_wait(&full[k % kWSlots], (k / kWSlots) & 1, abort_flag, kWaitLimitNs);
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer: projections, policy, group 0's gathers ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc1 = idesc_f16(OpType<OpT>::fmt, 128, 256);
+      constexpr uint32_t idesc_s = idesc_f16(OpType<OpT>::fmt, 128, 32);
+      constexpr uint32_t idesc_p = idesc_f16(OpType<OpT>::fmt, 128, kPN);
+      const uint64_t xdesc = sw128_desc(smem_u32(sX));
+      const uint64_t wdesc0 = sw128_desc(smem_u32(sW));
+      const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
+      uint32_t q = 0, xph = 0, rph[2] = {0, 0};
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        for (int l = 0; l <= kLayers && ok; ++l) {  // l == kLayers: the policy MMA
+          ok = mbar_wait(x_ready, xph & 1, abort_flag, kWaitLimitNs);
+          ++xph;
+          if (!ok) break;
+          tc_fence_after();
+          const bool pol = l == kLayers;
+          const int nchunk = l == 0 ? 1 : 4;
+          for (int c = 0; c < nchunk && ok; ++c, ++q) {
+            const int s = q % kWSlots;
+            ok = mbar_wait(&full[s], (q / kWSlots) & 1, abort_flag, kWaitLimitNs);
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t xd = xdesc + (uint64_t)(c * (16384 >> 4)), wd = wdesc0 + (uint64_t)(s * (kWChunk >> 4));
+            if (pol) {
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) mma_f16_ss(tmem + kPolCol, xd + kk * 2, wd + kk * 2, idesc_p, (c | kk) != 0);
+            } else {
+              const int ksteps = l == 0 ? 2 : 4;  // layer 0: 18 features in K = 32
+              for (int kk = 0; kk < ksteps; ++kk) {
+                mma_f16_ss(tmem, xd + kk * 2, wd + kk * 2, idesc1, (c | kk) != 0);
+                mma_f16_ss(tmem + kScoreCol, xd + kk * 2, wd + (kWScoreOff >> 4) + kk * 2, idesc_s, (c | kk) != 0);
+              }
+            }
+            mma_commit(&empty[s]);
+          }
+          if (!ok) break;
+          if (pol) {
+            mma_commit(pol_full);
+          } else {
+            mma_commit(acc_full);
+            ok = serve_gathers(0, tmem, b2desc0, req, done2, rph, abort_flag);
+          }
+        }
+      }
+      mma_commit(&drain[0]);
+      mbar_wait(&drain[0], 0, abort_flag, kWaitLimitNs);
+    }
+    __syncwarp();
+  } else if (warp == kGatherWarp) {
+    if (lane == 0) {
+      const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
+      uint32_t rph[2] = {0, 0};
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x)
+        for (int l = 0; l < kLayers && ok; ++l) ok = serve_gathers(1, tmem, b2desc0, req, done2, rph, abort_flag);
+      mma_commit(&drain[1]);
+      mbar_wait(&drain[1], 0, abort_flag, kWaitLimitNs);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: warpgroup g owns heads 4g..4g+3 ----------------
+    const int g = warp >> 2, qd = warp & 3;
+    const int i = 32 * qd + lane;        // node row
+    const int pg = i >> 6, sq = i & 63;  // position slot in the tile, square
+    const uint32_t tlane = tmem + ((uint32_t)(32 * qd) << 16);
+    const int jw0 = 64 * pg;             // first node of this row's position: its e window
+    uint8_t* srow = smem + kSmStage + (g * 128 + i) * kStageStride;
+    const float4* tsc = (const float4*)(smem + kSmTsc) + g * 129;
+    const int my_deg = deg[sq];
+    const uint8_t* my_nbr = nbr + sq * kMaxDeg;
+    const int gbar = 3 + g;
+    uint32_t aph = 0, pph = 0, dph[2] = {0, 0};
+    bool ok = true, wok = true;
+
+    {
+      uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int b = 0; b < 2; ++b)
+        for (int c = 0; c < 64; c += 8) tmem_st_x8(tlane + kAlphaCol + (2 * g + b) * 64 + c, z);
+      tmem_st_wait();
+    }
+
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      // -- encode the tile's positions into X chunk 0 (K = 0..31: 18 features, zeros) --
+      for (int t = threadIdx.x; t < kRows * 4; t += kEpiWarps * 32) {
+        const int j = t >> 2, unit = t & 3;
+        const int gj = j >> 6, lj = j & 63;
+        const int pos = tile * kGPT + gj;
+        uint32_t wv[4] = {0, 0, 0, 0};
+        if (unit < 3 && pos < p.n) {
+          float f[kF];
+          encode_node(kChess, p.boards + (size_t)pos * 66, p.side[pos], lj, f);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int k0 = unit * 8 + 2 * e;
+            wv[e] = OpType<OpT>::pack(k0 < kF ? f[k0 < kF ? k0 : 0] : 0.f, k0 + 1 < kF ? f[k0 + 1 < kF ? k0 + 1 : 0] : 0.f);
+          }
+        }
+        *(uint4*)(sX + sw128_offset(j, unit * 8)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(x_ready);
+
+      const int gt = threadIdx.x & 127, vu = gt & 63, vhalf = gt >> 6;
+      float* zacc = (float*)(smem + kSmZ) + (g * 2 + vhalf) * kGPT * 64 + vu;  // [pg * 64]
+
+      auto layer = [&](int l, auto last_tag) -> bool {
+        constexpr bool last = decltype(last_tag)::value;
+        float* vec = (float*)(smem + kSmVec) + (l & 1) * kVecFloats;
+        vec[threadIdx.x] = __ldg(p.w + ChOff::b(l) + threadIdx.x);
+        wok = mbar_wait(acc_full, aph & 1, abort_flag, kWaitLimitNs) && wok;
+        ok = epilogue_all(wok);
+        ++aph;
+        if (!ok) return false;
+        tc_fence_after();
+
+        float s[4];
+        {
+          float hi[8], lo[8];
+          tmem_ld_x8(tlane + kScoreCol + 8 * g, hi);
+          tmem_ld_x8(tlane + kScoreCol + 16 + 8 * g, lo);
+          tmem_ld_wait();
+#pragma unroll
+          for (int t = 0; t < 4; ++t) s[t] = hi[2 * t] + lo[2 * t];
+          ((float4*)(smem + kSmTsc))[g * 129 + i] =
+              make_float4(hi[1] + lo[1], hi[3] + lo[3], hi[5] + lo[5], hi[7] + lo[7]);
+        }
+        tc_fence_before();
+        named_bar_sync(1, kEpiWarps * 32);
+        tc_fence_after();
+        if (g == 0) {
+          uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) tmem_st_x8(tlane + kScoreCol + c, z);
+          tmem_st_wait();
+        }
+        float inv[4] = {0.f, 0.f, 0.f, 0.f};
+
+        auto finish_head = [&](int t) {
+          const int h = 4 * g + t, b = t & 1;
+          wok = mbar_wait(&done2[2 * g + b], dph[b] & 1, abort_flag, kWaitLimitNs) && wok;
+          ++dph[b];
+          tc_fence_after();
+          float o[32];
+          tmem_ld_x32(tlane + (uint32_t)(32 * h), o);
+          tmem_ld_wait();
+          const float4* bias4 = (const float4*)(vec + 32 * h);
+          const float2 iv = make_float2(inv[t], inv[t]);
+          float2 y[16];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float4 bv = bias4[k];
+            y[2 * k] = elu2(__ffma2_rn(make_float2(o[4 * k], o[4 * k + 1]), iv, make_float2(bv.x, bv.y)));
+            y[2 * k + 1] = elu2(__ffma2_rn(make_float2(o[4 * k + 2], o[4 * k + 3]), iv, make_float2(bv.z, bv.w)));
+          }
+          // next layer's operand (the last layer's feeds the policy MMA)
+          {
+            const uint32_t seed = round_seed(sq, l, h);
+            uint8_t* xrow = sX + (h >> 1) * 16384 + (i >> 3) * 1024 + (i & 7) * 128;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int unit = (4 * (h & 1) + u) ^ (i & 7);
+              uint32_t qv[4];
+#pragma unroll
+              for (int m = 0; m < 4; ++m)
+                qv[m] = OpType<OpT>::pack_sr(y[4 * u + m].x, y[4 * u + m].y, seed ^ pair_mix(4 * u + m));
+              *(uint4*)(xrow + unit * 16) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
+            }
+          }
+          if constexpr (last) {
+            // value head: node sums of this head (fp32), per position
+            float v32[32];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              v32[2 * k] = y[k].x;
+              v32[2 * k + 1] = y[k].y;
+            }
+            const float sum = reduce_scatter32(v32, lane);  // lane d: sum of feature d over this warp's rows
+            float* pool = (float*)(smem + kSmPool) + (g * 4 + qd) * 32;
+            pool[lane] = sum;
+            named_bar_sync(gbar, 128);
+            float wv[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) wv[j] = __ldg(p.w + ChOff::W_v1 + (32 * h + 16 * vhalf + j) * 64 + vu);
+#pragma unroll
+            for (int q2 = 0; q2 < kGPT; ++q2) {
+              const float* pa = (const float*)(smem + kSmPool) + (g * 4 + 2 * q2) * 32;
+              float acc = t == 0 ? 0.f : zacc[q2 * 64];
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                acc = fmaf((pa[16 * vhalf + j] + pa[32 + 16 * vhalf + j]) * (1.0f / kN), wv[j], acc);
+              zacc[q2 * 64] = acc;
+            }
+            named_bar_sync(gbar, 128);  // pool slots reused by the next head
+          }
+        };
+
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int h = 4 * g + t, b = t & 1;
+          {  // P1: Wh^h (fp32) -> fp16 B operand of the gather
+            float wh[32];
+            tmem_ld_x32(tlane + (uint32_t)(32 * h), wh);
+            tmem_ld_wait();
+            uint8_t* b2 = smem + kSmB2 + (2 * g + b) * 8192 + (i >> 3) * 512 + (i & 7) * 16;
+#pragma unroll
+            for (int ng = 0; ng < 4; ++ng)
+              *(uint4*)(b2 + ng * 128) =
+                  make_uint4(OpType<__half>::pack(wh[8 * ng + 0], wh[8 * ng + 1]), OpType<__half>::pack(wh[8 * ng + 2], wh[8 * ng + 3]),
+                             OpType<__half>::pack(wh[8 * ng + 4], wh[8 * ng + 5]), OpType<__half>::pack(wh[8 * ng + 6], wh[8 * ng + 7]));
+          }
+          {  // P2: softmax numerators over the square's neighbours -> e row (fp16)
+            float lg[kMaxDeg];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < kMaxDeg; ++k) {
+              const int j = my_nbr[k];  // 255 = none
+              const float tj = k < my_deg ? comp(tsc[jw0 + (j & 63)], t) : -INFINITY;
+              const float x = s[t] + tj;
+              lg[k] = fmaxf(x, kLeakySlope * x);
+              mx = fmaxf(mx, lg[k]);
+            }
+            const float c = -mx * kLog2e;
+            float z = 0.f;
+            const uint32_t sbase = smem_u32(srow);
+#pragma unroll
+            for (int k = 0; k < kMaxDeg; ++k) {
+              const __half e = __float2half_rn(ex2_approx(fmaf(lg[k], kLog2e, c)));
+              z += __half2float(e);
+              const int j = my_nbr[k];
+              // absent neighbours write a pad half-word (64) of the row
+              const uint32_t addr = sbase + 2 * (k < my_deg ? (j & 63) : 64);
+              asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(__half_as_ushort(e)) : "memory");
+            }
+            inv[t] = __frcp_rn(z);
+            uint32_t a[32];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint4 v = *(const uint4*)(srow + 16 * k);
+              a[4 * k] = v.x;
+              a[4 * k + 1] = v.y;
+              a[4 * k + 2] = v.z;
+              a[4 * k + 3] = v.w;
+            }
+            const uint32_t acol = tlane + kAlphaCol + (uint32_t)((2 * g + b) * 64 + (jw0 >> 1));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) tmem_st_x8(acol + 8 * k, *(const uint32_t(*)[8])(a + 8 * k));
+            tmem_st_wait();
+          }
+          fence_proxy_async_smem();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&req[2 * g + b]);
+          if (t >= 1) finish_head(t - 1);
+        }
+        finish_head(3);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(x_ready);  // next layer's X (after the last: the policy MMA's A)
+        return true;
+      };
+      for (int l = 0; l < kLayers && ok; ++l) {
+        const bool cont = l < kLayers - 1 ? layer(l, std::false_type{}) : layer(l, std::true_type{});
+        if (!cont) break;
+      }
+      if (!ok) break;
+
+      // ---------------- heads ----------------
+      wok = mbar_wait(pol_full, pph & 1, abort_flag, kWaitLimitNs) && wok;
+      ++pph;
+      ok = epilogue_all(wok);  // also: value partial sums of both groups visible
+      if (!ok) break;
+      tc_fence_after();
+      float* stage = (float*)(smem + kSmX);  // X is free once the policy MMA completed
+      float* red = (float*)(smem + kSmRed);
+      if (g == 0) {
+        // policy: this square's 73 logits, softmax over the position's 4672
+        float lgt[kPN];
+        tmem_ld_x32(tlane + kPolCol, *(float(*)[32])(lgt));
+        tmem_ld_x32(tlane + kPolCol + 32, *(float(*)[32])(lgt + 32));
+        tmem_ld_x8(tlane + kPolCol + 64, *(float(*)[8])(lgt + 64));
+        tmem_ld_x8(tlane + kPolCol + 72, *(float(*)[8])(lgt + 72));
+        tmem_ld_wait();
+        float mx = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < kP; ++k) {
+          lgt[k] += __ldg(p.w + ChOff::b_pi + k);
+          mx = fmaxf(mx, lgt[k]);
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) red[qd * 2] = mx;
+        named_bar_sync(gbar, 128);
+        mx = fmaxf(red[(qd & ~1) * 2], red[(qd | 1) * 2]);  // the two warps of this position
+        float z = 0.f;
+#pragma unroll
+        for (int k = 0; k < kP; ++k) {
+          lgt[k] = ex2_approx((lgt[k] - mx) * kLog2e);
+          z += lgt[k];
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+        if (lane == 0) red[qd * 2 + 1] = z;
+        named_bar_sync(gbar, 128);
+        const float iz = 1.0f / (red[(qd & ~1) * 2 + 1] + red[(qd | 1) * 2 + 1]);
+        float* out = stage + pg * kA + sq * kP;
+#pragma unroll
+        for (int k = 0; k < kP; ++k) out[k] = lgt[k] * iz;
+        // the policy accumulator overlaid e buffers (0, 0) and (0, 1): restore
+        // their zero background (columns outside each lane's window are read
+        // by every gather)
+        uint32_t zz[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int c = 0; c < kPN; c += 8) tmem_st_x8(tlane + kPolCol + c, zz);
+        tmem_st_wait();
+      } else if (warp - 4 < kGPT) {
+        // value head of position (warp - 4): 64 hidden units, two per lane
+        const int q2 = warp - 4, pos = tile * kGPT + q2;
+        const float* zp = (const float*)(smem + kSmZ);
+        float z0 = __ldg(p.w + ChOff::b_v1 + lane), z1 = __ldg(p.w + ChOff::b_v1 + 32 + lane);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {  // [group][half]
+          z0 += zp[(c4 * kGPT + q2) * 64 + lane];
+          z1 += zp[(c4 * kGPT + q2) * 64 + 32 + lane];
+        }
+        float vv = fmaxf(z0, 0.f) * __ldg(p.w + ChOff::w_v2 + lane) + fmaxf(z1, 0.f) * __ldg(p.w + ChOff::w_v2 + 32 + lane);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) vv += __shfl_xor_sync(0xffffffffu, vv, o);
+        if (lane == 0 && pos < p.n) p.v[pos] = tanhf(vv + __ldg(p.w + ChOff::b_v2));
+      }
+      fence_proxy_async_smem();  // staged probabilities -> the bulk copy's async proxy
+      tc_fence_before();
+      named_bar_sync(1, kEpiWarps * 32);
+      if (threadIdx.x == 0) {
+        for (int q2 = 0; q2 < kGPT; ++q2) {
+          const int pos = tile * kGPT + q2;
+          if (pos < p.n) bulk_s2g(p.pi + (size_t)pos * kA, stage + q2 * kA, kA * 4);
+        }
+        bulk_commit();
+        bulk_wait_read();  // X is rewritten by the next tile's encode
+      }
+      named_bar_sync(1, kEpiWarps * 32);
+    }
+    if (threadIdx.x == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) atomicExch(p.err, 1);
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---- weight packing ----
+// Chunks 0..28: per layer W_l^T (256 rows) + attention-score rows W_l a (16
+// high parts, 16 remainders), [288 rows][64 K] swizzled; layer 0 has K = 18.
+// Chunks 29..32: W_pi^T [80 rows (73 used)][64 K].
+template <typename OpT>
+__global__ void pack_chess_kernel(const float* __restrict__ w, uint8_t* __restrict__ out) {
+  const int chunk = blockIdx.x;
+  if (chunk >= kLayerChunks) {
+    const int c = chunk - kLayerChunks;
+    uint8_t* dst = out + (size_t)kLayerChunks * kWChunk + (size_t)c * kPolChunk;
+    for (int t = threadIdx.x; t < kPN * 64; t += blockDim.x) {
+      const int n = t / 64, kk = t % 64, k = c * 64 + kk;
+      const float x = n < kP ? w[ChOff::w_pi + (size_t)k * kP + n] : 0.f;
+      *(uint16_t*)(dst + sw128_offset(n, kk)) = OpType<OpT>::bits(x);
+    }
+    return;
+  }
+  const int layer = chunk == 0 ? 0 : 1 + (chunk - 1) / 4;
+  const int c = chunk == 0 ? 0 : (chunk - 1) % 4;
+  const int fin = layer == 0 ? kF : 256;
+  const float* W = w + ChOff::W(layer);
+  const float* A = w + ChOff::a(layer);
+  uint8_t* dst = out + (size_t)chunk * kWChunk;
+  for (int t = threadIdx.x; t < 256 * 64; t += blockDim.x) {
+    const int f = t / 64, kk = t % 64, k = c * 64 + kk;
+    const float x = k < fin ? W[(size_t)k * 256 + f] : 0.f;
+    *(uint16_t*)(dst + sw128_offset(f, kk)) = OpType<OpT>::bits(x);
+  }
+  for (int t = threadIdx.x; t < 16 * 64; t += blockDim.x) {
+    const int j = t / 64, kk = t % 64, k = c * 64 + kk, h = j >> 1, v = j & 1;
+    float acc = 0.f;
+    if (k < fin)
+      for (int f = 0; f < 32; ++f) acc = fmaf(W[(size_t)k * 256 + 32 * h + f], A[(2 * h + v) * 32 + f], acc);
+    const float hi = OpType<OpT>::round(acc);
+    *(uint16_t*)(dst + sw128_offset(256 + j, kk)) = OpType<OpT>::bits(hi);
+    *(uint16_t*)(dst + sw128_offset(272 + j, kk)) = OpType<OpT>::bits(acc - hi);
+  }
+}
+
+}  // namespace
+
+size_t chess_tc_packed_bytes() { return (size_t)kLayerChunks * kWChunk + 4 * (size_t)kPolChunk; }
+
+cudaError_t launch_chess_tc_pack(int fp16, const float* d_weights, void* d_packed, cudaStream_t stream) {
+  if (fp16) pack_chess_kernel<__half><<<kChunksPerTile, 256, 0, stream>>>(d_weights, (uint8_t*)d_packed);
+  else pack_chess_kernel<__nv_bfloat16><<<kChunksPerTile, 256, 0, stream>>>(d_weights, (uint8_t*)d_packed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_chess_tc(int fp16, const void* d_packed, const float* d_weights, const int8_t* d_boards,
+                            const int8_t* d_side, int n, float* d_pi, float* d_v, int* d_err, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  if (((uintptr_t)d_pi & 15u) != 0) return cudaErrorInvalidValue;  // bulk stores of the policy rows
+  TcParams p;
+  p.packed = (const uint8_t*)d_packed;
+  p.w = d_weights;
+  p.boards = d_boards;
+  p.side = d_side;
+  p.pi = d_pi;
+  p.v = d_v;
+  p.err = d_err;
+  p.n = n;
+  p.num_tiles = (n + kGPT - 1) / kGPT;
+  auto kern = fp16 ? gat_tc_chess_kernel<__half> : gat_tc_chess_kernel<__nv_bfloat16>;
+  static int cached_grid[64][2];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  int& full_grid = cached_grid[dev][fp16 ? 1 : 0];
+  if (full_grid == 0) {
+    int sms = 0;
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    full_grid = sms;
+  }
+  const int grid = full_grid < p.num_tiles ? full_grid : p.num_tiles;
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace gz

@@ -31,6 +31,13 @@ cudaError_t launch_gat_tc_pack(int game, int fp16, const float* d_weights, void*
 cudaError_t launch_gat_tc(int game, int fp16, const void* d_packed, const float* d_weights, const int8_t* d_boards,
                           const int8_t* d_side, int n, float* d_pi, float* d_v, int* d_err, cudaStream_t stream);
 
+// Chess tensor-core GAT (gat_tc_chess.cu); reached through the gat_tc
+// functions above with game == chess.
+size_t chess_tc_packed_bytes();
+cudaError_t launch_chess_tc_pack(int fp16, const float* d_weights, void* d_packed, cudaStream_t stream);
+cudaError_t launch_chess_tc(int fp16, const void* d_packed, const float* d_weights, const int8_t* d_boards,
+                            const int8_t* d_side, int n, float* d_pi, float* d_v, int* d_err, cudaStream_t stream);
+
 // bf16 tensor-core Connect4 ResNet forward (implicit-GEMM 3x3 convolutions).
 size_t resnet_tc_packed_bytes();
 cudaError_t launch_resnet_tc_pack(int fp16, const float* d_weights, void* d_packed, cudaStream_t stream);

@@ -33,9 +33,7 @@ def run(net, boards, side):
 
 
 def inputs(game, n, seed):
-    if game == gz.CHESS:
-        return chess_boards(n, seed)
-    return gz.synth_positions(game, n, seed=seed)
+    return gz.synth_positions(game, n, seed=seed)  # chess: random legal playouts
 
 
 CASES = [
@@ -158,3 +156,55 @@ def test_bounded_wait_reports_timeout_and_context_survives(cuda):
     boards, side = gz.synth_positions(gz.CONNECT4, 2, seed=3)
     pi, v = net.predict_host(boards, side)
     assert np.isfinite(pi).all() and np.isfinite(v).all()
+
+
+CHESS_TC_CASES = [
+    # precision, sharpened heads, tolerance (policy over 4672 moves, value)
+    (gz.PREC_BF16, False, 1e-3),
+    (gz.PREC_FP16, False, 1e-3),
+    (gz.PREC_FP16, True, 3e-3),
+    (gz.PREC_BF16, True, 1e-2),
+]
+
+
+@pytest.mark.parametrize("prec,sharp,tol", CHESS_TC_CASES)
+def test_chess_tensor_core_matches_oracle(cuda, prec, sharp, tol):
+    """Chess on tensor cores (2 positions per 128-row tile, queen+knight
+    graph, 4672-way policy as an MMA) against the oracle on legal positions."""
+    game = gz.CHESS
+    w = gz.synth_weights(game, seed=23, bias_scale=0.4 if sharp else 0.0)
+    if sharp:
+        w = sharpen(game, w)
+    net = gz.Net(game, precision=prec, max_batch=512)
+    assert net.kernel_name.startswith("gat_tc_")
+    net.load_weights(w)
+    for n in (1, 2, 3, 65, 300):
+        boards, side = inputs(game, n, seed=300 + n)
+        pi, v = run(net, boards, side)
+        opi, ov = oracle.gat_forward(game, w, boards, side)
+        assert np.isfinite(pi).all() and np.isfinite(v).all(), n
+        assert np.abs(pi.sum(1) - 1).max() < 1e-4
+        assert np.abs(pi - opi).max() < tol, (n, np.abs(pi - opi).max())
+        assert np.abs(v - ov).max() < tol, (n, np.abs(v - ov).max())
+    net.check()
+
+
+def test_chess_tensor_core_full_batch(cuda):
+    """The c3 shape: 8192 legal positions in one launch; determinism, batch
+    invariance, and a sample of rows against the oracle."""
+    game = gz.CHESS
+    w = gz.synth_weights(game, seed=0x6A5A + 3)
+    net = gz.Net(game, max_batch=8192)
+    net.load_weights(w)
+    boards, side = gz.synth_positions(game, 8192, seed=0x6A5A + 3)
+    pi, v = run(net, boards, side)
+    pi2, v2 = run(net, boards, side)
+    assert (pi == pi2).all() and (v == v2).all()
+    # the same positions in other batch slots give the same results
+    perm = np.random.default_rng(3).permutation(8192)
+    pi3, v3 = run(net, boards[perm], side[perm])
+    assert np.abs(pi3 - pi[perm]).max() < 1e-6 and np.abs(v3 - v[perm]).max() < 1e-6
+    idx = np.random.default_rng(4).choice(8192, 200, replace=False)
+    opi, ov = oracle.gat_forward(game, w, boards[idx], side[idx])
+    assert np.abs(pi[idx] - opi).max() < 1e-3 and np.abs(v[idx] - ov).max() < 1e-3
+    net.check()
