@@ -343,7 +343,8 @@ gz_status gz_net_create(const gz_net_config* cfg, int device, gz_net** out) {
   size_t out_floats = (size_t)n->max_batch * (s.actions + 1);
   chk(cudaMallocHost(&n->h_in, in_bytes), "cudaMallocHost in");
   chk(cudaMalloc(&n->d_in, in_bytes), "cudaMalloc in");
-  chk(cudaMallocHost(&n->h_out, out_floats * sizeof(float)), "cudaMallocHost out");
+  // + one word after the outputs: the error word, copied back with them
+  chk(cudaMallocHost(&n->h_out, (out_floats + 1) * sizeof(float)), "cudaMallocHost out");
   chk(cudaMalloc(&n->d_out, out_floats * sizeof(float)), "cudaMalloc out");
   chk(cudaStreamCreateWithFlags(&n->stream, cudaStreamNonBlocking), "stream");
   if (st == GZ_OK) {
@@ -474,17 +475,20 @@ gz_status gz_net_predict_batch(gz_net* n, const int8_t* boards, const int8_t* si
   return run_forward(n, boards, side, count, pi, v, (cudaStream_t)stream);
 }
 
+// Turns a nonzero device error word into a status (and clears the word).
+static gz_status forward_error(gz_net* n, int err) {
+  if (!err) return GZ_OK;
+  GZ_CUDA(cudaMemset(n->d_err, 0, sizeof(int)));
+  if (err == 2) return fail(GZ_ERR_CUDA, "forward kernel: dynamic shared memory base not 1024-byte aligned");
+  return fail(GZ_ERR_TIMEOUT, "a bounded wait inside the forward kernel gave up (outputs of that launch are invalid)");
+}
+
 gz_status gz_net_check(gz_net* n) {
   if (!n) return fail(GZ_ERR_INVALID_ARG, "null net");
   GZ_DEVICE(n->device);
   int err = 0;
   GZ_CUDA(cudaMemcpy(&err, n->d_err, sizeof(int), cudaMemcpyDeviceToHost));
-  if (err) {
-    GZ_CUDA(cudaMemset(n->d_err, 0, sizeof(int)));
-    if (err == 2) return fail(GZ_ERR_CUDA, "forward kernel: dynamic shared memory base not 1024-byte aligned");
-    return fail(GZ_ERR_TIMEOUT, "a bounded wait inside the forward kernel gave up (outputs of that launch are invalid)");
-  }
-  return GZ_OK;
+  return forward_error(n, err);
 }
 
 gz_status gz_net_predict_host(gz_net* n, const int8_t* boards, const int8_t* side, int count, float* pi, float* v) {
@@ -504,8 +508,11 @@ gz_status gz_net_predict_host(gz_net* n, const int8_t* boards, const int8_t* sid
   if (st != GZ_OK) return st;
   size_t outf = (size_t)count * (s.actions + 1);
   GZ_CUDA(cudaMemcpyAsync(n->h_out, n->d_out, outf * sizeof(float), cudaMemcpyDeviceToHost, n->stream));
+  // the error word rides in the same stream (no second round trip)
+  int* h_err = (int*)(n->h_out + (size_t)n->max_batch * (s.actions + 1));
+  GZ_CUDA(cudaMemcpyAsync(h_err, n->d_err, sizeof(int), cudaMemcpyDeviceToHost, n->stream));
   GZ_CUDA(cudaStreamSynchronize(n->stream));
-  gz_status chk_st = gz_net_check(n);
+  gz_status chk_st = forward_error(n, *h_err);
   if (chk_st != GZ_OK) return chk_st;
   memcpy(pi, n->h_out, (size_t)count * s.actions * sizeof(float));
   memcpy(v, n->h_out + (size_t)count * s.actions, (size_t)count * sizeof(float));
