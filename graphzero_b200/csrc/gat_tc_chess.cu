@@ -87,11 +87,10 @@ constexpr int kSmW = kSmX + 4 * 16384;
 constexpr int kSmB2 = kSmW + kWSlots * kWChunk;
 constexpr int kSmStage = kSmB2 + 4 * 8192;
 constexpr int kSmTsc = kSmStage + 2 * 128 * kStageStride;
-constexpr int kSmVec = kSmTsc + 2 * 129 * 16;
+constexpr int kSmVec = kSmTsc + 2 * 130 * 16;  // t scores: [group][position][64 squares + pad row][4 heads]
 constexpr int kVecFloats = 256;
-constexpr int kSmNbr = kSmVec + 2 * kVecFloats * 4;     // [64 squares][kMaxDeg] neighbour squares, 255 = none
-constexpr int kSmDeg = kSmNbr + 64 * kMaxDeg;           // [64]
-constexpr int kSmPool = kSmDeg + 64;                    // [2 groups][4 quarters][32] node sums of one head
+constexpr int kSmNbr = kSmVec + 2 * kVecFloats * 4;     // [64 squares][kMaxDeg] neighbour squares, 64 = none (pad)
+constexpr int kSmPool = kSmNbr + 64 * kMaxDeg;                    // [2 groups][4 quarters][32] node sums of one head
 constexpr int kSmZ = kSmPool + 2 * 4 * 32 * 4;          // [2 groups][2 halves][2 pos][64] value partial sums
 constexpr int kSmRed = kSmZ + 2 * 2 * kGPT * 64 * 4;    // [4 quarters][2] policy max / sum exchange
 constexpr int kSmBar = (kSmRed + 4 * 2 * 4 + 7) & ~7;
@@ -267,20 +266,21 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
   uint32_t* tmem_slot = (uint32_t*)(smem + kSmMisc);
   volatile int* abort_flag = (volatile int*)(smem + kSmMisc + 4);
   uint8_t* nbr = smem + kSmNbr;
-  uint8_t* deg = smem + kSmDeg;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   for (int i = threadIdx.x; i < 2 * 128 * kStageStride / 4; i += blockDim.x) ((uint32_t*)(smem + kSmStage))[i] = 0u;
-  if (threadIdx.x < 8) ((float*)(smem + kSmTsc))[(threadIdx.x >> 2) * 129 * 4 + 128 * 4 + (threadIdx.x & 3)] = -INFINITY;
+  // the pad row (square 64) of every (group, position) t-score table is -inf:
+  // absent neighbours point at it and get weight 0
+  if (threadIdx.x < 16)
+    ((float*)(smem + kSmTsc))[((threadIdx.x >> 3) * 130 + ((threadIdx.x >> 2) & 1) * 65 + 64) * 4 + (threadIdx.x & 3)] = -INFINITY;
   if (threadIdx.x < 64) {  // neighbour table of square s (the chess board graph, build_graph_csr order)
     const int s = threadIdx.x;
     int d = 0;
     for (int j = 0; j < 64; ++j)
       if (graph_adjacent(kChess, 8, 8, s, j)) nbr[s * kMaxDeg + d++] = (uint8_t)j;
-    deg[s] = (uint8_t)d;
-    for (int k = d; k < kMaxDeg; ++k) nbr[s * kMaxDeg + k] = 255;
+    for (int k = d; k < kMaxDeg; ++k) nbr[s * kMaxDeg + k] = 64;  // the pad square
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kWSlots; ++s) {
@@ -398,8 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
     const uint32_t tlane = tmem + ((uint32_t)(32 * qd) << 16);
     const int jw0 = 64 * pg;             // first node of this row's position: its e window
     uint8_t* srow = smem + kSmStage + (g * 128 + i) * kStageStride;
-    const float4* tsc = (const float4*)(smem + kSmTsc) + g * 129;
-    const int my_deg = deg[sq];
+    const float4* tsc = (const float4*)(smem + kSmTsc) + g * 130 + pg * 65;  // this row's position
     const uint8_t* my_nbr = nbr + sq * kMaxDeg;
     const int gbar = 3 + g;
     uint32_t aph = 0, pph = 0, dph[2] = {0, 0};
@@ -455,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
           tmem_ld_wait();
 #pragma unroll
           for (int t = 0; t < 4; ++t) s[t] = hi[2 * t] + lo[2 * t];
-          ((float4*)(smem + kSmTsc))[g * 129 + i] =
+          ((float4*)(smem + kSmTsc))[g * 130 + pg * 65 + sq] =
               make_float4(hi[1] + lo[1], hi[3] + lo[3], hi[5] + lo[5], hi[7] + lo[7]);
         }
         tc_fence_before();
@@ -543,27 +542,25 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
                              OpType<__half>::pack(wh[8 * ng + 4], wh[8 * ng + 5]), OpType<__half>::pack(wh[8 * ng + 6], wh[8 * ng + 7]));
           }
           {  // P2: softmax numerators over the square's neighbours -> e row (fp16)
-            float lg[kMaxDeg];
-            float mx = -INFINITY;
+            // LeakyReLU is monotonic: the largest logit is lrelu(s + max_j t_j)
+            float tj[kMaxDeg];
+            float tmax = -INFINITY;
 #pragma unroll
             for (int k = 0; k < kMaxDeg; ++k) {
-              const int j = my_nbr[k];  // 255 = none
-              const float tj = k < my_deg ? comp(tsc[jw0 + (j & 63)], t) : -INFINITY;
-              const float x = s[t] + tj;
-              lg[k] = fmaxf(x, kLeakySlope * x);
-              mx = fmaxf(mx, lg[k]);
+              tj[k] = comp(tsc[my_nbr[k]], t);  // absent neighbours: the pad row, -inf
+              tmax = fmaxf(tmax, tj[k]);
             }
-            const float c = -mx * kLog2e;
+            const float xm = s[t] + tmax;
+            const float c = -fmaxf(xm, kLeakySlope * xm) * kLog2e;
             float z = 0.f;
             const uint32_t sbase = smem_u32(srow);
 #pragma unroll
             for (int k = 0; k < kMaxDeg; ++k) {
-              const __half e = __float2half_rn(ex2_approx(fmaf(lg[k], kLog2e, c)));
+              const float x = s[t] + tj[k];
+              const __half e = __float2half_rn(ex2_approx(fmaf(fmaxf(x, kLeakySlope * x), kLog2e, c)));
               z += __half2float(e);
-              const int j = my_nbr[k];
-              // absent neighbours write a pad half-word (64) of the row
-              const uint32_t addr = sbase + 2 * (k < my_deg ? (j & 63) : 64);
-              asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(__half_as_ushort(e)) : "memory");
+              // absent neighbours write the pad half-word (64) of the row
+              asm volatile("st.shared.b16 [%0], %1;" ::"r"(sbase + 2 * my_nbr[k]), "h"(__half_as_ushort(e)) : "memory");
             }
             inv[t] = __frcp_rn(z);
             uint32_t a[32];
