@@ -14,20 +14,28 @@
 //   2. per head h (8 heads, two groups of four run by two warpgroups):
 //      softmax  e_ij = exp(LeakyReLU_0.2(s_i + t_j) - max_j), z_i = sum_j e_ij
 //               over the 8-neighbourhood + self of node i (the Connect4 board
-//               graph); e (fp16, unnormalised) goes into tensor memory
-//      gather   out^h = e^h . Wh^h   as a second tcgen05.mma: e^h (128 x 128,
-//               block-diagonal, zero outside each node's 3x3 stencil) is the
-//               A operand in tensor memory, Wh^h (fp16) the B operand in
-//               shared memory; the result overwrites the head's accumulator
-//               columns
+//               graph); e (fp16, unnormalised) goes into tensor memory, each
+//               lane quarter's rows relative to the 48-node window that holds
+//               all their neighbours
+//      gather   out^h = e^h . Wh^h   as a second tcgen05.mma per lane quarter
+//               (three K = 16 steps over the window, other lanes disabled):
+//               e^h is the A operand in tensor memory, Wh^h (fp16) the B
+//               operand in shared memory; the result overwrites the head's
+//               accumulator columns
 //   3. out / z + bias, ELU, stored as the next layer's X tile (128-byte
 //      swizzled, K-major) -- or, after the last layer, mean-pooled into the
 //      value head (256->64 ReLU, 64->1 tanh) and column-pooled into the policy
 //      head (256->1 per column, softmax over 7), in fp32.
+// The next layer's projection does not wait for the head loop: heads c and
+// c + 4 write K chunk c of the next X tile, and each chunk's MMAs are issued
+// as soon as it exists, into a third accumulator block (tensor memory holds
+// three 128-column blocks that rotate from layer to layer).  Only the last
+// chunk's MMAs remain between two head loops.
 // Weights are pre-packed on the device into 36 KB chunks (256 projection rows
 // + 32 score rows, 64 K each, swizzled) and streamed into a two-slot
 // shared-memory ring by one producer thread with 1-D bulk async copies (TMA
-// engine); one thread issues every MMA.  Every wait is bounded
+// engine).  Three threads issue MMAs: one the projections, two the gathers
+// (each half of every head's lane quarters).  Every wait is bounded
 // (%globaltimer); on a timeout the CTA drains its copies and MMAs, frees
 // tensor memory and reports through the error word.
 //
@@ -55,20 +63,36 @@ constexpr int kGPT = 3;             // positions per tile
 constexpr int kRows = 128;          // MMA M (node rows per tile)
 constexpr int kLayers = 6;
 constexpr int kEpiWarps = 8;        // two warpgroups: heads 0-3 and 4-7
-constexpr int kThreads = (kEpiWarps + 3) * 32;
+constexpr int kThreads = (kEpiWarps + 4) * 32;
 constexpr int kProducerWarp = kEpiWarps;
-constexpr int kMmaWarp = kEpiWarps + 1;     // projection MMAs + group 0's gathers
-constexpr int kGatherWarp = kEpiWarps + 2;  // group 1's gathers (a second issuing thread)
+constexpr int kMmaWarp = kEpiWarps + 1;     // group 0's gathers; allocates tensor memory
+constexpr int kGatherWarp = kEpiWarps + 2;  // group 1's gathers
+constexpr int kProjWarp = kEpiWarps + 3;    // projection and score MMAs
 constexpr int kWRows = 256 + 32;    // projection rows + score rows (16 high parts, 16 remainders)
 constexpr int kWChunk = kWRows * 128;  // 64 K x 2 B per row
 constexpr int kWScoreOff = 256 * 128;  // byte offset of the score rows in a chunk
 constexpr int kWSlots = 2;
 constexpr int kChunksPerTile = 1 + (kLayers - 1) * 4;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAlphaCol = 256;  // e buffers: 256 + (2 * group + buffer) * 64
-// Score accumulator: 32 columns that alias e buffer (group 0, buffer 1)
-// columns 0..31; read at the start of a layer, then re-zeroed by group 0.
-constexpr uint32_t kScoreCol = kAlphaCol + 64;
+// Tensor memory: three 128-column accumulator blocks, the e buffers and the
+// score accumulator.  Layer l's projection Wh occupies two blocks: the first
+// half (columns of heads 0, 4, 1, 5 in that order: the heads the two groups
+// finish first) in block first_block(l), the second half (heads 2, 6, 3, 7)
+// in block second_block(l).  Layer l+1's first half accumulates in the third
+// block from the moment the first K chunk of X(l+1) exists; its second half
+// reuses layer l's first-half block once both groups have finished heads 0
+// and 1 (4 and 5), so the next projection runs under the current head loop.
+// The blocks rotate with period 3 (six layers per tile: every tile starts
+// in the same place).
+constexpr uint32_t kECol = 384;      // e buffers: 384 + (2 * group + buffer) * 24
+constexpr uint32_t kScoreCol = 480;  // scores: 16 high parts + 16 remainders
+__host__ __device__ constexpr int first_block(int l) { return (3 - l % 3) % 3; }
+__host__ __device__ constexpr int second_block(int l) { return (4 - l % 3) % 3; }
+// head 4g + t of layer l: block by t / 2, slot 2 (t % 2) + g inside it
+__host__ __device__ constexpr uint32_t head_col(int l, int g, int t) {
+  return (uint32_t)(128 * (t < 2 ? first_block(l) : second_block(l)) + 32 * (2 * (t & 1) + g));
+}
+static_assert(first_block(kLayers) == first_block(0) && second_block(kLayers) == second_block(0), "rotation period");
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s per wait
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -82,7 +106,8 @@ constexpr int kSmTsc = kSmStage + 2 * 128 * kStageStride;  // t scores: [group][
 constexpr int kSmVec = kSmTsc + 2 * 129 * 16;           // per layer bias[256]; x2 (layer parity)
 constexpr int kVecFloats = 256;
 constexpr int kSmBar = kSmVec + 2 * kVecFloats * 4;
-constexpr int kNumBars = 2 * kWSlots + 1 + 1 + 4 + 4 + 2;  // full, empty, acc_full, x_ready, req[2][2], done2[2][2], drain[2]
+// full, empty, sc_full, acc_a, acc_b, x_ready[4], req[2][2], done2[2][2], drain[3]
+constexpr int kNumBars = 2 * kWSlots + 3 + 4 + 4 + 4 + 3;
 constexpr int kSmMisc = kSmBar + kNumBars * 8;
 constexpr int kSmemBytes = kSmMisc + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -189,31 +214,39 @@ __device__ __forceinline__ float2 elu2(float2 y) {
 
 // First node of the 48-node window that covers every neighbour of the 32
 // nodes owned by lane quarter q (nodes 32q .. 32q+31 have neighbours within
-// +-8); clamped to [0, 80] so the window stays inside the 128 columns.
-__device__ __forceinline__ int window_start(int q) { return q == 0 ? 0 : q == 3 ? 80 : 32 * q - 8; }
+// +-8); clamped to [0, 80] so the window stays inside the 128 nodes.  A
+// multiple of 8, so the window starts on a core-matrix row of Wh^h.
+__host__ __device__ constexpr int window_start(int q) { return q == 0 ? 0 : q == 3 ? 80 : 32 * q - 8; }
 
-
-// One group's four gathers of a layer, in head order: wait for head t's
-// request (e buffer and Wh^h staged), issue its eight K = 16 steps (8 columns
-// of e, two 8-row core-matrix groups of Wh), commit to done2.  Returns false
-// after an abort or a timed-out wait.
-__device__ __forceinline__ bool serve_gathers(int g, uint32_t tmem, uint64_t b2desc0, uint64_t* req, uint64_t* done2,
-                                              uint32_t (&rph)[2], volatile int* abort_flag) {
+// One issuing thread's half of the gather of one head: wait for the head's
+// request (e rows and Wh^h staged), then for lane quarters 2 * part and
+// 2 * part + 1 three K = 16 steps each over the quarter's 48-node window,
+// with the other quarters' output lanes disabled.  A (the e rows, fp16) is
+// in tensor memory relative to the window: row i holds
+// e[i][window_start(q) + k] in half-column k; B (Wh^h, fp16, N-contiguous)
+// starts at the window's first node.  Commits to done2 (two commits, one
+// per part, complete a phase).  Returns false after an abort or a timed-out
+// wait.
+__device__ __forceinline__ bool gather_half(int part, int l, int g, int t, uint32_t tmem, uint64_t b2desc0,
+                                            uint64_t* req, uint64_t* done2, uint32_t (&rph)[2][2],
+                                            volatile int* abort_flag) {
   constexpr uint32_t idesc2 = idesc_f16(0 /* fp16 */, 128, 32, 1 /* B N-contiguous */);
+  const int b = t & 1, ab = 2 * g + b;
+  if (!mbar_wait(&req[ab], rph[g][b] & 1, abort_flag, kWaitLimitNs)) return false;
+  ++rph[g][b];
+  tc_fence_after();
+  const uint32_t d = tmem + head_col(l, g, t);
+  const uint32_t a_col = tmem + kECol + (uint32_t)(ab * 24);
+  const uint64_t bd = b2desc0 + (uint64_t)(ab * (8192 >> 4));
 #pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    const int b = t & 1, ab = 2 * g + b;
-    if (!mbar_wait(&req[ab], rph[b] & 1, abort_flag, kWaitLimitNs)) return false;
-    ++rph[b];
-    tc_fence_after();
-    const uint32_t d = tmem + (uint32_t)(32 * (4 * g + t));
-    const uint32_t a_col = tmem + kAlphaCol + (uint32_t)(ab * 64);
-    const uint64_t bd = b2desc0 + (uint64_t)(ab * (8192 >> 4));
-    mma_f16_ts(d, a_col, bd, idesc2, 0);
+  for (int qq = 0; qq < 2; ++qq) {
+    const int q = 2 * part + qq;
+    const uint32_t mask[4] = {q == 0 ? 0u : ~0u, q == 1 ? 0u : ~0u, q == 2 ? 0u : ~0u, q == 3 ? 0u : ~0u};
+    const uint64_t bq = bd + (uint64_t)((window_start(q) / 8) * (512 >> 4));
 #pragma unroll
-    for (int kk = 1; kk < 8; ++kk) mma_f16_ts(d, a_col + kk * 8, bd + kk * (1024 >> 4), idesc2, 1);
-    mma_commit(&done2[ab]);
+    for (int j = 0; j < 3; ++j) mma_f16_ts_masked(d, a_col + 8 * j, bq + j * (1024 >> 4), idesc2, j != 0, mask);
   }
+  mma_commit(&done2[ab]);
   return true;
 }
 
@@ -241,14 +274,20 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
   uint64_t* bars = (uint64_t*)(smem + kSmBar);
   uint64_t* full = bars;
   uint64_t* empty = bars + kWSlots;
-  uint64_t* acc_full = bars + 2 * kWSlots;
-  uint64_t* x_ready = acc_full + 1;
+  // a layer's projection complete: scores (sc_full), first-half block
+  // (acc_a), second-half block (acc_b), committed in that order
+  uint64_t* sc_full = bars + 2 * kWSlots;
+  uint64_t* acc_a = sc_full + 1;
+  uint64_t* acc_b = sc_full + 2;
+  // x_ready[c]: K chunk c of the next X tile written (both groups' head c,
+  // c + 4; chunk 0 also marks a tile's encoded input)
+  uint64_t* x_ready = sc_full + 3;  // [4 chunks]
   // req / done2 per (group, buffer): a head's gather request and its
   // completion.  One barrier per buffer keeps every producer at most one
   // phase ahead of its consumer.
-  uint64_t* req = acc_full + 2;     // [2 groups][2 buffers]
-  uint64_t* done2 = acc_full + 6;   // [2 groups][2 buffers]
-  uint64_t* drain = acc_full + 10;  // [issuing thread]
+  uint64_t* req = sc_full + 7;      // [2 groups][2 buffers]
+  uint64_t* done2 = sc_full + 11;   // [2 groups][2 buffers]
+  uint64_t* drain = sc_full + 15;   // [issuing thread: gathers 0, gathers 1, projection]
   uint32_t* tmem_slot = (uint32_t*)(smem + kSmMisc);
   volatile int* abort_flag = (volatile int*)(smem + kSmMisc + 4);
 
@@ -264,14 +303,15 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(x_ready, kEpiWarps);
+    mbar_init(sc_full, 1);
+    mbar_init(acc_a, 1);
+    mbar_init(acc_b, 1);
     for (int i = 0; i < 4; ++i) {
+      mbar_init(&x_ready[i], kEpiWarps);
       mbar_init(&req[i], 4);
-      mbar_init(&done2[i], 1);
+      mbar_init(&done2[i], 2);
     }
-    mbar_init(&drain[0], 1);
-    mbar_init(&drain[1], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&drain[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -302,65 +342,130 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
         mbar_wait(&full[k % kWSlots], (k / kWSlots) & 1, abort_flag, kWaitLimitNs);
     }
     __syncwarp();
-  } else if (warp == kMmaWarp) {
-    // ---------------- MMA issuer ----------------
-    // One thread issues every MMA; its own instruction stream is on the
-    // critical path of the small gather MMAs, so descriptors are built once
+  } else if (warp == kMmaWarp || warp == kGatherWarp) {
+    // ---------------- gathers: two issuing threads ----------------
+    // Each thread issues half of every head's gather (lane quarters 0-1 or
+    // 2-3), both groups' heads in head order: a head's gather latency is
+    // bound by one thread's issue rate, so the halves run side by side.
+    if (lane == 0) {
+      const int part = warp - kMmaWarp;
+      const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
+      uint32_t rph[2][2] = {{0, 0}, {0, 0}};
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x)
+        for (int l = 0; l < kLayers && ok; ++l)
+          for (int t = 0; t < 4 && ok; ++t)
+            for (int g = 0; g < 2 && ok; ++g) ok = gather_half(part, l, g, t, tmem, b2desc0, req, done2, rph, abort_flag);
+      mma_commit(&drain[part]);
+      mbar_wait(&drain[part], 0, abort_flag, kWaitLimitNs);
+    }
+    __syncwarp();
+  } else if (warp == kProjWarp) {
+    // ---------------- projection and score MMAs ----------------
+    // Layer l + 1's projection is issued chunk by chunk under layer l's head
+    // loop, as the K chunks of X(l + 1) appear.  Descriptors are built once
     // and advanced by adding (byte offset >> 4) to the start-address field
     // (no carry out of the 14-bit field: shared addresses stay below 2^18).
     if (lane == 0) {
-      constexpr uint32_t idesc1 = idesc_f16(OpType<OpT>::fmt, 128, 256);
+      constexpr uint32_t idescH = idesc_f16(OpType<OpT>::fmt, 128, 128);
       constexpr uint32_t idesc_s = idesc_f16(OpType<OpT>::fmt, 128, 32);
       const uint64_t xdesc = sw128_desc(smem_u32(sX));
       const uint64_t wdesc0 = sw128_desc(smem_u32(sW));
-      const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
-      uint32_t q = 0, xph = 0, rph[2] = {0, 0};
+      uint32_t q = 0, xph[4] = {0, 0, 0, 0};
       bool ok = true;
+      auto wait_x = [&](int c) {
+        ok = ok && mbar_wait(&x_ready[c], xph[c] & 1, abort_flag, kWaitLimitNs);
+        ++xph[c];
+        tc_fence_after();
+      };
+      auto wait_w = [&](uint32_t k) {  // weight chunk k of the stream landed
+        ok = ok && mbar_wait(&full[k % kWSlots], (k / kWSlots) & 1, abort_flag, kWaitLimitNs);
+        tc_fence_after();
+      };
+      // K = 16 step kk of X chunk c against weight chunk k: N = 128 into
+      // `dcol` from weight rows 128 * half .., or the 32 score columns
+      auto proj = [&](uint32_t dcol, int half, int c, uint32_t k, int kk, bool first) {
+        const uint64_t xd = xdesc + (uint64_t)(c * (16384 >> 4) + kk * 2);
+        const uint64_t wd = wdesc0 + (uint64_t)((k % kWSlots) * (kWChunk >> 4) + kk * 2);
+        mma_f16_ss(tmem + dcol, xd, wd + (uint64_t)(half * (16384 >> 4)), idescH, !first);
+      };
+      auto score = [&](int c, uint32_t k, int kk, bool first) {
+        const uint64_t xd = xdesc + (uint64_t)(c * (16384 >> 4) + kk * 2);
+        const uint64_t wd = wdesc0 + (uint64_t)((k % kWSlots) * (kWChunk >> 4) + (kWScoreOff >> 4) + kk * 2);
+        mma_f16_ss(tmem + kScoreCol, xd, wd, idesc_s, !first);
+      };
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        for (int l = 0; l < kLayers && ok; ++l) {
-          ok = mbar_wait(x_ready, xph & 1, abort_flag, kWaitLimitNs);
-          ++xph;
+        // layer 0: the encoded features (K = 4, one K = 16 step)
+        wait_x(0);
+        wait_w(q);
+        if (!ok) break;
+        score(0, q, 0, true);
+        mma_commit(sc_full);
+        proj(128 * first_block(0), 0, 0, q, 0, true);
+        mma_commit(acc_a);
+        proj(128 * second_block(0), 1, 0, q, 0, true);
+        mma_commit(acc_b);
+        mma_commit(&empty[q % kWSlots]);
+        ++q;
+        for (int l = 1; l < kLayers && ok; ++l) {
+          // layer l from X(l), weight chunks q .. q + 3
+          const uint32_t fa = 128 * first_block(l), fb = 128 * second_block(l);
+          // chunk 0: first half + scores (the third block is free)
+          wait_x(0);
+          wait_w(q);
           if (!ok) break;
-          tc_fence_after();
-          const int nchunk = l == 0 ? 1 : 4;  // K chunks of 64 (layer 0: 4 features -> one K = 16 step)
-          for (int c = 0; c < nchunk && ok; ++c, ++q) {
-            const int s = q % kWSlots;
-            ok = mbar_wait(&full[s], (q / kWSlots) & 1, abort_flag, kWaitLimitNs);
-            if (!ok) break;
-            tc_fence_after();
-            const uint64_t xd = xdesc + (uint64_t)(c * (16384 >> 4)), wd = wdesc0 + (uint64_t)(s * (kWChunk >> 4));
-            mma_f16_ss(tmem, xd, wd, idesc1, c != 0);
-            mma_f16_ss(tmem + kScoreCol, xd, wd + (kWScoreOff >> 4), idesc_s, c != 0);
-            if (l != 0) {
 #pragma unroll
-              for (int kk = 1; kk < 4; ++kk) {  // K = 16 per MMA: 32 bytes along the swizzled row
-                mma_f16_ss(tmem, xd + kk * 2, wd + kk * 2, idesc1, 1);
-                mma_f16_ss(tmem + kScoreCol, xd + kk * 2, wd + (kWScoreOff >> 4) + kk * 2, idesc_s, 1);
-              }
-            }
-            mma_commit(&empty[s]);
+          for (int kk = 0; kk < 4; ++kk) {
+            proj(fa, 0, 0, q, kk, kk == 0);
+            score(0, q, kk, kk == 0);
           }
+          // chunk 1: first half + scores; the second half of chunks 0 and 1
+          // (layer l-1's first-half block is free: heads 0, 1, 4, 5 done)
+          wait_x(1);
+          wait_w(q + 1);
           if (!ok) break;
-          mma_commit(acc_full);
-          ok = serve_gathers(0, tmem, b2desc0, req, done2, rph, abort_flag);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            proj(fa, 0, 1, q + 1, kk, false);
+            score(1, q + 1, kk, false);
+          }
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fb, 1, 0, q, kk, kk == 0);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fb, 1, 1, q + 1, kk, false);
+          mma_commit(&empty[q % kWSlots]);
+          mma_commit(&empty[(q + 1) % kWSlots]);
+          // chunk 2: everything
+          wait_x(2);
+          wait_w(q + 2);
+          if (!ok) break;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            proj(fa, 0, 2, q + 2, kk, false);
+            score(2, q + 2, kk, false);
+            proj(fb, 1, 2, q + 2, kk, false);
+          }
+          mma_commit(&empty[(q + 2) % kWSlots]);
+          // chunk 3: scores first (the epilogue starts on them), then the
+          // first half, then the second, each committed on its own barrier
+          wait_x(3);
+          wait_w(q + 3);
+          if (!ok) break;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) score(3, q + 3, kk, false);
+          mma_commit(sc_full);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fa, 0, 3, q + 3, kk, false);
+          mma_commit(acc_a);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fb, 1, 3, q + 3, kk, false);
+          mma_commit(acc_b);
+          mma_commit(&empty[(q + 3) % kWSlots]);
+          q += 4;
         }
       }
-      mma_commit(&drain[0]);
-      mbar_wait(&drain[0], 0, abort_flag, kWaitLimitNs);
-    }
-    __syncwarp();
-  } else if (warp == kGatherWarp) {
-    // ---------------- group 1's gathers ----------------
-    // A second issuing thread, so the two groups' gather chains overlap in
-    // the tensor pipe (each chain is bound by one thread's issue rate).
-    if (lane == 0) {
-      const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
-      uint32_t rph[2] = {0, 0};
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x)
-        for (int l = 0; l < kLayers && ok; ++l) ok = serve_gathers(1, tmem, b2desc0, req, done2, rph, abort_flag);
-      mma_commit(&drain[1]);
-      mbar_wait(&drain[1], 0, abort_flag, kWaitLimitNs);
+      mma_commit(&drain[2]);
+      mbar_wait(&drain[2], 0, abort_flag, kWaitLimitNs);
     }
     __syncwarp();
   } else {
@@ -391,13 +496,6 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
     bool ok = true;    // collective: changes only through epilogue_all
     bool wok = true;   // this thread's waits inside a layer; folded into the next vote
 
-    // zero this warp's lanes of both e buffers of its group (static background)
-    {
-      uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int b = 0; b < 2; ++b)
-        for (int c = 0; c < 64; c += 8) tmem_st_x8(tlane + kAlphaCol + (2 * g + b) * 64 + c, z);
-      tmem_st_wait();
-    }
 
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       // -- encode the tile's positions into X chunk 0 (features 0..15) --
@@ -416,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(x_ready);
+      if (lane == 0) mbar_arrive(&x_ready[0]);
 
       // One layer.  `last` is a compile-time flag, so the last layer's head
       // code does not share registers with the head loop of the others.
@@ -425,9 +523,9 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
         // per-layer bias into shared memory, by layer parity
         float* vec = (float*)(smem + kSmVec) + (l & 1) * kVecFloats;
         vec[threadIdx.x] = __ldg(p.w + C4Off::b(l) + threadIdx.x);
-        wok = mbar_wait(acc_full, aph & 1, abort_flag, kWaitLimitNs) && wok;
+        const uint32_t lph = aph++ & 1;  // phase of this layer's sc_full / acc_a / acc_b
+        wok = mbar_wait(sc_full, lph, abort_flag, kWaitLimitNs) && wok;
         ok = epilogue_all(wok);  // also publishes vec
-        ++aph;
         if (!ok) return false;
         tc_fence_after();
 
@@ -446,12 +544,6 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
         tc_fence_before();
         named_bar_sync(1, kEpiWarps * 32);  // t scores visible; score columns read by everyone
         tc_fence_after();
-        if (g == 0) {  // restore the zero background of e buffer (0, 1) under the score columns
-          uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-          for (int c = 0; c < 32; c += 8) tmem_st_x8(tlane + kScoreCol + c, z);
-          tmem_st_wait();
-        }
         float4 tn[9];
 #pragma unroll
         for (int k = 0; k < 9; ++k) tn[k] = tsc[nidx[k]];
@@ -475,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           ++dph[b];
           tc_fence_after();
           float o[32];
-          tmem_ld_x32(tlane + (uint32_t)(32 * h), o);
+          tmem_ld_x32(tlane + head_col(l, g, t), o);
           tmem_ld_wait();
           const float4* bias4 = (const float4*)(vec + 32 * h);
           const float2 iv = make_float2(inv[t], inv[t]);
@@ -488,16 +580,22 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           }
           if constexpr (!last) {
             // the next layer's operand, stochastically rounded (see round_seed)
+            // K chunk t of the next X tile holds heads t (units 0-3) and
+            // t + 4 (units 4-7)
             const uint32_t seed = round_seed(li, l, h);
-            uint8_t* xrow = sX + (h >> 1) * 16384 + (i >> 3) * 1024 + (i & 7) * 128;
+            uint8_t* xrow = sX + t * 16384 + (i >> 3) * 1024 + (i & 7) * 128;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-              const int unit = (4 * (h & 1) + u) ^ (i & 7);
+              const int unit = (4 * g + u) ^ (i & 7);
               uint32_t q[4];
 #pragma unroll
               for (int m = 0; m < 4; ++m) q[m] = OpType<OpT>::pack_sr(y[4 * u + m].x, y[4 * u + m].y, seed ^ pair_mix(4 * u + m));
               *(uint4*)(xrow + unit * 16) = make_uint4(q[0], q[1], q[2], q[3]);
             }
+            fence_proxy_async_smem();  // X writes -> the next projection's async proxy
+            tc_fence_before();         // this head's tensor-memory reads precede the block's reuse
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&x_ready[t]);
           } else {
             // fp32 rows of this head into scratch, then per-position pooling
 #pragma unroll
@@ -544,9 +642,13 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
         for (int t = 0; t < 4; ++t) {
           const int h = 4 * g + t, b = t & 1;
           // ---- P1: Wh^h (fp32) -> fp16 copy as the gather's B operand ----
+          if (t == 0 || t == 2) {  // the block of heads t, t + 1 is complete
+            wok = mbar_wait(t == 0 ? acc_a : acc_b, lph, abort_flag, kWaitLimitNs) && wok;
+            tc_fence_after();
+          }
           {
             float wh[32];
-            tmem_ld_x32(tlane + (uint32_t)(32 * h), wh);
+            tmem_ld_x32(tlane + head_col(l, g, t), wh);
             tmem_ld_wait();
             // N-contiguous without swizzle: node i's 8-feature group ng at
             // ng * 128 + (i / 8) * 512 + (i % 8) * 16
@@ -588,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
               a[4 * k + 2] = v.z;
               a[4 * k + 3] = v.w;
             }
-            const uint32_t acol = tlane + kAlphaCol + (uint32_t)((2 * g + b) * 64 + (jw0 >> 1));
+            const uint32_t acol = tlane + kECol + (uint32_t)((2 * g + b) * 24);
             tmem_st_x8(acol, *(const uint32_t(*)[8])(a));
             tmem_st_x8(acol + 8, *(const uint32_t(*)[8])(a + 8));
             tmem_st_x8(acol + 16, *(const uint32_t(*)[8])(a + 16));
@@ -602,12 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           if (t >= 1) finish_head(t - 1);
         }
         finish_head(3);
-        if constexpr (!last) {
-          fence_proxy_async_smem();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(x_ready);
-        } else {
+        if constexpr (last) {
           // ---------------- heads (fp32) ----------------
           float* zpart = (float*)(smem + kSmZ);
           float* lgpart = (float*)(smem + kSmLogit);
@@ -668,10 +765,15 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
 }
 
 // ---- weight packing: 36 KB chunks [288 rows][64 K], 128-byte swizzled ----
-// Rows 0..255: W_l^T (feature f, K).  Rows 256..287: the attention-score
-// weights W_l a_l^h: row 256 + 2h + v holds the bf16/fp16 rounding of
-// sum_f W_l[k][32h + f] a_l[h][v][f] (v = 0 self, 1 neighbour), row 272 + 2h + v
-// the rounding of what is left over.
+// Rows 0..255: W_l^T in the order the accumulator blocks hold the output
+// features: rows 32 s .. 32 s + 31 are head (0, 4, 1, 5, 2, 6, 3, 7)[s].
+// Rows 256..287: the attention-score weights W_l a_l^h: row 256 + 2h + v
+// holds the bf16/fp16 rounding of sum_f W_l[k][32h + f] a_l[h][v][f]
+// (v = 0 self, 1 neighbour), row 272 + 2h + v the rounding of what is left
+// over.  K (layers 1..5): chunk c holds the input features of heads c and
+// c + 4 (the layer before writes them as its heads finish).
+__host__ __device__ constexpr int packed_row_head(int s) { return 4 * (s & 1) + (s >> 1); }
+
 template <typename OpT>
 __global__ void pack_c4_kernel(const float* __restrict__ w, uint8_t* __restrict__ out) {
   const int chunk = blockIdx.x;  // 0 .. kChunksPerTile-1
@@ -681,15 +783,18 @@ __global__ void pack_c4_kernel(const float* __restrict__ w, uint8_t* __restrict_
   const float* W = w + C4Off::W(layer);
   const float* A = w + C4Off::a(layer);
   uint8_t* dst = out + (size_t)chunk * kWChunk;
+  // input feature of K position kk of this chunk
+  auto kin = [&](int kk) { return layer == 0 ? kk : 32 * (4 * (kk >> 5) + c) + (kk & 31); };
   for (int t = threadIdx.x; t < 256 * 64; t += blockDim.x) {
-    const int f = t / 64, kk = t % 64;  // feature row, K within chunk
-    const int k = c * 64 + kk;
+    const int r = t / 64, kk = t % 64;  // packed row, K within chunk
+    const int f = 32 * packed_row_head(r >> 5) + (r & 31);
+    const int k = kin(kk);
     const float x = k < fin ? W[(size_t)k * kHidden + f] : 0.f;
-    *(uint16_t*)(dst + sw128_offset(f, kk)) = OpType<OpT>::bits(x);
+    *(uint16_t*)(dst + sw128_offset(r, kk)) = OpType<OpT>::bits(x);
   }
   for (int t = threadIdx.x; t < 16 * 64; t += blockDim.x) {
     const int j = t / 64, kk = t % 64;  // score column j = 2h + v
-    const int k = c * 64 + kk, h = j >> 1, v = j & 1;
+    const int k = kin(kk), h = j >> 1, v = j & 1;
     float acc = 0.f;
     if (k < fin)
       for (int f = 0; f < 32; ++f) acc = fmaf(W[(size_t)k * kHidden + 32 * h + f], A[(2 * h + v) * 32 + f], acc);

@@ -235,6 +235,17 @@ __device__ __forceinline__ void mma_f16_ss_masked(uint32_t d_tmem, uint64_t a_de
       : "memory");
 }
 
+// The same with A in tensor memory.
+__device__ __forceinline__ void mma_f16_ts_masked(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate, const uint32_t (&mask)[4]) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(mask[0]), "r"(mask[1]), "r"(mask[2]), "r"(mask[3])
+      : "memory");
+}
+
 // Instruction descriptor for kind::f16: fp32 accumulator, operands of format
 // `fmt` (0 = fp16, 1 = bf16), shape M x N; A K-major, B K-major unless
 // b_mn_major (then B is stored N-contiguous).
