@@ -15,9 +15,9 @@
 //      softmax  e_ij = exp(LeakyReLU_0.2(s_i + t_j) - max_j), z_i = sum_j e_ij
 //               over the 8-neighbourhood + self of node i (the Connect4 board
 //               graph); e (fp16, unnormalised) goes into tensor memory, each
-//               lane quarter's rows relative to the 48-node window that holds
-//               all their neighbours
-//      gather   out^h = e^h . Wh^h   as a second tcgen05.mma per lane quarter
+//               position's rows relative to a 48-node window that holds the
+//               position (neighbours never cross positions)
+//      gather   out^h = e^h . Wh^h   as a second tcgen05.mma per position
 //               (three K = 16 steps over the window, other lanes disabled):
 //               e^h is the A operand in tensor memory, Wh^h (fp16) the B
 //               operand in shared memory; the result overwrites the head's
@@ -34,8 +34,8 @@
 // Weights are pre-packed on the device into 36 KB chunks (256 projection rows
 // + 32 score rows, 64 K each, swizzled) and streamed into a two-slot
 // shared-memory ring by one producer thread with 1-D bulk async copies (TMA
-// engine).  Three threads issue MMAs: one the projections, two the gathers
-// (each half of every head's lane quarters).  Every wait is bounded
+// engine).  Three threads issue MMAs: one the projections, one each group's
+// gathers.  Every wait is bounded
 // (%globaltimer); on a timeout the CTA drains its copies and MMAs, frees
 // tensor memory and reports through the error word.
 //
@@ -212,39 +212,44 @@ __device__ __forceinline__ float2 elu2(float2 y) {
   return make_float2(fmaxf(em.x, y.x), fmaxf(em.y, y.y));
 }
 
-// First node of the 48-node window that covers every neighbour of the 32
-// nodes owned by lane quarter q (nodes 32q .. 32q+31 have neighbours within
-// +-8); clamped to [0, 80] so the window stays inside the 128 nodes.  A
-// multiple of 8, so the window starts on a core-matrix row of Wh^h.
-__host__ __device__ constexpr int window_start(int q) { return q == 0 ? 0 : q == 3 ? 80 : 32 * q - 8; }
+// The e rows of a tile's position p live in tensor memory relative to the
+// 48-node window that starts at node window_start(p) (a multiple of 8, so on
+// a core-matrix row of Wh^h) and holds the position's 42 nodes: neighbours
+// never cross positions.  The padding rows 126, 127 go with position 2.
+__host__ __device__ constexpr int window_start(int p) { return p == 0 ? 0 : p == 1 ? 40 : 80; }
+__host__ __device__ constexpr int row_position(int i) { return i < kN ? 0 : i < 2 * kN ? 1 : 2; }
+// disable-output-lane mask word w of position p: bit set = lane not p's
+__host__ __device__ constexpr uint32_t position_mask(int p, int w) {
+  uint32_t m = 0;
+  for (int b = 0; b < 32; ++b) m |= (row_position(32 * w + b) != p ? 1u : 0u) << b;
+  return m;
+}
 
-// One issuing thread's half of the gather of one head: wait for the head's
-// request (e rows and Wh^h staged), then for lane quarters 2 * part and
-// 2 * part + 1 three K = 16 steps each over the quarter's 48-node window,
-// with the other quarters' output lanes disabled.  A (the e rows, fp16) is
-// in tensor memory relative to the window: row i holds
-// e[i][window_start(q) + k] in half-column k; B (Wh^h, fp16, N-contiguous)
-// starts at the window's first node.  Commits to done2 (two commits, one
-// per part, complete a phase).  Returns false after an abort or a timed-out
-// wait.
-__device__ __forceinline__ bool gather_half(int part, int l, int g, int t, uint32_t tmem, uint64_t b2desc0,
-                                            uint64_t* req, uint64_t* done2, uint32_t (&rph)[2][2],
-                                            volatile int* abort_flag) {
+// The gather of one head: wait for its request (e rows and Wh^h staged),
+// then per position p three K = 16 steps over the position's window, with
+// the other positions' output lanes disabled.  A is the e buffer (row i
+// holds e[i][window_start(p) + k] in half-column k), B is Wh^h (fp16,
+// N-contiguous) from the window's first node.  Commits to done2.  Returns
+// false after an abort or a timed-out wait.
+__device__ __forceinline__ bool gather_head(int l, int g, int t, uint32_t tmem, uint64_t b2desc0, uint64_t* req,
+                                            uint64_t* done2, uint32_t (&rph)[2], volatile int* abort_flag) {
   constexpr uint32_t idesc2 = idesc_f16(0 /* fp16 */, 128, 32, 1 /* B N-contiguous */);
   const int b = t & 1, ab = 2 * g + b;
-  if (!mbar_wait(&req[ab], rph[g][b] & 1, abort_flag, kWaitLimitNs)) return false;
-  ++rph[g][b];
+  if (!mbar_wait(&req[ab], rph[b] & 1, abort_flag, kWaitLimitNs)) return false;
+  ++rph[b];
   tc_fence_after();
   const uint32_t d = tmem + head_col(l, g, t);
   const uint32_t a_col = tmem + kECol + (uint32_t)(ab * 24);
   const uint64_t bd = b2desc0 + (uint64_t)(ab * (8192 >> 4));
 #pragma unroll
-  for (int qq = 0; qq < 2; ++qq) {
-    const int q = 2 * part + qq;
-    const uint32_t mask[4] = {q == 0 ? 0u : ~0u, q == 1 ? 0u : ~0u, q == 2 ? 0u : ~0u, q == 3 ? 0u : ~0u};
-    const uint64_t bq = bd + (uint64_t)((window_start(q) / 8) * (512 >> 4));
+  for (int p = 0; p < kGPT; ++p) {
+    constexpr uint32_t kMasks[kGPT][4] = {
+        {position_mask(0, 0), position_mask(0, 1), position_mask(0, 2), position_mask(0, 3)},
+        {position_mask(1, 0), position_mask(1, 1), position_mask(1, 2), position_mask(1, 3)},
+        {position_mask(2, 0), position_mask(2, 1), position_mask(2, 2), position_mask(2, 3)}};
+    const uint64_t bp = bd + (uint64_t)((window_start(p) / 8) * (512 >> 4));
 #pragma unroll
-    for (int j = 0; j < 3; ++j) mma_f16_ts_masked(d, a_col + 8 * j, bq + j * (1024 >> 4), idesc2, j != 0, mask);
+    for (int j = 0; j < 3; ++j) mma_f16_ts_masked(d, a_col + 8 * j, bp + j * (1024 >> 4), idesc2, j != 0, kMasks[p]);
   }
   mma_commit(&done2[ab]);
   return true;
@@ -309,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
     for (int i = 0; i < 4; ++i) {
       mbar_init(&x_ready[i], kEpiWarps);
       mbar_init(&req[i], 4);
-      mbar_init(&done2[i], 2);
+      mbar_init(&done2[i], 1);
     }
     for (int i = 0; i < 3; ++i) mbar_init(&drain[i], 1);
     *abort_flag = 0;
@@ -343,21 +348,19 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
     }
     __syncwarp();
   } else if (warp == kMmaWarp || warp == kGatherWarp) {
-    // ---------------- gathers: two issuing threads ----------------
-    // Each thread issues half of every head's gather (lane quarters 0-1 or
-    // 2-3), both groups' heads in head order: a head's gather latency is
-    // bound by one thread's issue rate, so the halves run side by side.
+    // ---------------- gathers: one issuing thread per group ----------------
+    // A head's gather latency is bound by its thread's issue rate, so the
+    // two groups' chains run side by side.
     if (lane == 0) {
-      const int part = warp - kMmaWarp;
+      const int g = warp - kMmaWarp;
       const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
-      uint32_t rph[2][2] = {{0, 0}, {0, 0}};
+      uint32_t rph[2] = {0, 0};
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x)
         for (int l = 0; l < kLayers && ok; ++l)
-          for (int t = 0; t < 4 && ok; ++t)
-            for (int g = 0; g < 2 && ok; ++g) ok = gather_half(part, l, g, t, tmem, b2desc0, req, done2, rph, abort_flag);
-      mma_commit(&drain[part]);
-      mbar_wait(&drain[part], 0, abort_flag, kWaitLimitNs);
+          for (int t = 0; t < 4 && ok; ++t) ok = gather_head(l, g, t, tmem, b2desc0, req, done2, rph, abort_flag);
+      mma_commit(&drain[g]);
+      mbar_wait(&drain[g], 0, abort_flag, kWaitLimitNs);
     }
     __syncwarp();
   } else if (warp == kProjWarp) {
@@ -475,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
     const uint32_t tlane = tmem + ((uint32_t)(32 * qd) << 16);
     const int li = i % kN, rr = li / 7, cc = li % 7;
     const bool real = i < kGPT * kN;
-    const int jw0 = window_start(qd);
+    const int jw0 = window_start(row_position(i));
     uint8_t* srow = smem + kSmStage + (g * 128 + i) * kStageStride;
     const float4* tsc = (const float4*)(smem + kSmTsc) + g * 129;
     // node i's 3x3 stencil: the t-score row of each neighbour (128 = none,
