@@ -75,7 +75,7 @@ _SIGS = {
     "gz_net_save_weights": (C.c_int, [_vp, _f32p, C.c_size_t]),
     "gz_net_predict_batch": (C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp, _vp]),
     "gz_net_check": (C.c_int, [_vp]),
-    "gz_net_predict_host": (C.c_int, [_vp, _i8p, _i8p, C.c_int, _f32p, _f32p]),
+    "gz_net_predict_host": (C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp]),  # raw addresses: the per-step call
     "gz_net_predict": (C.c_int, [_vp, _f32p, _f32p, _f32p]),
     "gz_net_broadcast": (C.c_int, [_vp, _vp, C.c_int, _vp]),
     "gz_net_save_checkpoint": (C.c_int, [_vp, C.c_char_p]),
@@ -306,14 +306,24 @@ class Net:
         """Raise if a bounded wait inside a forward kernel gave up."""
         _check(_lib.gz_net_check(self._h))
 
-    def predict_host(self, boards: np.ndarray, side: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    def predict_host(self, boards: np.ndarray, side: np.ndarray,
+                     out: tuple[np.ndarray, np.ndarray] | None = None) -> tuple[np.ndarray, np.ndarray]:
+        """Host buffers in, host buffers out (synchronous).  `out` = (pi, v)
+        reuses caller arrays (float32, C-contiguous, [n][actions] and [n]);
+        page-locked arrays (see `pinned_empty`) are transferred directly."""
         boards = np.ascontiguousarray(boards, np.int8)
         side = np.ascontiguousarray(side, np.int8)
         n = side.shape[0]
-        pi = np.empty((n, self.shape.actions), np.float32)
-        v = np.empty(n, np.float32)
-        _check(_lib.gz_net_predict_host(self._h, _ptr(boards, C.c_int8), _ptr(side, C.c_int8), n,
-                                        _ptr(pi, C.c_float), _ptr(v, C.c_float)))
+        if out is None:
+            pi = np.empty((n, self.shape.actions), np.float32)
+            v = np.empty(n, np.float32)
+        else:
+            pi, v = out
+            if (pi.dtype != np.float32 or v.dtype != np.float32 or not pi.flags.c_contiguous
+                    or not v.flags.c_contiguous or pi.size < n * self.shape.actions or v.size < n):
+                raise ValueError("out must be float32 C-contiguous arrays of at least [n][actions] and [n]")
+        _check(_lib.gz_net_predict_host(self._h, boards.ctypes.data, side.ctypes.data, n, pi.ctypes.data,
+                                        v.ctypes.data))
         return pi, v
 
     def predict(self, canonical_board: np.ndarray) -> tuple[np.ndarray, float]:

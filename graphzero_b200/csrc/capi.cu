@@ -114,6 +114,10 @@ struct gz_net {
   int8_t *h_in = nullptr, *d_in = nullptr;
   float *h_out = nullptr, *d_out = nullptr;
   cudaStream_t stream = nullptr;
+  // host calls: a copy stream beside `stream`, and per half of a split call
+  // the events "inputs copied", "forward done", "outputs copied"
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_fwd[2] = {nullptr, nullptr}, ev_out[2] = {nullptr, nullptr};
 };
 
 struct gz_mcts {
@@ -347,6 +351,12 @@ gz_status gz_net_create(const gz_net_config* cfg, int device, gz_net** out) {
   chk(cudaMallocHost(&n->h_out, (out_floats + 1) * sizeof(float)), "cudaMallocHost out");
   chk(cudaMalloc(&n->d_out, out_floats * sizeof(float)), "cudaMalloc out");
   chk(cudaStreamCreateWithFlags(&n->stream, cudaStreamNonBlocking), "stream");
+  chk(cudaStreamCreateWithFlags(&n->copy_stream, cudaStreamNonBlocking), "copy stream");
+  for (int h = 0; h < 2; ++h) {
+    chk(cudaEventCreateWithFlags(&n->ev_in[h], cudaEventDisableTiming), "event");
+    chk(cudaEventCreateWithFlags(&n->ev_fwd[h], cudaEventDisableTiming), "event");
+    chk(cudaEventCreateWithFlags(&n->ev_out[h], cudaEventDisableTiming), "event");
+  }
   if (st == GZ_OK) {
     gz_status p = prepare_weights(n, n->stream);
     if (p != GZ_OK) st = p;
@@ -364,6 +374,7 @@ gz_status gz_net_destroy(gz_net* n) {
   if (!n) return GZ_OK;
   DeviceGuard g(n->device);
   if (n->stream) cudaStreamSynchronize(n->stream);
+  if (n->copy_stream) cudaStreamSynchronize(n->copy_stream);
   cudaFree(n->d_weights);
   cudaFree(n->d_csr);
   cudaFree(n->d_tc);
@@ -373,6 +384,12 @@ gz_status gz_net_destroy(gz_net* n) {
   cudaFreeHost(n->h_out);
   cudaFree(n->d_out);
   if (n->stream) cudaStreamDestroy(n->stream);
+  if (n->copy_stream) cudaStreamDestroy(n->copy_stream);
+  for (int h = 0; h < 2; ++h) {
+    if (n->ev_in[h]) cudaEventDestroy(n->ev_in[h]);
+    if (n->ev_fwd[h]) cudaEventDestroy(n->ev_fwd[h]);
+    if (n->ev_out[h]) cudaEventDestroy(n->ev_out[h]);
+  }
   delete n;
   return GZ_OK;
 }
@@ -491,6 +508,20 @@ gz_status gz_net_check(gz_net* n) {
   return forward_error(n, err);
 }
 
+namespace {
+// Page-locked host memory (cudaHostAlloc / cudaHostRegister): the copy
+// engines read and write it directly.
+bool page_locked(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+constexpr int kSplitMin = 1024;  // host calls at least this large run as two overlapped halves
+}  // namespace
+
 gz_status gz_net_predict_host(gz_net* n, const int8_t* boards, const int8_t* side, int count, float* pi, float* v) {
   if (!n) return fail(GZ_ERR_INVALID_ARG, "null net");
   if (count < 0 || count > n->max_batch) return fail(GZ_ERR_INVALID_ARG, "batch %d outside [0, %d]", count, n->max_batch);
@@ -498,25 +529,82 @@ gz_status gz_net_predict_host(gz_net* n, const int8_t* boards, const int8_t* sid
   if (!boards || !side || !pi || !v) return fail(GZ_ERR_INVALID_ARG, "null buffer");
   GZ_DEVICE(n->device);
   GameShape s = game_shape(n->game);
-  size_t bb = (size_t)count * s.board_bytes;
-  memcpy(n->h_in, boards, bb);
-  memcpy(n->h_in + bb, side, (size_t)count);
-  GZ_CUDA(cudaMemcpyAsync(n->d_in, n->h_in, bb + count, cudaMemcpyHostToDevice, n->stream));
+  const size_t bb = (size_t)count * s.board_bytes;
+  int8_t* d_boards = n->d_in;
+  int8_t* d_side = n->d_in + bb;
   float* d_pi = n->d_out;
   float* d_v = n->d_out + (size_t)count * s.actions;
-  gz_status st = run_forward(n, n->d_in, n->d_in + bb, count, d_pi, d_v, n->stream);
-  if (st != GZ_OK) return st;
-  size_t outf = (size_t)count * (s.actions + 1);
-  GZ_CUDA(cudaMemcpyAsync(n->h_out, n->d_out, outf * sizeof(float), cudaMemcpyDeviceToHost, n->stream));
-  // the error word rides in the same stream (no second round trip)
+  // the error word rides in the same stream as the outputs (no second round trip)
   int* h_err = (int*)(n->h_out + (size_t)n->max_batch * (s.actions + 1));
-  GZ_CUDA(cudaMemcpyAsync(h_err, n->d_err, sizeof(int), cudaMemcpyDeviceToHost, n->stream));
-  GZ_CUDA(cudaStreamSynchronize(n->stream));
-  gz_status chk_st = forward_error(n, *h_err);
-  if (chk_st != GZ_OK) return chk_st;
-  memcpy(pi, n->h_out, (size_t)count * s.actions * sizeof(float));
-  memcpy(v, n->h_out + (size_t)count * s.actions, (size_t)count * sizeof(float));
-  return GZ_OK;
+
+  // A large call runs as two halves: inputs on the copy stream, forward
+  // passes on the compute stream, outputs back on the copy stream once each
+  // half's forward pass is done, so that one half's transfers (and, for
+  // pageable caller buffers, host copies) overlap the other half's forward
+  // pass.  The split point is a multiple of 6, so every position keeps its
+  // slot in the kernels' tiles (2 or 3 positions each) and the results are
+  // the unsplit call's bit for bit.
+  const int halves = count >= kSplitMin ? 2 : 1;
+  const int first[3] = {0, halves == 2 ? count / 2 / 6 * 6 : count, count};
+  auto issue = [&](const int8_t* src_b, const int8_t* src_s, int h) -> gz_status {
+    const size_t lo = first[h], m = first[h + 1] - first[h];
+    GZ_CUDA(cudaMemcpyAsync(d_boards + lo * s.board_bytes, src_b + lo * s.board_bytes, m * s.board_bytes,
+                            cudaMemcpyHostToDevice, n->copy_stream));
+    GZ_CUDA(cudaMemcpyAsync(d_side + lo, src_s + lo, m, cudaMemcpyHostToDevice, n->copy_stream));
+    GZ_CUDA(cudaEventRecord(n->ev_in[h], n->copy_stream));
+    GZ_CUDA(cudaStreamWaitEvent(n->stream, n->ev_in[h], 0));
+    gz_status st = run_forward(n, d_boards + lo * s.board_bytes, d_side + lo, (int)m, d_pi + lo * s.actions, d_v + lo,
+                               n->stream);
+    if (st != GZ_OK) {
+      cudaStreamSynchronize(n->copy_stream);  // no copy left reading the caller's or the staging buffers
+      return st;
+    }
+    GZ_CUDA(cudaEventRecord(n->ev_fwd[h], n->stream));
+    return GZ_OK;
+  };
+  auto collect = [&](float* dst_pi, float* dst_v, int h) -> gz_status {
+    const size_t lo = first[h], m = first[h + 1] - first[h];
+    GZ_CUDA(cudaStreamWaitEvent(n->copy_stream, n->ev_fwd[h], 0));
+    GZ_CUDA(cudaMemcpyAsync(dst_pi + lo * s.actions, d_pi + lo * s.actions, m * s.actions * sizeof(float),
+                            cudaMemcpyDeviceToHost, n->copy_stream));
+    GZ_CUDA(cudaMemcpyAsync(dst_v + lo, d_v + lo, m * sizeof(float), cudaMemcpyDeviceToHost, n->copy_stream));
+    if (h == halves - 1) GZ_CUDA(cudaMemcpyAsync(h_err, n->d_err, sizeof(int), cudaMemcpyDeviceToHost, n->copy_stream));
+    GZ_CUDA(cudaEventRecord(n->ev_out[h], n->copy_stream));
+    return GZ_OK;
+  };
+
+  if (page_locked(boards) && page_locked(side) && page_locked(pi) && page_locked(v)) {
+    // caller buffers are page-locked: the copy engines read and write them directly
+    for (int h = 0; h < halves; ++h)
+      if (gz_status st = issue(boards, side, h); st != GZ_OK) return st;
+    for (int h = 0; h < halves; ++h)
+      if (gz_status st = collect(pi, v, h); st != GZ_OK) return st;
+    GZ_CUDA(cudaStreamSynchronize(n->copy_stream));
+    return forward_error(n, *h_err);
+  }
+
+  // Pageable caller buffers go through the page-locked staging buffers; the
+  // host copies of one half overlap the other half's transfers and forward
+  // pass.
+  int8_t* h_boards = n->h_in;
+  int8_t* h_side = n->h_in + bb;
+  float* h_pi = n->h_out;
+  float* h_v = n->h_out + (size_t)count * s.actions;
+  for (int h = 0; h < halves; ++h) {
+    const size_t lo = first[h], m = first[h + 1] - first[h];
+    memcpy(h_boards + lo * s.board_bytes, boards + lo * s.board_bytes, m * s.board_bytes);
+    memcpy(h_side + lo, side + lo, m);
+    if (gz_status st = issue(h_boards, h_side, h); st != GZ_OK) return st;
+  }
+  for (int h = 0; h < halves; ++h)
+    if (gz_status st = collect(h_pi, h_v, h); st != GZ_OK) return st;
+  for (int h = 0; h < halves; ++h) {
+    const size_t lo = first[h], m = first[h + 1] - first[h];
+    GZ_CUDA(cudaEventSynchronize(n->ev_out[h]));
+    memcpy(pi + lo * s.actions, h_pi + lo * s.actions, m * s.actions * sizeof(float));
+    memcpy(v + lo, h_v + lo, m * sizeof(float));
+  }
+  return forward_error(n, *h_err);
 }
 
 gz_status gz_net_predict(gz_net* n, const float* h_board, float* h_pi, float* h_v) {

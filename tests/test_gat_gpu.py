@@ -126,6 +126,29 @@ def test_host_call_matches_device_call(cuda):
         net.predict_host(np.zeros((301, 42), np.int8), np.ones(301, np.int8))
 
 
+@pytest.mark.parametrize("game,n", [(gz.CONNECT4, 4096), (gz.CONNECT4, 1023), (gz.CHESS, 1500)])
+def test_host_call_routes_agree(cuda, game, n):
+    """The three routes of the host call give the device call's results:
+    pageable buffers in one piece (n < 1024) or as two overlapped halves,
+    and page-locked buffers copied directly (outputs reused via out=)."""
+    net = gz.Net(game, max_batch=n)
+    net.load_weights(gz.synth_weights(game, seed=5))
+    boards, side = gz.synth_positions(game, n, seed=6)
+    p_dev, v_dev = run(net, boards, side)
+    p1, v1 = net.predict_host(boards, side)
+    pin_b = torch.empty(boards.shape, dtype=torch.int8, pin_memory=True).numpy()
+    pin_s = torch.empty(side.shape, dtype=torch.int8, pin_memory=True).numpy()
+    pin_b[:] = boards
+    pin_s[:] = side
+    pi = torch.full(p1.shape, float("nan"), pin_memory=True).numpy()
+    v = torch.full(v1.shape, float("nan"), pin_memory=True).numpy()
+    p2, v2 = net.predict_host(pin_b, pin_s, out=(pi, v))
+    assert p2 is pi and v2 is v
+    for p, vv in ((p1, v1), (p2, v2)):
+        assert (p == p_dev).all() and (vv == v_dev).all()
+    net.check()
+
+
 def test_single_position_predict_uses_canonical_board(cuda):
     """INeuralNet::predict takes one canonical float board."""
     w = sharpen(gz.CONNECT4, gz.synth_weights(gz.CONNECT4, seed=5, bias_scale=0.3))
