@@ -95,6 +95,7 @@ __host__ __device__ constexpr uint32_t head_col(int l, int g, int t) {
 static_assert(first_block(kLayers) == first_block(0) && second_block(kLayers) == second_block(0), "rotation period");
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s per wait
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 
 // Shared memory map (bytes).
 constexpr int kStageStride = 112;                       // bytes per staging row (24 used words + pad)
@@ -204,12 +205,15 @@ __device__ __forceinline__ float comp(const float4& v, int k) {
   return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
 }
 
-// ELU of two values: max(2^(-|y| log2 e) - 1, y) equals y for y > 0 and
-// e^y - 1 otherwise (e^y - 1 >= y everywhere), with no select.
-__device__ __forceinline__ float2 elu2(float2 y) {
-  const float2 zl = __fmul2_rn(y, make_float2(kLog2e, kLog2e));
-  const float2 em = __fadd2_rn(make_float2(ex2_approx(-fabsf(zl.x)), ex2_approx(-fabsf(zl.y))), make_float2(-1.f, -1.f));
-  return make_float2(fmaxf(em.x, y.x), fmaxf(em.y, y.y));
+// Activations are carried multiplied by log2(e) from the first ELU on (the
+// next projection, its attention scores and the softmax then work in base 2
+// at no cost; the pooled heads multiply by ln 2 once).  For u = y log2(e)
+// this returns ELU(y) log2(e) = max((2^(-|u|) - 1) log2(e), u): u for u > 0,
+// (e^y - 1) log2(e) otherwise (e^y - 1 >= y everywhere), with no select.
+__device__ __forceinline__ float2 elu2_log2e(float2 u) {
+  const float2 em = make_float2(ex2_approx(-fabsf(u.x)), ex2_approx(-fabsf(u.y)));
+  const float2 m = __ffma2_rn(em, make_float2(kLog2e, kLog2e), make_float2(-kLog2e, -kLog2e));
+  return make_float2(fmaxf(m.x, u.x), fmaxf(m.y, u.y));
 }
 
 // The e rows of a tile's position p live in tensor memory relative to the
@@ -525,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
         constexpr bool last = decltype(last_tag)::value;
         // per-layer bias into shared memory, by layer parity
         float* vec = (float*)(smem + kSmVec) + (l & 1) * kVecFloats;
-        vec[threadIdx.x] = __ldg(p.w + C4Off::b(l) + threadIdx.x);
+        vec[threadIdx.x] = __ldg(p.w + C4Off::b(l) + threadIdx.x) * kLog2e;
         const uint32_t lph = aph++ & 1;  // phase of this layer's sc_full / acc_a / acc_b
         wok = mbar_wait(sc_full, lph, abort_flag, kWaitLimitNs) && wok;
         ok = epilogue_all(wok);  // also publishes vec
@@ -578,8 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const float4 bv = bias4[k];
-            y[2 * k] = elu2(__ffma2_rn(make_float2(o[4 * k], o[4 * k + 1]), iv, make_float2(bv.x, bv.y)));
-            y[2 * k + 1] = elu2(__ffma2_rn(make_float2(o[4 * k + 2], o[4 * k + 3]), iv, make_float2(bv.z, bv.w)));
+            y[2 * k] = elu2_log2e(__ffma2_rn(make_float2(o[4 * k], o[4 * k + 1]), iv, make_float2(bv.x, bv.y)));
+            y[2 * k + 1] = elu2_log2e(__ffma2_rn(make_float2(o[4 * k + 2], o[4 * k + 3]), iv, make_float2(bv.z, bv.w)));
           }
           if constexpr (!last) {
             // the next layer's operand, stochastically rounded (see round_seed)
@@ -622,8 +626,8 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
                   cs[c] += x;
                   tot += x;
                 }
-              pooled[pg * 32 + d] = tot * (1.0f / kN);
-              const float wp = __ldg(p.w + C4Off::w_pi + 32 * h + d) * (1.0f / 6.0f);
+              pooled[pg * 32 + d] = tot * (kLn2 / kN);  // rows hold ELU log2(e)
+              const float wp = __ldg(p.w + C4Off::w_pi + 32 * h + d) * (kLn2 / 6.0f);
 #pragma unroll
               for (int c = 0; c < 7; ++c) lgacc[c] = fmaf(cs[c], wp, t == 0 ? 0.f : lgacc[c]);
             }
@@ -672,18 +676,19 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
               lg[k] = fmaxf(x, kLeakySlope * x);
               mx = fmaxf(mx, lg[k]);
             }
-            const float c = -mx * kLog2e;
+            const float c = -mx;  // scores are in base 2 (see elu2_log2e)
             // z sums the fp16 values the gather multiplies, so the weights
             // e / z form an exact convex combination (a uniform neighbourhood
             // reproduces Wh exactly instead of drifting by the rounding of z)
             float z = 0.f;
 #pragma unroll
             for (int k = 0; k < 9; ++k) {
-              const __half e = __float2half_rn(ex2_approx(fmaf(lg[k], kLog2e, c)));
+              const __half e = __float2half_rn(ex2_approx(lg[k] + c));
               z += __half2float(e);
               asm volatile("st.shared.b16 [%0], %1;" ::"r"(saddr[k]), "h"(__half_as_ushort(e)) : "memory");
             }
-            inv[t] = __frcp_rn(z);
+            // layer 0 reads the raw features: its Wh carries no log2(e) yet
+            inv[t] = rcp_approx(z) * (l == 0 ? kLog2e : 1.f);
             uint32_t a[24];
 #pragma unroll
             for (int k = 0; k < 6; ++k) {
@@ -772,7 +777,8 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
 // features: rows 32 s .. 32 s + 31 are head (0, 4, 1, 5, 2, 6, 3, 7)[s].
 // Rows 256..287: the attention-score weights W_l a_l^h: row 256 + 2h + v
 // holds the bf16/fp16 rounding of sum_f W_l[k][32h + f] a_l[h][v][f]
-// (v = 0 self, 1 neighbour), row 272 + 2h + v the rounding of what is left
+// (v = 0 self, 1 neighbour; times log2(e) for layer 0, whose input is not
+// yet carried in base 2), row 272 + 2h + v the rounding of what is left
 // over.  K (layers 1..5): chunk c holds the input features of heads c and
 // c + 4 (the layer before writes them as its heads finish).
 __host__ __device__ constexpr int packed_row_head(int s) { return 4 * (s & 1) + (s >> 1); }
@@ -801,6 +807,7 @@ __global__ void pack_c4_kernel(const float* __restrict__ w, uint8_t* __restrict_
     float acc = 0.f;
     if (k < fin)
       for (int f = 0; f < 32; ++f) acc = fmaf(W[(size_t)k * kHidden + 32 * h + f], A[(2 * h + v) * 32 + f], acc);
+    if (layer == 0) acc *= kLog2e;  // layer 0's scores in base 2, like the later layers'
     const float hi = OpType<OpT>::round(acc);
     *(uint16_t*)(dst + sw128_offset(256 + j, kk)) = OpType<OpT>::bits(hi);
     *(uint16_t*)(dst + sw128_offset(272 + j, kk)) = OpType<OpT>::bits(acc - hi);

@@ -80,6 +80,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// 1/x, hardware approximation (MUFU), flushing denormals.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ---- bulk async copy global -> shared (TMA engine), completes on an mbarrier ----
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
   asm volatile(

@@ -102,10 +102,13 @@ def test_tensor_core_full_batch(cuda):
     opi, ov = oracle.gat_forward(game, w, boards, side)
     assert np.abs(pi - opi).max() < 1e-3 and np.abs(v - ov).max() < 1e-3
     assert np.allclose(pi.sum(1), 1, atol=1e-5)
-    # batch composition changes a position's result at most in the last bits
-    # (its slot in a 3-position tile changes how the gather MMA splits K)
-    pj, vj = run(net, boards[1000:1003], side[1000:1003])
-    assert np.abs(pj - pi[1000:1003]).max() < 1e-6 and np.abs(vj - v[1000:1003]).max() < 1e-6
+    # batch composition changes a position's result only slightly: its slot
+    # in a 3-position tile changes how the gather MMA splits K, i.e. the last
+    # bit of some fp32 sums, and such a bit can flip the stochastic rounding
+    # of one activation by one bf16 unit (measured: up to 1.7e-6 on outputs)
+    for s0 in (1000, 1500, 2000):
+        pj, vj = run(net, boards[s0:s0 + 3], side[s0:s0 + 3])
+        assert np.abs(pj - pi[s0:s0 + 3]).max() < 1e-5 and np.abs(vj - v[s0:s0 + 3]).max() < 1e-5
     net.check()
 
 
