@@ -256,11 +256,30 @@ def mcts_bench(net, device, game: int, trees: int, sims: int, leaves: int, moves
     m.check()
     waves = math.ceil(sims / leaves)
     world = gzd.rank_info().world
-    return {"sims_per_s": trees * waves * leaves * moves * world / el,
-            "positions_per_s": trees * moves * world / el,
-            "config": f"{trees} games/GPU x {sims} sims/move, leaf batch {trees * leaves}, c_puct 1.5, "
-                      f"virtual loss 3, Dirichlet(1.0, 0.25), {moves} timed moves",
-            "gpu_launches_per_move": 3 * waves + 2}
+    out = {"sims_per_s": trees * waves * leaves * moves * world / el,
+           "positions_per_s": trees * moves * world / el,
+           "config": f"{trees} games/GPU x {sims} sims/move, leaf batch {trees * leaves}, c_puct 1.5, "
+                     f"virtual loss 3, Dirichlet(1.0, 0.25), {moves} timed moves",
+           "gpu_launches_per_move": 3 * waves + 2}
+
+    # Whole games through the self-play driver: every tree starts from the
+    # empty board and plays until `trees` games have ended; examples are the
+    # TrainingExample records the driver writes.
+    m.reset_roots(boards, side)
+    sp = gz.SelfPlay(m, max_examples=trees * s.nodes * 2)
+    torch.cuda.synchronize()
+    gzd.barrier()
+    t0 = time.perf_counter()
+    sp.run(net, trees, sims, 15, stream)
+    el = gzd.max_over_ranks(time.perf_counter() - t0, device=f"cuda:{device}")
+    ex, games = sp.take()
+    m.check()
+    out["selfplay"] = {"games_per_s": games * world / el, "examples_per_s": ex.size * world / el,
+                       "games": games, "examples": int(ex.size), "seconds": el,
+                       "call": f"gz_selfplay_run until {trees} games/GPU ended, from empty boards, "
+                               f"{sims} sims/move, temperature moves 15"}
+    sp.close()
+    return out
 
 
 def ours(args, cfg: dict) -> None:

@@ -103,6 +103,13 @@ _SIGS = {
     "gz_mcts_choose": (C.c_int, [_vp, C.c_int, _vp, _vp]),
     "gz_mcts_play": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
     "gz_mcts_check": (C.c_int, [_vp]),
+    "gz_selfplay_create": (C.c_int, [_vp, C.c_int, C.POINTER(_vp)]),
+    "gz_selfplay_destroy": (C.c_int, [_vp]),
+    "gz_selfplay_run": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_int, _vp]),
+    "gz_selfplay_take": (C.c_int, [_vp, _vp, C.c_int64, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "gz_train_examples_save": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(_vp), _i32p]),
+    "gz_train_examples_load": (C.c_int, [C.c_char_p, _vp, C.c_int64, _i32p, C.c_int, C.POINTER(C.c_int),
+                                         C.POINTER(C.c_int64)]),
     "gz_selftest_wait_timeout": (C.c_int, [C.c_int, C.c_int]),
     "gz_gat_c4_predict_noalloc": (C.c_int, [C.c_int, _f32p, C.c_size_t, _i8p, _i8p, C.c_int, _f32p, _f32p]),
     "gz_gat_c4_noalloc_scratch_bytes": (C.c_size_t, []),
@@ -444,6 +451,66 @@ class Mcts:
 
     def check(self) -> None:
         _check(_lib.gz_mcts_check(self._h))
+
+
+# TrainingExample of self_play/self_play.cuh:56-60 (gz_train_example): 516 bytes
+EXAMPLE_DTYPE = np.dtype([("board", "<i4", 64), ("pi", "<f4", 64), ("v", "<f4")])
+assert EXAMPLE_DTYPE.itemsize == 516
+
+
+class SelfPlay:
+    """Self-play episodes on every tree of a search handle (gz_selfplay_*)."""
+
+    def __init__(self, mcts: Mcts, max_examples: int):
+        h = _vp()
+        _check(_lib.gz_selfplay_create(mcts._h, max_examples, C.byref(h)))
+        self._h, self.mcts = h, mcts  # keeps the search handle alive
+
+    def close(self) -> None:
+        if self._h:
+            _lib.gz_selfplay_destroy(self._h)
+            self._h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass
+
+    def run(self, net: Net, n_games: int, sims: int, temp_moves: int = 15, stream=None) -> None:
+        _check(_lib.gz_selfplay_run(self._h, net._h, n_games, sims, temp_moves, _stream(stream)))
+
+    def take(self) -> tuple[np.ndarray, int]:
+        """The buffered examples (EXAMPLE_DTYPE records, in the order the games
+        ended) and the number of games they come from; empties the buffer."""
+        n, g = C.c_int64(), C.c_int64()
+        # with no room the call only reports the counts (or, with nothing
+        # buffered, succeeds and resets them)
+        if _lib.gz_selfplay_take(self._h, None, 0, C.byref(n), C.byref(g)) == 0:
+            return np.zeros(0, EXAMPLE_DTYPE), int(g.value)
+        out = np.zeros(n.value, EXAMPLE_DTYPE)
+        _check(_lib.gz_selfplay_take(self._h, out.ctypes.data, out.size, C.byref(n), C.byref(g)))
+        return out, int(g.value)
+
+
+def save_train_examples(path, iterations: list) -> None:
+    """The reference's train_examples_*.bin layout (self_play.cu:510-534)."""
+    arrs = [np.ascontiguousarray(a, dtype=EXAMPLE_DTYPE) for a in iterations]
+    ptrs = (_vp * max(1, len(arrs)))(*[a.ctypes.data for a in arrs])
+    counts = np.array([a.size for a in arrs] or [0], np.int32)
+    _check(_lib.gz_train_examples_save(str(path).encode(), len(arrs), ptrs, _ptr(counts, C.c_int32)))
+
+
+def load_train_examples(path) -> list:
+    """Reads such a file back: one EXAMPLE_DTYPE array per iteration."""
+    n_it, total = C.c_int(), C.c_int64()
+    _check(_lib.gz_train_examples_load(str(path).encode(), None, 0, None, 0, C.byref(n_it), C.byref(total)))
+    out = np.zeros(total.value, EXAMPLE_DTYPE)
+    counts = np.zeros(max(1, n_it.value), np.int32)
+    _check(_lib.gz_train_examples_load(str(path).encode(), out.ctypes.data, out.size, _ptr(counts, C.c_int32),
+                                       n_it.value, C.byref(n_it), C.byref(total)))
+    offs = np.concatenate([[0], np.cumsum(counts[:n_it.value])])
+    return [out[offs[i]:offs[i + 1]] for i in range(n_it.value)]
 
 
 # ---- reference-layout shim (include/graphzero_b200_compat.h) ----

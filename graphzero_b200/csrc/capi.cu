@@ -128,6 +128,15 @@ struct gz_mcts {
   int32_t* d_tmp = nullptr;
 };
 
+struct gz_selfplay {
+  SelfPlayDev s{};
+  gz_mcts* m = nullptr;
+  int device = 0;
+  std::vector<void*> allocs;
+  int32_t* d_actions = nullptr;
+  int* d_counts = nullptr;  // out_count, games_done, overflow (contiguous)
+};
+
 namespace {
 
 bool use_tensor_cores(const gz_net* n) {
@@ -900,6 +909,174 @@ gz_status gz_mcts_play(gz_mcts* m, const int32_t* actions, int reserve, int8_t* 
   if (!m || !actions || reserve < 0) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
   GZ_DEVICE(m->device);
   GZ_CUDA(mcts_launch_play(m->d, actions, reserve, done, (cudaStream_t)stream));
+  return GZ_OK;
+}
+
+// ---- self-play ----
+
+static_assert(sizeof(gz_train_example) == 516, "TrainingExample layout of self_play/self_play.cuh:56-60");
+
+gz_status gz_selfplay_create(gz_mcts* m, int max_examples, gz_selfplay** out) {
+  if (!m || !out || max_examples <= 0) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  *out = nullptr;
+  GZ_DEVICE(m->device);
+  gz_selfplay* sp = new gz_selfplay();
+  sp->m = m;
+  sp->device = m->device;
+  SelfPlayDev& s = sp->s;
+  const MctsDev& d = m->d;
+  s.max_moves = d.N;  // a game fills at most every cell, one example per move
+  s.out_cap = max_examples;
+  const size_t slots = (size_t)d.trees * s.max_moves;
+  gz_status st = GZ_OK;
+  auto alloc = [&](auto** p, size_t bytes) {
+    if (st != GZ_OK) return;
+    cudaError_t e = cudaMalloc((void**)p, bytes ? bytes : 1);
+    if (e != cudaSuccess) st = fail(GZ_ERR_CUDA, "cudaMalloc %zu bytes: %s", bytes, cudaGetErrorString(e));
+    else sp->allocs.push_back((void*)*p);
+  };
+  alloc(&s.log_board, slots * d.N);
+  alloc(&s.log_pi, slots * d.A * 4);
+  alloc(&s.log_v, slots * 4);
+  alloc(&s.log_side, slots);
+  alloc(&s.log_len, (size_t)d.trees * 4);
+  alloc(&s.fin_len, (size_t)d.trees * 4);
+  alloc(&s.out, (size_t)max_examples * sizeof(gz_train_example));
+  alloc(&sp->d_counts, 3 * 4);
+  alloc(&sp->d_actions, (size_t)d.trees * 4);
+  if (st == GZ_OK) {
+    s.out_count = sp->d_counts;
+    s.games_done = sp->d_counts + 1;
+    s.overflow = sp->d_counts + 2;
+    cudaError_t e = cudaMemset(s.log_len, 0, (size_t)d.trees * 4);
+    if (e == cudaSuccess) e = cudaMemset(sp->d_counts, 0, 3 * 4);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) st = fail(GZ_ERR_CUDA, "init: %s", cudaGetErrorString(e));
+  }
+  if (st != GZ_OK) {
+    gz_selfplay_destroy(sp);
+    return st;
+  }
+  *out = sp;
+  return GZ_OK;
+}
+
+gz_status gz_selfplay_destroy(gz_selfplay* sp) {
+  if (!sp) return GZ_OK;
+  DeviceGuard g(sp->device);
+  cudaDeviceSynchronize();
+  for (void* p : sp->allocs) cudaFree(p);
+  delete sp;
+  return GZ_OK;
+}
+
+gz_status gz_selfplay_run(gz_selfplay* sp, gz_net* net, int n_games, int sims, int temp_moves, void* stream) {
+  if (!sp || !net || n_games < 0 || sims <= 0) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  gz_mcts* m = sp->m;
+  if (net->game != m->d.game) return fail(GZ_ERR_INVALID_ARG, "net and search play different games");
+  if (net->device != m->device) return fail(GZ_ERR_INVALID_ARG, "net and search live on different devices");
+  GZ_DEVICE(m->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  int counts[3];
+  GZ_CUDA(cudaMemcpyAsync(counts, sp->d_counts, sizeof counts, cudaMemcpyDeviceToHost, s));
+  GZ_CUDA(cudaStreamSynchronize(s));
+  const int target = counts[1] + n_games;
+  // every tree ends a game at least every max_moves moves
+  const long long max_moves = ((long long)n_games / m->d.trees + 2) * (sp->s.max_moves + 1);
+  // keep a child's subtree while the next move's simulations fit in the pool
+  const int reserve = sims + m->d.leaves;
+  for (long long mv = 0; mv < max_moves && counts[1] < target; ++mv) {
+    gz_status st = gz_mcts_run(m, net, sims, stream);
+    if (st != GZ_OK) return st;
+    GZ_CUDA(selfplay_launch_record(m->d, sp->s, temp_moves, s));
+    GZ_CUDA(mcts_launch_choose(m->d, temp_moves, sp->d_actions, s));
+    GZ_CUDA(selfplay_launch_finish(m->d, sp->s, sp->d_actions, s));
+    GZ_CUDA(selfplay_launch_emit(m->d, sp->s, s));
+    GZ_CUDA(mcts_launch_play(m->d, sp->d_actions, reserve, nullptr, s));
+    GZ_CUDA(cudaMemcpyAsync(counts, sp->d_counts, sizeof counts, cudaMemcpyDeviceToHost, s));
+    GZ_CUDA(cudaStreamSynchronize(s));
+    if (counts[2]) break;
+  }
+  gz_status st = gz_mcts_check(m);
+  if (st != GZ_OK) return st;
+  if (counts[2] == 1) return fail(GZ_ERR_CAPACITY, "a game outgrew its example log");
+  if (counts[2] == 2) return fail(GZ_ERR_CAPACITY, "example buffer full (%d examples): take them first", sp->s.out_cap);
+  if (counts[1] < target) return fail(GZ_ERR_TIMEOUT, "games did not end within %lld moves", max_moves);
+  return GZ_OK;
+}
+
+gz_status gz_selfplay_take(gz_selfplay* sp, gz_train_example* out, int64_t capacity, int64_t* n_examples,
+                           int64_t* n_games) {
+  if (!sp || (!out && capacity > 0) || capacity < 0) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  GZ_DEVICE(sp->device);
+  int counts[3];
+  GZ_CUDA(cudaMemcpy(counts, sp->d_counts, sizeof counts, cudaMemcpyDeviceToHost));
+  if (n_examples) *n_examples = counts[0];
+  if (n_games) *n_games = counts[1];
+  if (counts[0] > capacity) return fail(GZ_ERR_CAPACITY, "%d examples buffered, room for %lld", counts[0], (long long)capacity);
+  if (counts[0] > 0) GZ_CUDA(cudaMemcpy(out, sp->s.out, (size_t)counts[0] * sizeof(gz_train_example), cudaMemcpyDeviceToHost));
+  GZ_CUDA(cudaMemset(sp->d_counts, 0, 3 * 4));
+  return GZ_OK;
+}
+
+gz_status gz_train_examples_save(const char* path, int n_iters, const gz_train_example* const* iters,
+                                 const int32_t* counts) {
+  if (!path || n_iters < 0 || (n_iters > 0 && (!iters || !counts))) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  for (int i = 0; i < n_iters; ++i)
+    if (counts[i] < 0 || (counts[i] > 0 && !iters[i])) return fail(GZ_ERR_INVALID_ARG, "bad iteration %d", i);
+  FILE* f = fopen(path, "wb");
+  if (!f) return fail(GZ_ERR_IO, "cannot open %s for writing", path);
+  const int32_t h = n_iters;
+  bool ok = fwrite(&h, 4, 1, f) == 1;
+  for (int i = 0; i < n_iters && ok; ++i) {
+    ok = fwrite(&counts[i], 4, 1, f) == 1;
+    if (ok && counts[i] > 0) ok = fwrite(iters[i], sizeof(gz_train_example), (size_t)counts[i], f) == (size_t)counts[i];
+  }
+  ok = (fclose(f) == 0) && ok;
+  return ok ? GZ_OK : fail(GZ_ERR_IO, "write to %s failed", path);
+}
+
+gz_status gz_train_examples_load(const char* path, gz_train_example* out, int64_t capacity, int32_t* counts,
+                                 int max_iters, int* n_iters, int64_t* total) {
+  if (!path || !n_iters || !total || capacity < 0 || (out && (!counts || max_iters < 0)))
+    return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  FILE* f = fopen(path, "rb");
+  if (!f) return fail(GZ_ERR_IO, "cannot open %s", path);
+  gz_status st = GZ_OK;
+  int32_t h = 0;
+  long long sum = 0;
+  if (fread(&h, 4, 1, f) != 1 || h < 0) st = fail(GZ_ERR_IO, "%s: bad header", path);
+  if (st == GZ_OK && out && h > max_iters) st = fail(GZ_ERR_CAPACITY, "%s holds %d iterations, room for %d", path, h, max_iters);
+  for (int i = 0; i < h && st == GZ_OK; ++i) {
+    int32_t c = 0;
+    if (fread(&c, 4, 1, f) != 1 || c < 0) {
+      st = fail(GZ_ERR_IO, "%s: bad count of iteration %d", path, i);
+      break;
+    }
+    if (out) {
+      if (sum + c > capacity) {
+        st = fail(GZ_ERR_CAPACITY, "%s holds more than %lld examples", path, (long long)capacity);
+        break;
+      }
+      if (c > 0 && fread(out + sum, sizeof(gz_train_example), (size_t)c, f) != (size_t)c) {
+        st = fail(GZ_ERR_IO, "%s: short iteration %d", path, i);
+        break;
+      }
+      counts[i] = c;
+    } else if (c > 0 && fseek(f, (long)((size_t)c * sizeof(gz_train_example)), SEEK_CUR) != 0) {
+      st = fail(GZ_ERR_IO, "%s: short iteration %d", path, i);
+      break;
+    }
+    sum += c;
+  }
+  if (st == GZ_OK && !out) {  // a size query still checks that the records are all there
+    const long pos = ftell(f);
+    if (fseek(f, 0, SEEK_END) != 0 || ftell(f) < pos) st = fail(GZ_ERR_IO, "%s: short file", path);
+  }
+  fclose(f);
+  if (st != GZ_OK) return st;
+  *n_iters = h;
+  *total = sum;
   return GZ_OK;
 }
 

@@ -9,6 +9,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/graphzero_b200.h"
+
 namespace gz {
 
 constexpr int kMctsBoardStride = 48;  // bytes per stored position (>= 42, 16-aligned)
@@ -60,5 +62,28 @@ cudaError_t mcts_launch_root_visits(const MctsDev& d, int32_t* visits, float* ws
 cudaError_t mcts_launch_choose(const MctsDev& d, int temp_moves, int32_t* actions, cudaStream_t s);
 cudaError_t mcts_launch_play(const MctsDev& d, const int32_t* actions, int reserve, int8_t* done, cudaStream_t s);
 cudaError_t mcts_launch_tree_sizes(const MctsDev& d, int32_t* nodes, int32_t* edges, cudaStream_t s);
+
+// Self-play bookkeeping (selfplay.cu): per-tree logs of the game in progress
+// and the output buffer of finished examples.
+struct SelfPlayDev {
+  int max_moves;          // examples one game can produce (plies)
+  int8_t* log_board;      // [trees][max_moves][N] canonical boards
+  float* log_pi;          // [trees][max_moves][A]
+  float* log_v;           // [trees][max_moves]
+  int8_t* log_side;       // [trees][max_moves] player to move
+  int* log_len;           // [trees] examples of the game in progress
+  int* fin_len;           // [trees] examples of the game that ended this move (0 = none)
+  gz_train_example* out;  // [out_cap]
+  int out_cap;
+  int* out_count;
+  int* games_done;
+  int* overflow;          // 1 = a game log overflowed, 2 = the output buffer did
+};
+
+// Per move, around mcts_launch_choose: record the roots, then (given the
+// chosen actions, before mcts_launch_play) finish ended games and emit them.
+cudaError_t selfplay_launch_record(const MctsDev& d, const SelfPlayDev& s, int temp_moves, cudaStream_t st);
+cudaError_t selfplay_launch_finish(const MctsDev& d, const SelfPlayDev& s, const int32_t* actions, cudaStream_t st);
+cudaError_t selfplay_launch_emit(const MctsDev& d, const SelfPlayDev& s, cudaStream_t st);
 
 }  // namespace gz

@@ -1,0 +1,181 @@
+// Self-play episodes on top of the batched search: every tree of a search
+// handle plays games back to back; each move records the root position and
+// its visit-count policy, and when a game ends its examples get the outcome
+// and are copied, in a fixed order, to an output buffer of TrainingExample
+// records.
+//
+// Reference: parallel_self_play_kernel and execute_self_play
+// (self_play/self_play.cu:75-145, 403-472): per move, simulations, the
+// policy N^(1/T) (mcts_get_policy, 645-662), the example (board, pi), the
+// chosen move, the next state, and at the game's end v = the outcome for each
+// example.  Differences, all deliberate:
+//   * the stored board is the canonical form (board x player to move,
+//     games/connect4/connect4.cu:89-93), so every example is seen from the
+//     player to move, and v is the outcome for that player (+1 win, -1 loss,
+//     0 draw); the reference stores the raw board and signs v by the parity of
+//     the move index relative to the last move (self_play.cu:442-447);
+//   * after temp_moves moves the policy is one-hot on the most visited move
+//     (lowest action on ties), the limit of the reference's T = 1e-3;
+//   * games never exceed the board's number of cells, so no forced draw at
+//     MAX_GAME_LENGTH (self_play.cu:457-465) is needed.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gz_games.h"
+#include "gz_mcts.h"
+
+namespace gz {
+namespace {
+
+// The root's expanded edges: visit counts -> policy over actions (zeroed
+// elsewhere).  T = 1 while move_no < temp_moves: N_a / sum N; afterwards
+// one-hot on the most visited action (the first edge, i.e. the lowest
+// action, on ties).
+__device__ void root_policy(const MctsDev& d, int t, int temp_moves, float* pi) {
+  const size_t nb = (size_t)t * d.node_cap, eb = (size_t)t * d.edge_cap;
+  const int r = d.root[t];
+  for (int a = 0; a < d.A; ++a) pi[a] = 0.0f;
+  if (!d.expanded[nb + r]) return;
+  const int fe = d.first_edge[nb + r], ne = d.n_edges[nb + r];
+  long long total = 0;
+  int best = 0;
+  for (int k = 0; k < ne; ++k) {
+    const int nv = d.Nv[eb + fe + k];
+    total += nv;
+    if (nv > d.Nv[eb + fe + best]) best = k;
+  }
+  if (ne == 0) return;
+  if (d.move_no[t] < temp_moves && total > 0) {
+    for (int k = 0; k < ne; ++k) pi[d.action[eb + fe + k]] = (float)d.Nv[eb + fe + k] / (float)total;
+  } else {
+    pi[d.action[eb + fe + best]] = 1.0f;
+  }
+}
+
+__global__ void record_kernel(MctsDev d, SelfPlayDev s, int temp_moves) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= d.trees) return;
+  const int k = s.log_len[t];
+  if (k >= s.max_moves) {  // cannot happen for games of at most max_moves plies
+    atomicExch(s.overflow, 1);
+    return;
+  }
+  const size_t slot = (size_t)t * s.max_moves + k;
+  const size_t root = (size_t)t * d.node_cap + d.root[t];
+  const int8_t side = d.side[root];
+  const int8_t* b = d.board + root * kMctsBoardStride;
+  for (int i = 0; i < d.N; ++i) s.log_board[slot * d.N + i] = (int8_t)(b[i] * side);
+  root_policy(d, t, temp_moves, s.log_pi + slot * d.A);
+  s.log_side[slot] = side;
+  s.log_len[t] = k + 1;
+}
+
+// Outcome of the chosen move (before play_kernel applies it): a game that
+// ends gets its examples' values and its length in fin_len.
+__global__ void finish_kernel(MctsDev d, SelfPlayDev s, const int32_t* __restrict__ actions) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= d.trees) return;
+  s.fin_len[t] = 0;
+  const size_t root = (size_t)t * d.node_cap + d.root[t];
+  int8_t b[kMctsBoardStride];
+  for (int i = 0; i < kMctsBoardStride; ++i) b[i] = d.board[root * kMctsBoardStride + i];
+  const int mover = d.side[root];
+  const int sq = apply_action(d.game, b, actions[t], mover);
+  const int oc = sq < 0 ? 2 : outcome_after(d.game, b, sq, mover);
+  if (oc == 0) return;
+  const float z = oc == 1 ? 1.0f : 0.0f;  // for the mover
+  const int n = s.log_len[t];
+  for (int k = 0; k < n; ++k) {
+    const size_t slot = (size_t)t * s.max_moves + k;
+    s.log_v[slot] = s.log_side[slot] == mover ? z : -z;
+  }
+  s.fin_len[t] = n;
+}
+
+// Block-wide exclusive prefix sum (blockDim.x a multiple of 32, <= 1024).
+__device__ int block_exclusive_sum(int x, int* total) {
+  __shared__ int warp_sums[32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int incl = x;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_sums[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    int v = lane < nw ? warp_sums[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
+    }
+    if (lane < nw) warp_sums[lane] = v;  // inclusive over warps
+  }
+  __syncthreads();
+  const int before = (w > 0 ? warp_sums[w - 1] : 0) + incl - x;
+  *total = warp_sums[nw - 1];
+  __syncthreads();
+  return before;
+}
+
+// One block: the games that ended this move, in tree order, appended to the
+// output as TrainingExample records (board and pi zero-padded to 64).
+__global__ void emit_kernel(MctsDev d, SelfPlayDev s) {
+  __shared__ int base_ex, base_games;
+  if (threadIdx.x == 0) {
+    base_ex = *s.out_count;
+    base_games = *s.games_done;
+  }
+  __syncthreads();
+  for (int t0 = 0; t0 < d.trees; t0 += blockDim.x) {
+    const int t = t0 + threadIdx.x;
+    const int n = t < d.trees ? s.fin_len[t] : 0;
+    int tot_ex = 0, tot_games = 0;
+    const int off = block_exclusive_sum(n, &tot_ex);
+    block_exclusive_sum(n > 0 ? 1 : 0, &tot_games);
+    if (n > 0) {
+      const int dst = base_ex + off;
+      if (dst + n > s.out_cap) {
+        atomicExch(s.overflow, 2);
+      } else {
+        for (int k = 0; k < n; ++k) {
+          const size_t slot = (size_t)t * s.max_moves + k;
+          gz_train_example* e = s.out + dst + k;
+          for (int i = 0; i < GZ_EXAMPLE_CELLS; ++i) e->board[i] = i < d.N ? (int32_t)s.log_board[slot * d.N + i] : 0;
+          for (int a = 0; a < GZ_EXAMPLE_CELLS; ++a) e->pi[a] = a < d.A ? s.log_pi[slot * d.A + a] : 0.0f;
+          e->v = s.log_v[slot];
+        }
+      }
+      s.log_len[t] = 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      base_ex += tot_ex;
+      base_games += tot_games;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    *s.out_count = base_ex < s.out_cap ? base_ex : s.out_cap;
+    *s.games_done = base_games;
+  }
+}
+
+}  // namespace
+
+cudaError_t selfplay_launch_record(const MctsDev& d, const SelfPlayDev& s, int temp_moves, cudaStream_t st) {
+  record_kernel<<<(d.trees + 127) / 128, 128, 0, st>>>(d, s, temp_moves);
+  return cudaGetLastError();
+}
+
+cudaError_t selfplay_launch_finish(const MctsDev& d, const SelfPlayDev& s, const int32_t* actions, cudaStream_t st) {
+  finish_kernel<<<(d.trees + 127) / 128, 128, 0, st>>>(d, s, actions);
+  return cudaGetLastError();
+}
+
+cudaError_t selfplay_launch_emit(const MctsDev& d, const SelfPlayDev& s, cudaStream_t st) {
+  emit_kernel<<<1, 1024, 0, st>>>(d, s);
+  return cudaGetLastError();
+}
+
+}  // namespace gz

@@ -211,6 +211,53 @@ gz_status gz_mcts_play(gz_mcts* m, const int32_t* d_actions, int reserve, int8_t
  * pool, 3 depth); synchronises. */
 gz_status gz_mcts_check(gz_mcts* m);
 
+/* ---- self-play episodes and training examples (self_play/self_play.cu) --- */
+#define GZ_EXAMPLE_CELLS 64 /* MAX_BOARD_SIZE, games/game.cuh:7 */
+/* TrainingExample of self_play/self_play.cuh:56-60 (516 bytes, no padding):
+ * the record the reference's train_examples_*.bin files hold.  board is the
+ * canonical position (board x player to move, connect4.cu:89-93), pi the
+ * search policy over actions, v the game's outcome for the player to move
+ * (+1 win, -1 loss, 0 draw); unused cells are zero. */
+typedef struct gz_train_example {
+  int32_t board[GZ_EXAMPLE_CELLS];
+  float pi[GZ_EXAMPLE_CELLS];
+  float v;
+} gz_train_example;
+typedef struct gz_selfplay gz_selfplay;
+/* Self-play state on top of a search handle (which it uses, not owns):
+ * per-tree logs of the game in progress and a device buffer for up to
+ * max_examples finished examples (replaces SelfPlayPipeline's d_examples,
+ * self_play.cu:102-105). */
+gz_status gz_selfplay_create(gz_mcts* m, int max_examples, gz_selfplay** out);
+gz_status gz_selfplay_destroy(gz_selfplay* sp);
+/* Plays moves on every tree until n_games more games have ended
+ * (execute_self_play / parallel_self_play_kernel, self_play.cu:75-145,
+ * 403-472): per move `sims` simulations, the root recorded as an example
+ * with pi = N / sum N for the first temp_moves moves of a game and one-hot
+ * on the most visited move afterwards (mcts_get_policy, 645-662), a move
+ * chosen as gz_mcts_choose does, the roots advanced (a finished game's tree
+ * starts a new game).  Ended games' examples go to the buffer in the order
+ * the games ended (ties: tree order).  Synchronises once per move.
+ * GZ_ERR_CAPACITY when the buffer overflows (gz_selfplay_take empties it). */
+gz_status gz_selfplay_run(gz_selfplay* sp, gz_net* net, int n_games, int sims, int temp_moves, void* stream);
+/* Copies the buffered examples to the host, in order, and empties the
+ * buffer; *n_examples and *n_games (either may be NULL) receive the counts.
+ * GZ_ERR_CAPACITY (nothing copied, buffer kept) if capacity is too small. */
+gz_status gz_selfplay_take(gz_selfplay* sp, gz_train_example* h_out, int64_t capacity, int64_t* n_examples,
+                           int64_t* n_games);
+/* save_train_examples (self_play.cu:510-534): the reference's file layout,
+ * int32 number of iterations, then per iteration int32 count and count
+ * 516-byte records (little endian).  iters[i] holds counts[i] examples. */
+gz_status gz_train_examples_save(const char* path, int n_iters, const gz_train_example* const* iters,
+                                 const int32_t* counts);
+/* load_train_examples (self_play.cu:536-573): reads such a file.  With
+ * out == NULL only *n_iters and *total are set (sizes for a second call);
+ * otherwise the iterations' records go to `out` back to back and counts[i]
+ * gets iteration i's count (max_iters entries).  GZ_ERR_IO on a short or
+ * malformed file, GZ_ERR_CAPACITY if capacity or max_iters is too small. */
+gz_status gz_train_examples_load(const char* path, gz_train_example* out, int64_t capacity, int32_t* counts,
+                                 int max_iters, int* n_iters, int64_t* total);
+
 /* ---- allocation-free leaf evaluation --------------------------------------
  * No counterpart in the reference.  For callers that may not allocate device
  * memory (a plugin inside a host application that fixes the device-memory
