@@ -29,8 +29,11 @@
 // The next layer's projection does not wait for the head loop: heads c and
 // c + 4 write K chunk c of the next X tile, and each chunk's MMAs are issued
 // as soon as it exists, into a third accumulator block (tensor memory holds
-// three 128-column blocks that rotate from layer to layer).  Only the last
-// chunk's MMAs remain between two head loops.
+// three 128-column blocks that rotate from layer to layer).  Between two head
+// loops remain the last chunk's score MMAs, which go first, and the
+// projection halves of the last two chunks: chunk 2's halves are held back
+// until chunk 3's scores are issued, so that the tensor pipe (in order)
+// reaches the scores the next head loop starts on without a queue ahead.
 // Weights are pre-packed on the device into 36 KB chunks (256 projection rows
 // + 32 score rows, 64 K each, swizzled) and streamed into a two-slot
 // shared-memory ring by one producer thread with 1-D bulk async copies (TMA
@@ -442,19 +445,16 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           for (int kk = 0; kk < 4; ++kk) proj(fb, 1, 1, q + 1, kk, false);
           mma_commit(&empty[q % kWSlots]);
           mma_commit(&empty[(q + 1) % kWSlots]);
-          // chunk 2: everything
+          // chunk 2: scores only; its halves wait until chunk 3's scores are
+          // issued, so nothing queues ahead of the scores the epilogue waits on
           wait_x(2);
           wait_w(q + 2);
           if (!ok) break;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            proj(fa, 0, 2, q + 2, kk, false);
-            score(2, q + 2, kk, false);
-            proj(fb, 1, 2, q + 2, kk, false);
-          }
-          mma_commit(&empty[(q + 2) % kWSlots]);
+          for (int kk = 0; kk < 4; ++kk) score(2, q + 2, kk, false);
           // chunk 3: scores first (the epilogue starts on them), then the
-          // first half, then the second, each committed on its own barrier
+          // first half of chunks 2 and 3, then the second, each committed on
+          // its own barrier
           wait_x(3);
           wait_w(q + 3);
           if (!ok) break;
@@ -462,11 +462,16 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           for (int kk = 0; kk < 4; ++kk) score(3, q + 3, kk, false);
           mma_commit(sc_full);
 #pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fa, 0, 2, q + 2, kk, false);
+#pragma unroll
           for (int kk = 0; kk < 4; ++kk) proj(fa, 0, 3, q + 3, kk, false);
           mma_commit(acc_a);
 #pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fb, 1, 2, q + 2, kk, false);
+#pragma unroll
           for (int kk = 0; kk < 4; ++kk) proj(fb, 1, 3, q + 3, kk, false);
           mma_commit(acc_b);
+          mma_commit(&empty[(q + 2) % kWSlots]);
           mma_commit(&empty[(q + 3) % kWSlots]);
           q += 4;
         }

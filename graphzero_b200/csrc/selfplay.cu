@@ -13,7 +13,8 @@
 //     games/connect4/connect4.cu:89-93), so every example is seen from the
 //     player to move, and v is the outcome for that player (+1 win, -1 loss,
 //     0 draw); the reference stores the raw board and signs v by the parity of
-//     the move index relative to the last move (self_play.cu:442-447);
+//     the move index (self_play.cu:438-447), from a game-end test of the
+//     player who did not just move;
 //   * after temp_moves moves the policy is one-hot on the most visited move
 //     (lowest action on ties), the limit of the reference's T = 1e-3;
 //   * games never exceed the board's number of cells, so no forced draw at
