@@ -107,6 +107,7 @@ _SIGS = {
     "gz_selfplay_destroy": (C.c_int, [_vp]),
     "gz_selfplay_run": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_int, _vp]),
     "gz_selfplay_take": (C.c_int, [_vp, _vp, C.c_int64, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "gz_arena_play": (C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, _i32p, _i32p, _i32p, _vp]),
     "gz_train_examples_save": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(_vp), _i32p]),
     "gz_train_examples_load": (C.c_int, [C.c_char_p, _vp, C.c_int64, _i32p, C.c_int, C.POINTER(C.c_int),
                                          C.POINTER(C.c_int64)]),
@@ -491,6 +492,14 @@ class SelfPlay:
         out = np.zeros(n.value, EXAMPLE_DTYPE)
         _check(_lib.gz_selfplay_take(self._h, out.ctypes.data, out.size, C.byref(n), C.byref(g)))
         return out, int(g.value)
+
+
+def arena_play(mcts: Mcts, net_a: Net, net_b: Net, n_games: int, sims: int, stream=None) -> tuple[int, int, int]:
+    """(games won by net_a, games won by net_b, draws); see gz_arena_play."""
+    r = np.zeros(3, np.int32)
+    _check(_lib.gz_arena_play(mcts._h, net_a._h, net_b._h, n_games, sims, _ptr(r[0:], C.c_int32),
+                              _ptr(r[1:], C.c_int32), _ptr(r[2:], C.c_int32), _stream(stream)))
+    return int(r[0]), int(r[1]), int(r[2])
 
 
 def save_train_examples(path, iterations: list) -> None:

@@ -1019,6 +1019,88 @@ gz_status gz_selfplay_take(gz_selfplay* sp, gz_train_example* out, int64_t capac
   return GZ_OK;
 }
 
+// ---- arena ----
+
+gz_status gz_arena_play(gz_mcts* m, gz_net* net_a, gz_net* net_b, int n_games, int sims, int32_t* a_wins,
+                        int32_t* b_wins, int32_t* draws, void* stream) {
+  if (!m || !net_a || !net_b || n_games < 0 || sims <= 0 || !a_wins || !b_wins || !draws)
+    return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  if (net_a->game != m->d.game || net_b->game != m->d.game)
+    return fail(GZ_ERR_INVALID_ARG, "nets and search play different games");
+  if (net_a->device != m->device || net_b->device != m->device)
+    return fail(GZ_ERR_INVALID_ARG, "nets and search live on different devices");
+  GZ_DEVICE(m->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  const MctsDev& d = m->d;
+  const int T = d.trees, A = d.A, N = d.N;
+  const size_t L = (size_t)T * d.leaves;
+  // one scratch block: two networks' evaluations, game state, moves
+  const size_t o_pib = L * A * 4, o_va = 2 * o_pib, o_vb = o_va + L * 4, o_act = o_vb + L * 4,
+               o_cnt = o_act + (size_t)T * 4, o_brd = o_cnt + 16, o_side = o_brd + (size_t)T * N,
+               o_amv = o_side + T, o_actv = o_amv + T, o_res = o_actv + T, bytes = o_res + T;
+  uint8_t* buf = nullptr;
+  GZ_CUDA(cudaMallocAsync((void**)&buf, bytes, s));
+  float *pi_a = (float*)buf, *pi_b = (float*)(buf + o_pib), *v_a = (float*)(buf + o_va), *v_b = (float*)(buf + o_vb);
+  int32_t* actions = (int32_t*)(buf + o_act);
+  int* n_active = (int*)(buf + o_cnt);
+  int8_t *boards = (int8_t*)(buf + o_brd), *side = (int8_t*)(buf + o_side), *a_moves = (int8_t*)(buf + o_amv),
+         *active = (int8_t*)(buf + o_actv), *result = (int8_t*)(buf + o_res);
+  std::vector<int8_t> h_side(T, 1), h_amv(T), h_act(T), h_res(T);
+  const int waves = (sims + d.leaves - 1) / d.leaves;
+  int wa = 0, wb = 0, dr = 0;
+  gz_status st = GZ_OK;
+  auto cuda = [&](cudaError_t e, const char* what) {
+    if (st == GZ_OK && e != cudaSuccess) st = fail(GZ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return st == GZ_OK;
+  };
+  for (int g0 = 0; g0 < n_games && st == GZ_OK; g0 += T) {
+    const int n = n_games - g0 < T ? n_games - g0 : T;
+    for (int t = 0; t < T; ++t) {
+      h_act[t] = t < n;
+      h_amv[t] = g0 + t < n_games / 2;  // net A moves first in the first half (arena.cu:98-102)
+    }
+    cuda(cudaMemsetAsync(boards, 0, (size_t)T * N, s), "memset");
+    cuda(cudaMemsetAsync(result, 0, T, s), "memset");
+    cuda(cudaMemcpyAsync(side, h_side.data(), T, cudaMemcpyHostToDevice, s), "copy");
+    cuda(cudaMemcpyAsync(a_moves, h_amv.data(), T, cudaMemcpyHostToDevice, s), "copy");
+    cuda(cudaMemcpyAsync(active, h_act.data(), T, cudaMemcpyHostToDevice, s), "copy");
+    int live = n;
+    for (int mv = 0; live > 0 && mv <= N && st == GZ_OK; ++mv) {
+      cuda(mcts_launch_reset(d, boards, side, s), "reset");
+      for (int w = 0; w < waves && st == GZ_OK; ++w) {
+        cuda(mcts_launch_select(d, s), "select");
+        if (st == GZ_OK) st = run_forward(net_a, d.leaf_board, d.leaf_side, (int)L, pi_a, v_a, s);
+        if (st == GZ_OK) st = run_forward(net_b, d.leaf_board, d.leaf_side, (int)L, pi_b, v_b, s);
+        cuda(arena_launch_merge((int)L, d.leaves, A, a_moves, pi_a, v_a, pi_b, v_b, m->d_pi, m->d_v, s), "merge");
+        cuda(mcts_launch_backup(d, m->d_pi, m->d_v, s), "backup");
+      }
+      cuda(mcts_launch_choose(d, 0, actions, s), "choose");
+      cuda(cudaMemsetAsync(n_active, 0, 4, s), "memset");
+      cuda(arena_launch_play(d.game, T, N, boards, side, a_moves, active, actions, result, n_active, s), "play");
+      cuda(cudaMemcpyAsync(&live, n_active, 4, cudaMemcpyDeviceToHost, s), "copy");
+      cuda(cudaStreamSynchronize(s), "synchronize");
+    }
+    cuda(cudaMemcpyAsync(h_res.data(), result, T, cudaMemcpyDeviceToHost, s), "copy");
+    cuda(cudaStreamSynchronize(s), "synchronize");
+    for (int t = 0; t < n && st == GZ_OK; ++t) {
+      wa += h_res[t] == 1;
+      wb += h_res[t] == 2;
+      dr += h_res[t] == 3;
+    }
+  }
+  cudaFreeAsync(buf, s);
+  cudaStreamSynchronize(s);
+  if (st != GZ_OK) return st;
+  if ((st = gz_mcts_check(m)) != GZ_OK) return st;
+  if ((st = gz_net_check(net_a)) != GZ_OK) return st;
+  if ((st = gz_net_check(net_b)) != GZ_OK) return st;
+  if (wa + wb + dr != n_games) return fail(GZ_ERR_TIMEOUT, "%d of %d games did not end", n_games - wa - wb - dr, n_games);
+  *a_wins = wa;
+  *b_wins = wb;
+  *draws = dr;
+  return GZ_OK;
+}
+
 gz_status gz_train_examples_save(const char* path, int n_iters, const gz_train_example* const* iters,
                                  const int32_t* counts) {
   if (!path || n_iters < 0 || (n_iters > 0 && (!iters || !counts))) return fail(GZ_ERR_INVALID_ARG, "bad arguments");

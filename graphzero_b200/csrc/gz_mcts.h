@@ -86,4 +86,14 @@ cudaError_t selfplay_launch_record(const MctsDev& d, const SelfPlayDev& s, int t
 cudaError_t selfplay_launch_finish(const MctsDev& d, const SelfPlayDev& s, const int32_t* actions, cudaStream_t st);
 cudaError_t selfplay_launch_emit(const MctsDev& d, const SelfPlayDev& s, cudaStream_t st);
 
+// Arena helpers (selfplay.cu): per-tree choice between two networks' leaf
+// evaluations, and the moves applied to the games in play (result per tree:
+// 1 = net A won, 2 = net B won, 3 = draw; n_active counts games still going).
+cudaError_t arena_launch_merge(int n_leaves, int leaves_per_tree, int A, const int8_t* a_moves, const float* pi_a,
+                               const float* v_a, const float* pi_b, const float* v_b, float* pi, float* v,
+                               cudaStream_t st);
+cudaError_t arena_launch_play(int game, int trees, int N, int8_t* boards, int8_t* side, int8_t* a_moves,
+                              int8_t* active, const int32_t* actions, int8_t* result, int* n_active,
+                              cudaStream_t st);
+
 }  // namespace gz

@@ -1,5 +1,6 @@
-// Self-play episodes on top of the batched search: every tree of a search
-// handle plays games back to back; each move records the root position and
+// Self-play episodes and arena games on top of the batched search.
+//
+// Self-play: every tree of a search handle plays games back to back; each move records the root position and
 // its visit-count policy, and when a game ends its examples get the outcome
 // and are copied, in a fixed order, to an output buffer of TrainingExample
 // records.
@@ -19,6 +20,12 @@
 //     (lowest action on ties), the limit of the reference's T = 1e-3;
 //   * games never exceed the board's number of cells, so no forced draw at
 //     MAX_GAME_LENGTH (self_play.cu:457-465) is needed.
+//
+// Arena (arena/arena.cu:31-106 with the NNet player of
+// players/players.cu:96-104): games between two networks, each move searched
+// from a fresh root by the side to move's network, the most visited move
+// played; the helper kernels here merge the two networks' leaf evaluations
+// per tree and apply the moves.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -162,7 +169,64 @@ __global__ void emit_kernel(MctsDev d, SelfPlayDev s) {
   }
 }
 
+// Arena: per leaf slot, the evaluation of the network that searches at the
+// slot's tree (net A where a_moves[tree], else net B).
+__global__ void arena_merge_kernel(int n_leaves, int leaves_per_tree, int A, const int8_t* __restrict__ a_moves,
+                                   const float* __restrict__ pi_a, const float* __restrict__ v_a,
+                                   const float* __restrict__ pi_b, const float* __restrict__ v_b,
+                                   float* __restrict__ pi, float* __restrict__ v) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n_leaves) return;
+  const bool a = a_moves[k / leaves_per_tree] != 0;
+  for (int j = 0; j < A; ++j) pi[(size_t)k * A + j] = a ? pi_a[(size_t)k * A + j] : pi_b[(size_t)k * A + j];
+  v[k] = a ? v_a[k] : v_b[k];
+}
+
+// Arena: the chosen moves applied to the games in play.  A game that ends
+// records its result (1 = net A won, 2 = net B won, 3 = draw) and goes back
+// to the empty board (searched but no longer played); otherwise the side to
+// move flips and so does which network moves.
+__global__ void arena_play_kernel(int game, int trees, int N, int8_t* __restrict__ boards, int8_t* __restrict__ side,
+                                  int8_t* __restrict__ a_moves, int8_t* __restrict__ active,
+                                  const int32_t* __restrict__ actions, int8_t* __restrict__ result,
+                                  int* __restrict__ n_active) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= trees || !active[t]) return;
+  int8_t b[kMctsBoardStride];
+  for (int i = 0; i < N; ++i) b[i] = boards[(size_t)t * N + i];
+  const int mover = side[t];
+  const int sq = apply_action(game, b, actions[t], mover);
+  const int oc = sq < 0 ? 2 : outcome_after(game, b, sq, mover);
+  if (oc != 0) {
+    result[t] = (int8_t)(oc == 2 ? 3 : (a_moves[t] ? 1 : 2));
+    active[t] = 0;
+    for (int i = 0; i < N; ++i) boards[(size_t)t * N + i] = 0;
+    side[t] = 1;
+    return;
+  }
+  for (int i = 0; i < N; ++i) boards[(size_t)t * N + i] = b[i];
+  side[t] = (int8_t)(-mover);
+  a_moves[t] = (int8_t)!a_moves[t];
+  atomicAdd(n_active, 1);
+}
+
 }  // namespace
+
+cudaError_t arena_launch_merge(int n_leaves, int leaves_per_tree, int A, const int8_t* a_moves, const float* pi_a,
+                               const float* v_a, const float* pi_b, const float* v_b, float* pi, float* v,
+                               cudaStream_t st) {
+  arena_merge_kernel<<<(n_leaves + 255) / 256, 256, 0, st>>>(n_leaves, leaves_per_tree, A, a_moves, pi_a, v_a, pi_b,
+                                                             v_b, pi, v);
+  return cudaGetLastError();
+}
+
+cudaError_t arena_launch_play(int game, int trees, int N, int8_t* boards, int8_t* side, int8_t* a_moves,
+                              int8_t* active, const int32_t* actions, int8_t* result, int* n_active,
+                              cudaStream_t st) {
+  arena_play_kernel<<<(trees + 127) / 128, 128, 0, st>>>(game, trees, N, boards, side, a_moves, active, actions,
+                                                          result, n_active);
+  return cudaGetLastError();
+}
 
 cudaError_t selfplay_launch_record(const MctsDev& d, const SelfPlayDev& s, int temp_moves, cudaStream_t st) {
   record_kernel<<<(d.trees + 127) / 128, 128, 0, st>>>(d, s, temp_moves);

@@ -245,6 +245,18 @@ gz_status gz_selfplay_run(gz_selfplay* sp, gz_net* net, int n_games, int sims, i
  * GZ_ERR_CAPACITY (nothing copied, buffer kept) if capacity is too small. */
 gz_status gz_selfplay_take(gz_selfplay* sp, gz_train_example* h_out, int64_t capacity, int64_t* n_examples,
                            int64_t* n_games);
+/* Arena (arena/arena.cu:31-106 play_game / play_games, used by
+ * pit_against_previous_version, self_play.cu:576-606): n_games games of
+ * net_a against net_b, played up to one game per tree of `m` at a time.
+ * Every move is searched from a fresh root with `sims` simulations by the
+ * network of the side to move, which plays its most visited move (the
+ * reference's NNet player, players/players.cu:96-104).  Net A moves first in
+ * the first n_games / 2 games, net B in the rest (the reference swaps the
+ * players half way, arena.cu:98-102).  Results count games won by each
+ * network and draws.  For a deterministic arena create `m` without root
+ * noise (dirichlet_eps 0); its trees are overwritten. */
+gz_status gz_arena_play(gz_mcts* m, gz_net* net_a, gz_net* net_b, int n_games, int sims, int32_t* a_wins,
+                        int32_t* b_wins, int32_t* draws, void* stream);
 /* save_train_examples (self_play.cu:510-534): the reference's file layout,
  * int32 number of iterations, then per iteration int32 count and count
  * 516-byte records (little endian).  iters[i] holds counts[i] examples. */
