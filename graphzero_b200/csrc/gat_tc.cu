@@ -23,9 +23,10 @@
 //               operand in shared memory; the result overwrites the head's
 //               accumulator columns
 //   3. out / z + bias, ELU, stored as the next layer's X tile (128-byte
-//      swizzled, K-major) -- or, after the last layer, mean-pooled into the
-//      value head (256->64 ReLU, 64->1 tanh) and column-pooled into the policy
-//      head (256->1 per column, softmax over 7), in fp32.
+//      swizzled, K-major) -- or, after the last layer, stored as fp16 in the
+//      same layout and read once: mean-pooled into the value head (256->64
+//      ReLU, 64->1 tanh) and column-pooled into the policy head (256->1 per
+//      column, softmax over 7), sums in fp32.
 // The next layer's projection does not wait for the head loop: heads c and
 // c + 4 write K chunk c of the next X tile, and each chunk's MMAs are issued
 // as soon as it exists, into a third accumulator block (tensor memory holds
@@ -116,14 +117,14 @@ constexpr int kSmMisc = kSmBar + kNumBars * 8;
 constexpr int kSmemBytes = kSmMisc + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 static_assert(kSmW % 1024 == 0 && kWChunk % 1024 == 0, "swizzled tiles need 1024-byte alignment");
-// last-layer head scratch inside the (then unused) X tile
-constexpr int kHeadRowStride = 33;                      // floats, padded
-constexpr int kSmHeadRows = kSmX;                       // [group][128][33] floats
-constexpr int kSmPooled = kSmHeadRows + 2 * 128 * kHeadRowStride * 4;  // [group][3][32] one head's node means
-constexpr int kSmZ = kSmPooled + 2 * kGPT * 32 * 4;     // [group][half][3][64] value-head partial sums
-constexpr int kSmLogit = kSmZ + 2 * 2 * kGPT * 64 * 4;  // [group][3][8] policy-logit partial sums
-constexpr int kSmLgAcc = kSmLogit + 2 * kGPT * 8 * 4;   // [group][96 pooling lanes][7] running sums
-static_assert(kSmLgAcc + 2 * kGPT * 32 * 7 * 4 <= kSmW, "head scratch fits in the X tile");
+// Last-layer head scratch: node means and policy partial sums in the t-score
+// region (free once a layer's head loop has its scores), value-head partial
+// sums in the X tile once the pooling has read it.
+constexpr int kSmMean = kSmTsc;                          // [3][256] floats
+constexpr int kSmLgW = kSmMean + kGPT * 256 * 4;         // [8 warps][3 x 7] floats
+static_assert(kSmLgW + kEpiWarps * kGPT * 7 * 4 <= kSmVec, "head sums fit in the t-score region");
+constexpr int kXZPart = 3 * 16384;                       // X tile offset of [8 warps][3][64] floats
+static_assert(kXZPart + kEpiWarps * kGPT * 64 * 4 <= 4 * 16384, "value partials fit in the X tile");
 
 // Offsets (floats) into the fp32 weight blob for Connect4 (gat_layout order).
 struct C4Off {
@@ -503,7 +504,6 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
       nidx[k] = in ? i + 7 * dr + dc : 128;
       saddr[k] = smem_u32(srow) + 2 * (in ? i + 7 * dr + dc - jw0 : 48);
     }
-    const int gbar = 3 + g;
     uint32_t aph = 0, dph[2] = {0, 0};
     bool ok = true;    // collective: changes only through epilogue_all
     bool wok = true;   // this thread's waits inside a layer; folded into the next vote
@@ -560,17 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
 #pragma unroll
         for (int k = 0; k < 9; ++k) tn[k] = tsc[nidx[k]];
 
-        float* hrow = (float*)(smem + kSmHeadRows) + g * 128 * kHeadRowStride;
-        float* pooled = (float*)(smem + kSmPooled) + g * kGPT * 32;
         float inv[4] = {0.f, 0.f, 0.f, 0.f};
-        // last layer: the heads are accumulated head by head.  Value head:
-        // thread (u, half) of the group sums pooled[c] W_v1[c][u] over the 16
-        // features c of its half of each head; policy head: the pooling lanes
-        // sum column-mean x w_pi over their feature.
-        // The running sums live in thread-private shared-memory slots.
-        const int gt = threadIdx.x & 127, vu = gt & 63, vhalf = gt >> 6;
-        float* zacc = (float*)(smem + kSmZ) + (g * 2 + vhalf) * kGPT * 64 + vu;  // [pg * 64]
-        float* lgacc = (float*)(smem + kSmLgAcc) + (g * kGPT * 32 + gt) * 7;     // pooling lanes only
 
         // P3: result of head t -> / z, + bias, ELU -> next X (or head pooling)
         auto finish_head = [&](int t) {
@@ -609,41 +599,18 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&x_ready[t]);
           } else {
-            // fp32 rows of this head into scratch, then per-position pooling
+            // last layer: the activations as fp16 (rounded to nearest) in the
+            // X tile's layout; the pooling reads them once all heads are done
+            uint8_t* xrow = sX + t * 16384 + (i >> 3) * 1024 + (i & 7) * 128;
 #pragma unroll
-            for (int k = 0; k < 16; ++k) {
-              hrow[i * kHeadRowStride + 2 * k + 0] = y[k].x;
-              hrow[i * kHeadRowStride + 2 * k + 1] = y[k].y;
+            for (int u = 0; u < 4; ++u) {
+              const int unit = (4 * g + u) ^ (i & 7);
+              uint32_t q[4];
+#pragma unroll
+              for (int m = 0; m < 4; ++m) q[m] = OpType<__half>::pack(y[4 * u + m].x, y[4 * u + m].y);
+              *(uint4*)(xrow + unit * 16) = make_uint4(q[0], q[1], q[2], q[3]);
             }
-            // this thread's W_v1 slice for the head (lands during the pooling)
-            float wv[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) wv[j] = __ldg(p.w + C4Off::W_v1 + (32 * h + 16 * vhalf + j) * 64 + vu);
-            named_bar_sync(gbar, 128);
-            if (gt < kGPT * 32) {
-              const int pg = gt >> 5, d = gt & 31;
-              float cs[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, tot = 0.f;
-#pragma unroll
-              for (int r = 0; r < 6; ++r)
-#pragma unroll
-                for (int c = 0; c < 7; ++c) {
-                  const float x = hrow[(pg * kN + r * 7 + c) * kHeadRowStride + d];
-                  cs[c] += x;
-                  tot += x;
-                }
-              pooled[pg * 32 + d] = tot * (kLn2 / kN);  // rows hold ELU log2(e)
-              const float wp = __ldg(p.w + C4Off::w_pi + 32 * h + d) * (kLn2 / 6.0f);
-#pragma unroll
-              for (int c = 0; c < 7; ++c) lgacc[c] = fmaf(cs[c], wp, t == 0 ? 0.f : lgacc[c]);
-            }
-            named_bar_sync(gbar, 128);  // node means visible; scratch reused by the next head
-#pragma unroll
-            for (int pg = 0; pg < kGPT; ++pg) {
-              float acc = t == 0 ? 0.f : zacc[pg * 64];
-#pragma unroll
-              for (int j = 0; j < 16; ++j) acc = fmaf(pooled[pg * 32 + 16 * vhalf + j], wv[j], acc);
-              zacc[pg * 64] = acc;
-            }
+            tc_fence_before();  // this head's tensor-memory reads precede the next tile's projection
           }
         };
 
@@ -719,31 +686,85 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
         finish_head(3);
         if constexpr (last) {
           // ---------------- heads (fp32) ----------------
-          float* zpart = (float*)(smem + kSmZ);
-          float* lgpart = (float*)(smem + kSmLogit);
-          if (gt < kGPT * 32) {
+          // One pass over the tile's activations: thread f (0..255) owns
+          // feature f and sums it over each position's 42 nodes (value head)
+          // and over each column's 6 nodes (policy head).  Scales: rows hold
+          // ELU log2(e), so means carry ln 2.
+          named_bar_sync(1, kEpiWarps * 32);  // every head's activations written
+          float* mean = (float*)(smem + kSmMean);  // [3][256] node means
+          float* lgw = (float*)(smem + kSmLgW);    // [warp][3 x 7] policy partial sums
+          {
+            const int f = threadIdx.x, hf = f >> 5;
+            const uint8_t* col = sX + (hf & 3) * 16384 + (f & 7) * 2;
+            const int unit0 = 4 * (hf >> 2) + ((f & 31) >> 3);
+            float lp[kGPT * 7];
+            const float wpf = __ldg(p.w + C4Off::w_pi + f) * (kLn2 / 6.0f);
 #pragma unroll
-            for (int c = 0; c < 7; ++c) {
-              float x = lgacc[c];
+            for (int pg = 0; pg < kGPT; ++pg) {
+              float tot = 0.f;
+#pragma unroll
+              for (int c = 0; c < 7; ++c) {
+                float cs = 0.f;
+#pragma unroll
+                for (int r = 0; r < 6; ++r) {
+                  const int row = pg * kN + r * 7 + c;
+                  const __half x = *(const __half*)(col + (row >> 3) * 1024 + (row & 7) * 128 + ((unit0 ^ (row & 7)) << 4));
+                  cs += __half2float(x);
+                }
+                tot += cs;
+                lp[pg * 7 + c] = cs * wpf;
+              }
+              mean[pg * 256 + f] = tot * (kLn2 / kN);
+            }
+#pragma unroll
+            for (int k = 0; k < kGPT * 7; ++k) {
+              float x = lp[k];
 #pragma unroll
               for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-              if (lane == 0) lgpart[(g * kGPT + (gt >> 5)) * 8 + c] = x;
+              if (lane == 0) lgw[warp * (kGPT * 7) + k] = x;
             }
           }
-          named_bar_sync(1, kEpiWarps * 32);  // partial sums of both groups visible
+          named_bar_sync(1, kEpiWarps * 32);  // means and policy partials visible; X tile read
+          // value head, first layer: warp w sums features 32 w .. 32 w + 31,
+          // lane l units 2 l, 2 l + 1 (each W_v1 element read once per tile)
+          float* zpart = (float*)(sX + kXZPart);  // [warp][3][64]
+          {
+            float a[kGPT][2] = {};
+#pragma unroll 8
+            for (int k = 0; k < 32; ++k) {
+              const int f = 32 * warp + k;
+              // W_v1 starts at an odd float offset of the blob: scalar loads
+              const float2 w2 = make_float2(__ldg(p.w + C4Off::W_v1 + f * 64 + 2 * lane),
+                                            __ldg(p.w + C4Off::W_v1 + f * 64 + 2 * lane + 1));
+#pragma unroll
+              for (int pg = 0; pg < kGPT; ++pg) {
+                const float m = mean[pg * 256 + f];
+                a[pg][0] = fmaf(m, w2.x, a[pg][0]);
+                a[pg][1] = fmaf(m, w2.y, a[pg][1]);
+              }
+            }
+#pragma unroll
+            for (int pg = 0; pg < kGPT; ++pg)
+              *(float2*)(zpart + (warp * kGPT + pg) * 64 + 2 * lane) = make_float2(a[pg][0], a[pg][1]);
+          }
+          named_bar_sync(1, kEpiWarps * 32);  // value partials visible
           if (warp < kGPT) {
             const int pg = warp, pos = tile * kGPT + pg;
             float z0 = __ldg(p.w + C4Off::b_v1 + lane), z1 = __ldg(p.w + C4Off::b_v1 + 32 + lane);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < kEpiWarps; ++q) {
               z0 += zpart[(q * kGPT + pg) * 64 + lane];
               z1 += zpart[(q * kGPT + pg) * 64 + 32 + lane];
             }
             float vv = fmaxf(z0, 0.f) * __ldg(p.w + C4Off::w_v2 + lane) + fmaxf(z1, 0.f) * __ldg(p.w + C4Off::w_v2 + 32 + lane);
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) vv += __shfl_xor_sync(0xffffffffu, vv, o);
-            const float lg = lane < 7 ? __ldg(p.w + C4Off::b_pi) + lgpart[pg * 8 + lane] + lgpart[(kGPT + pg) * 8 + lane]
-                                      : -INFINITY;
+            float lg = -INFINITY;
+            if (lane < 7) {
+              lg = __ldg(p.w + C4Off::b_pi);
+#pragma unroll
+              for (int q = 0; q < kEpiWarps; ++q) lg += lgw[q * (kGPT * 7) + pg * 7 + lane];
+            }
             float mx = lg;
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -757,6 +778,8 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
             }
           }
           named_bar_sync(1, kEpiWarps * 32);  // head scratch (X tile) free for the next encode
+          // the node means overwrote group 0's "no neighbour" t-score row: restore it
+          if (threadIdx.x < 4) ((float*)(smem + kSmTsc))[128 * 4 + threadIdx.x] = -INFINITY;
         }
         return true;
       };
