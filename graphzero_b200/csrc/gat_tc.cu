@@ -509,20 +509,33 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
     bool wok = true;   // this thread's waits inside a layer; folded into the next vote
 
 
+    // Thread t (of 256) encodes the first 16 features (t odd: the zero
+    // upper 8) of row t / 2.  Its board cell and side to move are fetched one
+    // tile ahead, during the previous tile's last layer, so the encode does
+    // not wait on memory.
+    static_assert(kEpiWarps * 32 == 2 * kRows, "one encode item per epilogue thread");
+    const int ej = threadIdx.x >> 1, ehalf = threadIdx.x & 1, egj = ej / kN, elj = ej % kN;
+    int ecell = 0, eside = 1;
+    auto fetch_cell = [&](int tile) {
+      const int pos = tile * kGPT + egj;
+      if (ehalf == 0 && egj < kGPT && tile < p.num_tiles && pos < p.n) {
+        ecell = p.boards[(size_t)pos * 42 + elj];
+        eside = p.side[pos];
+      }
+    };
+    fetch_cell(blockIdx.x);
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       // -- encode the tile's positions into X chunk 0 (features 0..15) --
-      for (int t = threadIdx.x; t < kRows * 2; t += kEpiWarps * 32) {
-        const int j = t >> 1, half = t & 1;
-        const int gj = j / kN, lj = j % kN;
-        const int pos = tile * kGPT + gj;
+      {
         uint32_t wv[4] = {0, 0, 0, 0};
-        if (half == 0 && gj < kGPT && pos < p.n) {
+        if (ehalf == 0 && egj < kGPT && tile * kGPT + egj < p.n) {
+          const int8_t cell[1] = {(int8_t)ecell};
           float f[4];
-          encode_node(kConnect4, p.boards + (size_t)pos * 42, p.side[pos], lj, f);
+          encode_node(kConnect4, cell, eside, 0, f);
           wv[0] = OpType<OpT>::pack(f[0], f[1]);
           wv[1] = OpType<OpT>::pack(f[2], f[3]);
         }
-        *(uint4*)(sX + sw128_offset(j, half * 8)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        *(uint4*)(sX + sw128_offset(ej, ehalf * 8)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -690,6 +703,25 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           // feature f and sums it over each position's 42 nodes (value head)
           // and over each column's 6 nodes (policy head).  Scales: rows hold
           // ELU log2(e), so means carry ln 2.
+          // the value head's weights for this thread (warp w: features
+          // 32 w .. 32 w + 31, lane l: units 2 l, 2 l + 1) and the head
+          // constants, loaded now so that their latency overlaps the pooling
+          float2 wv1[32];
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const float* src = p.w + C4Off::W_v1 + (32 * warp + k) * 64 + 2 * lane;  // odd offset: scalar loads
+            wv1[k] = make_float2(__ldg(src), __ldg(src + 1));
+          }
+          float hb[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // b_v1 (2), w_v2 (2), b_pi, b_v2
+          if (warp < kGPT) {
+            hb[0] = __ldg(p.w + C4Off::b_v1 + lane);
+            hb[1] = __ldg(p.w + C4Off::b_v1 + 32 + lane);
+            hb[2] = __ldg(p.w + C4Off::w_v2 + lane);
+            hb[3] = __ldg(p.w + C4Off::w_v2 + 32 + lane);
+            hb[4] = __ldg(p.w + C4Off::b_pi);
+            hb[5] = __ldg(p.w + C4Off::b_v2);
+          }
+          fetch_cell(tile + gridDim.x);  // the next tile's encode input
           named_bar_sync(1, kEpiWarps * 32);  // every head's activations written
           float* mean = (float*)(smem + kSmMean);  // [3][256] node means
           float* lgw = (float*)(smem + kSmLgW);    // [warp][3 x 7] policy partial sums
@@ -730,12 +762,10 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           float* zpart = (float*)(sX + kXZPart);  // [warp][3][64]
           {
             float a[kGPT][2] = {};
-#pragma unroll 8
+#pragma unroll
             for (int k = 0; k < 32; ++k) {
               const int f = 32 * warp + k;
-              // W_v1 starts at an odd float offset of the blob: scalar loads
-              const float2 w2 = make_float2(__ldg(p.w + C4Off::W_v1 + f * 64 + 2 * lane),
-                                            __ldg(p.w + C4Off::W_v1 + f * 64 + 2 * lane + 1));
+              const float2 w2 = wv1[k];
 #pragma unroll
               for (int pg = 0; pg < kGPT; ++pg) {
                 const float m = mean[pg * 256 + f];
@@ -750,18 +780,18 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
           named_bar_sync(1, kEpiWarps * 32);  // value partials visible
           if (warp < kGPT) {
             const int pg = warp, pos = tile * kGPT + pg;
-            float z0 = __ldg(p.w + C4Off::b_v1 + lane), z1 = __ldg(p.w + C4Off::b_v1 + 32 + lane);
+            float z0 = hb[0], z1 = hb[1];
 #pragma unroll
             for (int q = 0; q < kEpiWarps; ++q) {
               z0 += zpart[(q * kGPT + pg) * 64 + lane];
               z1 += zpart[(q * kGPT + pg) * 64 + 32 + lane];
             }
-            float vv = fmaxf(z0, 0.f) * __ldg(p.w + C4Off::w_v2 + lane) + fmaxf(z1, 0.f) * __ldg(p.w + C4Off::w_v2 + 32 + lane);
+            float vv = fmaxf(z0, 0.f) * hb[2] + fmaxf(z1, 0.f) * hb[3];
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) vv += __shfl_xor_sync(0xffffffffu, vv, o);
             float lg = -INFINITY;
             if (lane < 7) {
-              lg = __ldg(p.w + C4Off::b_pi);
+              lg = hb[4];
 #pragma unroll
               for (int q = 0; q < kEpiWarps; ++q) lg += lgw[q * (kGPT * 7) + pg * 7 + lane];
             }
@@ -774,7 +804,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
             for (int o = 16; o >= 1; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
             if (pos < p.n) {
               if (lane < 7) p.pi[(size_t)pos * 7 + lane] = ex / z;
-              if (lane == 0) p.v[pos] = tanhf(vv + __ldg(p.w + C4Off::b_v2));
+              if (lane == 0) p.v[pos] = tanhf(vv + hb[5]);
             }
           }
           named_bar_sync(1, kEpiWarps * 32);  // head scratch (X tile) free for the next encode
