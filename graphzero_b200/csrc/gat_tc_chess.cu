@@ -61,6 +61,7 @@ constexpr uint32_t kScoreCol = kAlphaCol + 64;          // aliases e buffer (0, 
 constexpr uint32_t kPolCol = kAlphaCol;                 // policy accumulator, after the last gathers
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kMaxDeg = 36;                             // queen lines (27 max) + knights (8) + self
 
 // chess graph degree of a square (queen lines + knight + self), host/device
@@ -175,10 +176,14 @@ __device__ __forceinline__ float comp(const float4& v, int k) {
   return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
 }
 
-__device__ __forceinline__ float2 elu2(float2 y) {
-  const float2 zl = __fmul2_rn(y, make_float2(kLog2e, kLog2e));
-  const float2 em = __fadd2_rn(make_float2(ex2_approx(-fabsf(zl.x)), ex2_approx(-fabsf(zl.y))), make_float2(-1.f, -1.f));
-  return make_float2(fmaxf(em.x, y.x), fmaxf(em.y, y.y));
+// Activations are carried multiplied by log2(e) from the first ELU on (the
+// next projection, its attention scores, the softmax and the policy softmax
+// then work in base 2 at no cost; the value head multiplies by ln 2 once).
+// For u = y log2(e) this returns ELU(y) log2(e) = max((2^(-|u|) - 1) log2(e), u).
+__device__ __forceinline__ float2 elu2_log2e(float2 u) {
+  const float2 em = make_float2(ex2_approx(-fabsf(u.x)), ex2_approx(-fabsf(u.y)));
+  const float2 m = __ffma2_rn(em, make_float2(kLog2e, kLog2e), make_float2(-kLog2e, -kLog2e));
+  return make_float2(fmaxf(m.x, u.x), fmaxf(m.y, u.y));
 }
 
 // Sum of v[0..31] over the 32 lanes, scattered: lane d returns the sum of
@@ -439,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
       auto layer = [&](int l, auto last_tag) -> bool {
         constexpr bool last = decltype(last_tag)::value;
         float* vec = (float*)(smem + kSmVec) + (l & 1) * kVecFloats;
-        vec[threadIdx.x] = __ldg(p.w + ChOff::b(l) + threadIdx.x);
+        vec[threadIdx.x] = __ldg(p.w + ChOff::b(l) + threadIdx.x) * kLog2e;
         wok = mbar_wait(acc_full, aph & 1, abort_flag, kWaitLimitNs) && wok;
         ok = epilogue_all(wok);
         ++aph;
@@ -482,8 +487,8 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const float4 bv = bias4[k];
-            y[2 * k] = elu2(__ffma2_rn(make_float2(o[4 * k], o[4 * k + 1]), iv, make_float2(bv.x, bv.y)));
-            y[2 * k + 1] = elu2(__ffma2_rn(make_float2(o[4 * k + 2], o[4 * k + 3]), iv, make_float2(bv.z, bv.w)));
+            y[2 * k] = elu2_log2e(__ffma2_rn(make_float2(o[4 * k], o[4 * k + 1]), iv, make_float2(bv.x, bv.y)));
+            y[2 * k + 1] = elu2_log2e(__ffma2_rn(make_float2(o[4 * k + 2], o[4 * k + 3]), iv, make_float2(bv.z, bv.w)));
           }
           // next layer's operand (the last layer's feeds the policy MMA)
           {
@@ -520,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
               float acc = t == 0 ? 0.f : zacc[q2 * 64];
 #pragma unroll
               for (int j = 0; j < 16; ++j)
-                acc = fmaf((pa[16 * vhalf + j] + pa[32 + 16 * vhalf + j]) * (1.0f / kN), wv[j], acc);
+                acc = fmaf((pa[16 * vhalf + j] + pa[32 + 16 * vhalf + j]) * (kLn2 / kN), wv[j], acc);
               zacc[q2 * 64] = acc;
             }
             named_bar_sync(gbar, 128);  // pool slots reused by the next head
@@ -551,18 +556,19 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
               tmax = fmaxf(tmax, tj[k]);
             }
             const float xm = s[t] + tmax;
-            const float c = -fmaxf(xm, kLeakySlope * xm) * kLog2e;
+            const float c = -fmaxf(xm, kLeakySlope * xm);  // scores are in base 2
             float z = 0.f;
             const uint32_t sbase = smem_u32(srow);
 #pragma unroll
             for (int k = 0; k < kMaxDeg; ++k) {
               const float x = s[t] + tj[k];
-              const __half e = __float2half_rn(ex2_approx(fmaf(fmaxf(x, kLeakySlope * x), kLog2e, c)));
+              const __half e = __float2half_rn(ex2_approx(fmaxf(x, kLeakySlope * x) + c));
               z += __half2float(e);
               // absent neighbours write the pad half-word (64) of the row
               asm volatile("st.shared.b16 [%0], %1;" ::"r"(sbase + 2 * my_nbr[k]), "h"(__half_as_ushort(e)) : "memory");
             }
-            inv[t] = __frcp_rn(z);
+            // layer 0 reads the raw features: its Wh carries no log2(e) yet
+            inv[t] = rcp_approx(z) * (l == 0 ? kLog2e : 1.f);
             uint32_t a[32];
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
@@ -615,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
         float mx = -INFINITY;
 #pragma unroll
         for (int k = 0; k < kP; ++k) {
-          lgt[k] += __ldg(p.w + ChOff::b_pi + k);
+          lgt[k] += __ldg(p.w + ChOff::b_pi + k) * kLog2e;  // logits in base 2
           mx = fmaxf(mx, lgt[k]);
         }
 #pragma unroll
@@ -626,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
         float z = 0.f;
 #pragma unroll
         for (int k = 0; k < kP; ++k) {
-          lgt[k] = ex2_approx((lgt[k] - mx) * kLog2e);
+          lgt[k] = ex2_approx(lgt[k] - mx);
           z += lgt[k];
         }
 #pragma unroll
@@ -717,6 +723,7 @@ __global__ void pack_chess_kernel(const float* __restrict__ w, uint8_t* __restri
     float acc = 0.f;
     if (k < fin)
       for (int f = 0; f < 32; ++f) acc = fmaf(W[(size_t)k * 256 + 32 * h + f], A[(2 * h + v) * 32 + f], acc);
+    if (layer == 0) acc *= kLog2e;  // layer 0's scores in base 2, like the later layers'
     const float hi = OpType<OpT>::round(acc);
     *(uint16_t*)(dst + sw128_offset(256 + j, kk)) = OpType<OpT>::bits(hi);
     *(uint16_t*)(dst + sw128_offset(272 + j, kk)) = OpType<OpT>::bits(acc - hi);
