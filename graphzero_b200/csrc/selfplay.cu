@@ -129,10 +129,11 @@ __device__ int block_exclusive_sum(int x, int* total) {
 // One block: the games that ended this move, in tree order, appended to the
 // output as TrainingExample records (board and pi zero-padded to 64).
 __global__ void emit_kernel(MctsDev d, SelfPlayDev s) {
-  __shared__ int base_ex, base_games;
+  __shared__ int base_ex, base_games, first_lost;
   if (threadIdx.x == 0) {
     base_ex = *s.out_count;
     base_games = *s.games_done;
+    first_lost = s.out_cap;  // where the first game that did not fit would have gone
   }
   __syncthreads();
   for (int t0 = 0; t0 < d.trees; t0 += blockDim.x) {
@@ -145,6 +146,7 @@ __global__ void emit_kernel(MctsDev d, SelfPlayDev s) {
       const int dst = base_ex + off;
       if (dst + n > s.out_cap) {
         atomicExch(s.overflow, 2);
+        atomicMin(&first_lost, dst);
       } else {
         for (int k = 0; k < n; ++k) {
           const size_t slot = (size_t)t * s.max_moves + k;
@@ -164,7 +166,9 @@ __global__ void emit_kernel(MctsDev d, SelfPlayDev s) {
     __syncthreads();
   }
   if (threadIdx.x == 0) {
-    *s.out_count = base_ex < s.out_cap ? base_ex : s.out_cap;
+    // after an overflow the buffer holds the games before the first one that
+    // did not fit (later games that would have fitted are dropped with it)
+    *s.out_count = base_ex < first_lost ? base_ex : first_lost;
     *s.games_done = base_games;
   }
 }

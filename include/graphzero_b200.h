@@ -238,7 +238,9 @@ gz_status gz_selfplay_destroy(gz_selfplay* sp);
  * chosen as gz_mcts_choose does, the roots advanced (a finished game's tree
  * starts a new game).  Ended games' examples go to the buffer in the order
  * the games ended (ties: tree order).  Synchronises once per move.
- * GZ_ERR_CAPACITY when the buffer overflows (gz_selfplay_take empties it). */
+ * GZ_ERR_CAPACITY when the buffer overflows: it then holds the games that
+ * ended before the first one that did not fit, the rest of that move's
+ * ended games are lost (gz_selfplay_take empties the buffer). */
 gz_status gz_selfplay_run(gz_selfplay* sp, gz_net* net, int n_games, int sims, int temp_moves, void* stream);
 /* Copies the buffered examples to the host, in order, and empties the
  * buffer; *n_examples and *n_games (either may be NULL) receive the counts.

@@ -175,3 +175,8 @@ def test_selfplay_buffer_overflow_is_reported(cuda):
     with pytest.raises(gz.GZError) as e:
         sp.run(net, 8, 16, 2)
     assert e.value.status == gz.ERR_CAPACITY
+    # what the buffer keeps are whole games, each opening on the empty board
+    ex, _ = sp.take()
+    assert ex.size <= 5
+    if ex.size:
+        assert (ex["board"][0] == 0).all()
