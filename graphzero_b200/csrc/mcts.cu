@@ -104,14 +104,21 @@ __global__ void select_kernel(MctsDev d) {
     int s = d.root[t];
     int depth = 0;
     if (lane == 0) pn[0] = s;
-    while (d.expanded[nb + s] && !d.terminal[nb + s]) {
-      const int ne = d.n_edges[nb + s], fe = d.first_edge[nb + s];
-      const int np = d.n[nb + s] + d.vl_k * d.vl[nb + s];
+    while (true) {
+      // the node's fields in one round of loads (read before the test: the
+      // fields of an unexpanded node are read and not used)
+      const size_t gs = nb + s;
+      const int8_t expanded = d.expanded[gs], terminal = d.terminal[gs];
+      const int ne = d.n_edges[gs], fe = d.first_edge[gs];
+      const int np = d.n[gs] + d.vl_k * d.vl[gs];
+      if (!expanded || terminal) break;
       const float sq = __fsqrt_rn((float)np);
       float u = -INFINITY;
       int idx = 0x7fffffff;
+      int child = -1;  // this lane's edge's child, loaded with the edge's statistics
       if (lane < ne) {
         const size_t e = eb + fe + lane;
+        child = d.child[e];
         const int vlk = d.vl_k * d.VL[e];
         const int nev = d.Nv[e] + vlk;
         const float q = nev > 0 ? __fdiv_rn(__fsub_rn(d.W[e], (float)vlk), (float)nev) : 0.0f;
@@ -128,11 +135,10 @@ __global__ void select_kernel(MctsDev d) {
         if (uo > u || (uo == u && io < idx)) { u = uo; idx = io; }
       }
       const int e = fe + idx;
-      int c = 0;
+      int c = __shfl_sync(kFull, child, idx);
       if (lane == 0) {
         d.vl[nb + s] += 1;
         d.VL[eb + e] += 1;
-        c = d.child[eb + e];
         if (c < 0) {
           c = d.node_count[t];
           if (c >= d.node_cap) {
