@@ -252,20 +252,23 @@ __global__ void backup_kernel(MctsDev d, const float* __restrict__ pi, const flo
       }
     }
     __syncwarp();
+    // The path's levels touch distinct nodes and edges, so the lanes update
+    // them at once; the value at level i is -val for i = len - 1 and changes
+    // sign every level up (the same additions as a walk from the leaf, and
+    // the leaves of a tree still back up in order).
     if (lane == 0) {
       d.n[gl] += 1;
       d.vl[gl] -= 1;
-      float x = -val;
-      for (int i = len - 1; i >= 0; --i) {
-        const size_t e = eb + pe[i];
-        d.Nv[e] += 1;
-        d.W[e] = __fadd_rn(d.W[e], x);
-        d.VL[e] -= 1;
-        const size_t gs = nb + pn[i];
-        d.n[gs] += 1;
-        d.vl[gs] -= 1;
-        x = -x;
-      }
+    }
+    for (int i = lane; i < len; i += 32) {
+      const float x = ((len - 1 - i) & 1) ? val : -val;
+      const size_t e = eb + pe[i];
+      d.Nv[e] += 1;
+      d.W[e] = __fadd_rn(d.W[e], x);
+      d.VL[e] -= 1;
+      const size_t gs = nb + pn[i];
+      d.n[gs] += 1;
+      d.vl[gs] -= 1;
     }
     __syncwarp();
   }
