@@ -110,16 +110,19 @@ __global__ void select_kernel(MctsDev d) {
       const size_t gs = nb + s;
       const int8_t expanded = d.expanded[gs], terminal = d.terminal[gs];
       const int ne = d.n_edges[gs], fe = d.first_edge[gs];
-      const int np = d.n[gs] + d.vl_k * d.vl[gs];
+      const int vl_s = d.vl[gs];
+      const int np = d.n[gs] + d.vl_k * vl_s;
       if (!expanded || terminal) break;
       const float sq = __fsqrt_rn((float)np);
       float u = -INFINITY;
       int idx = 0x7fffffff;
-      int child = -1;  // this lane's edge's child, loaded with the edge's statistics
+      int child = -1;  // this lane's edge's child and virtual visits, loaded with its statistics
+      int vl_e = 0;
       if (lane < ne) {
         const size_t e = eb + fe + lane;
         child = d.child[e];
-        const int vlk = d.vl_k * d.VL[e];
+        vl_e = d.VL[e];
+        const int vlk = d.vl_k * vl_e;
         const int nev = d.Nv[e] + vlk;
         const float q = nev > 0 ? __fdiv_rn(__fsub_rn(d.W[e], (float)vlk), (float)nev) : 0.0f;
         const float u1 = __fmul_rn(d.c_puct, d.P[e]);
@@ -136,9 +139,10 @@ __global__ void select_kernel(MctsDev d) {
       }
       const int e = fe + idx;
       int c = __shfl_sync(kFull, child, idx);
-      if (lane == 0) {
-        d.vl[nb + s] += 1;
-        d.VL[eb + e] += 1;
+      const int vl_c = __shfl_sync(kFull, vl_e, idx);
+      if (lane == 0) {  // virtual visits: the values loaded above, stored back incremented
+        d.vl[nb + s] = vl_s + 1;
+        d.VL[eb + e] = vl_c + 1;
         if (c < 0) {
           c = d.node_count[t];
           if (c >= d.node_cap) {
