@@ -53,13 +53,14 @@ constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
 constexpr int kWChunk = 16384;              // 128 co rows x 64 ci x 2 B
 constexpr int kChunksPerTile = 9 + (kConvs - 1) * 18;
-// The ring moves one tap per copy: both 64-channel chunks of a block conv's
-// tap (adjacent in the packed weights, 32 KB), or the stem's one chunk.  A
-// 32 KB bulk copy moves about 1.7x the bytes per cycle of a 16 KB one from
-// L2 (measured on B200 with every SM streaming), and the weights are
-// re-streamed for every tile.
-constexpr int kWSlot = 2 * kWChunk;
-constexpr int kWSlots = 2;
+// The ring moves one 64-channel chunk (16 KB) per copy, four slots deep: a
+// tap's two chunks land in two slots, and up to two taps' copies are in
+// flight while the MMAs of the current one run (measured on B200: faster
+// than two 32 KB slots holding a whole tap each, whose single copy in flight
+// exposed its L2 latency at every tap).  The weights are re-streamed for
+// every tile.
+constexpr int kWSlot = kWChunk;
+constexpr int kWSlots = 4;
 constexpr uint32_t kTmemCols = 256;         // slot s accumulates in columns [128 s, 128 s + 128)
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
 constexpr int kGuard = 8;                   // guard rows before and after
@@ -216,16 +217,18 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
       bool ok = true;
       // consumption order: per tile pair, per conv, slot A's nine taps then slot B's
       for (int ta = blockIdx.x; ta < p.num_tiles && ok; ta += 2 * gridDim.x)
-        for (int u = 0; u < 18 * kConvs && ok; ++u, ++q) {
-          const int s = q % kWSlots;
+        for (int u = 0; u < 18 * kConvs && ok; ++u) {
           const int cv = u / 18, t = u % 9;
-          // stem tap: one chunk; block conv tap: its two adjacent chunks
-          const int c = cv == 0 ? t : 9 + (cv - 1) * 18 + 2 * t;
-          const uint32_t bytes = cv == 0 ? kWChunk : kWSlot;
-          ok = mbar_wait(&empty[s], ((q / kWSlots) & 1) ^ 1, abort_flag, kWaitLimitNs);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&full[s], bytes);
-          bulk_g2s(smem + kSmW + s * kWSlot, p.packed + (size_t)c * kWChunk, bytes, &full[s]);
+          // stem tap: one chunk; block conv tap: its two adjacent chunks, one slot each
+          const int nchunk = cv == 0 ? 1 : 2;
+          for (int h = 0; h < nchunk && ok; ++h, ++q) {
+            const int s = q % kWSlots;
+            const int c = cv == 0 ? t : 9 + (cv - 1) * 18 + 2 * t + h;
+            ok = mbar_wait(&empty[s], ((q / kWSlots) & 1) ^ 1, abort_flag, kWaitLimitNs);
+            if (!ok) break;
+            mbar_arrive_expect_tx(&full[s], kWChunk);
+            bulk_g2s(smem + kSmW + s * kWSlot, p.packed + (size_t)c * kWChunk, kWChunk, &full[s]);
+          }
         }
       for (uint32_t k = (q > kWSlots ? q - kWSlots : 0); k < q; ++k)
         mbar_wait(&full[k % kWSlots], (k / kWSlots) & 1, abort_flag, kWaitLimitNs);
@@ -258,21 +261,21 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
           for (int t = 0; t < 9; ++t) {
             const int shift = 7 * tap_dy(t) + tap_dx(t);  // rows; x 128 bytes
             if (!ok) break;
-            const int s = q % kWSlots;
-            ok = mbar_wait(&full[s], (q / kWSlots) & 1, abort_flag, kWaitLimitNs);
-            ++q;
-            if (!ok) break;
-            tc_fence_after();
-            for (int c = 0; c < nchunk; ++c) {  // 64-channel K chunks of this tap's slot
-              const uint64_t wd = w_desc + (uint64_t)((s * kWSlot + c * kWChunk) >> 4);
+            for (int c = 0; c < nchunk && ok; ++c) {  // 64-channel K chunks of this tap, one slot each
+              const int s = q % kWSlots;
+              ok = mbar_wait(&full[s], (q / kWSlots) & 1, abort_flag, kWaitLimitNs);
+              ++q;
+              if (!ok) break;
+              tc_fence_after();
+              const uint64_t wd = w_desc + (uint64_t)((s * kWSlot) >> 4);
               const uint64_t ad = in_desc + (uint64_t)((c * kActChunk + shift * 128) >> 4);
               mma_f16_ss_masked(dt, ad, wd, idesc, (t | c) != 0, kMask.m[t]);
               if (cv != 0) {
 #pragma unroll
                 for (int kk = 1; kk < 4; ++kk) mma_f16_ss_masked(dt, ad + kk * 2, wd + kk * 2, idesc, 1, kMask.m[t]);
               }
+              mma_commit(&empty[s]);
             }
-            mma_commit(&empty[s]);
           }
           if (ok) mma_commit(&acc_full[sl]);
         }
