@@ -3,16 +3,21 @@
 GPU), plus batched-search simulations per second, on 1..8 B200s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c1|c0|c2|c3] [--mcts-moves M]
+                    [--config c1|c0|c2|c3] [--mcts-moves M] [--no-other-configs]
 
 One step = one forward pass over one batch of positions.  Multi-GPU runs
 are launched with torchrun (one process per GPU); every rank evaluates its
 own shard of positions with the network replicated (weak scaling), the
 weights reach every GPU through one NCCL broadcast before timing, and the
 reported time is the maximum over ranks.  Prints ONE JSON line on rank 0.
+The c1 line also carries, under "configs", the other leaf-evaluation
+workloads (c0 TicTacToe fp32, c2 Connect4 ResNet, c3 chess GAT) measured on
+the same GPU, each with its roofline and CPU baseline.
 
 --impl reference times the CPU restatement of the same math (the reference's
-own network code does not build) on the host cores with all threads.
+own network code does not build) on the host cores with all threads; that
+arm builds its weights and positions with the oracle's own generator and
+never loads the product library.
 """
 from __future__ import annotations
 
@@ -31,30 +36,67 @@ sys.path[:0] = [str(ROOT), str(ROOT / "oracle")]
 
 import numpy as np  # noqa: E402
 
-import graphzero_b200 as gz  # noqa: E402
-from graphzero_b200 import dist as gzd  # noqa: E402
+# The product package (graphzero_b200, which loads libgraphzero_b200.so) is
+# imported only by the product arm; the reference arm runs on the oracle alone.
 
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAK_TFLOPS = 1590.0
+# fp32 CUDA-core peak for the TicTacToe fp32 workload: 148 SMs x 128 fp32
+# lanes x 2 FLOP (FMA) x 1.965 GHz (nominal, computed; not measured here).
+FP32_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+TICTACTOE, CONNECT4, CHESS = 0, 1, 2
+GAT, RESNET = 0, 1
+PREC_AUTO, PREC_FP32 = 0, 1
+BASE_SEED = 0x6A5A
+BOARD_BYTES = {TICTACTOE: 9, CONNECT4: 42, CHESS: 66}
 
 CONFIGS = {
-    "c0": dict(index=0, game=gz.TICTACTOE, kind=gz.GAT, batch=256, precision=gz.PREC_FP32, dtype="f32",
+    "c0": dict(index=0, game=TICTACTOE, kind=GAT, batch=256, precision=PREC_FP32, steps=300,
                workload="TicTacToe GAT forward, 4 layers 8x32 heads, fp32, batch 256 per GPU"),
-    "c1": dict(index=1, game=gz.CONNECT4, kind=gz.GAT, batch=4096, precision=gz.PREC_AUTO, dtype="bf16",
-               workload="Connect4 GAT leaf evaluation, 6 layers 8x32 heads, bf16 operands fp32 accumulate, "
-                        "batch 4096 per GPU"),
-    "c2": dict(index=2, game=gz.CONNECT4, kind=gz.RESNET, batch=4096, precision=gz.PREC_AUTO, dtype="bf16",
+    "c1": dict(index=1, game=CONNECT4, kind=GAT, batch=4096, precision=PREC_AUTO, steps=2000,
+               workload="Connect4 GAT leaf evaluation, 6 layers 8x32 heads, 16-bit tensor-core operands "
+                        "(fp16 by default), fp32 accumulate, batch 4096 per GPU"),
+    "c2": dict(index=2, game=CONNECT4, kind=RESNET, batch=4096, precision=PREC_AUTO, steps=300,
                workload="Connect4 ResNet leaf evaluation, 3x3 stem + 10 residual blocks of 128 channels, "
-                        "bf16 operands fp32 accumulate, batch 4096 per GPU"),
-    "c3": dict(index=3, game=gz.CHESS, kind=gz.GAT, batch=8192, precision=gz.PREC_AUTO, dtype="bf16",
+                        "16-bit tensor-core operands (fp16 by default), fp32 accumulate, batch 4096 per GPU"),
+    "c3": dict(index=3, game=CHESS, kind=GAT, batch=8192, precision=PREC_AUTO, steps=100,
                workload="Chess GAT leaf evaluation, 64 nodes x 18 features, queen+knight graph (1856 edges), "
-                        "8 layers 8x32 heads, 4672-way policy, bf16 operands fp32 accumulate, batch 8192 per GPU"),
+                        "8 layers 8x32 heads, 4672-way policy, 16-bit tensor-core operands (fp16 by default), "
+                        "fp32 accumulate, batch 8192 per GPU"),
 }
 
 
+def rank_env() -> tuple[int, int, int]:
+    """(rank, world, local_rank) from the torchrun environment."""
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def shard_seed(config_index: int, rank: int) -> int:
+    """Per-rank input seed: base + 1000 x config + rank (graphzero_b200.dist)."""
+    return BASE_SEED + 1000 * config_index + rank
+
+
+def pool_batches(cfg: dict) -> int:
+    """Distinct batches cycled by the device-timed loop: more board bytes
+    than L2, so no batch is read from L2 twice in a row."""
+    return max(8, math.ceil(1.05 * L2_BYTES / (cfg["batch"] * BOARD_BYTES[cfg["game"]])))
+
+
+def config_block(cfg: dict, world: int) -> dict:
+    """The workload description; identical in both arms."""
+    B = cfg["batch"]
+    nb = pool_batches(cfg)
+    return {"workload": cfg["workload"], "batch_per_gpu": B, "global_batch": B * world,
+            "positions": "uniform random legal playouts (seeded per rank)",
+            "weights": "Glorot-uniform from seed, bf16-representable",
+            "l2": f"inputs larger than L2: {nb} distinct batches ({nb * B * BOARD_BYTES[cfg['game']] / 2**20:.0f} "
+                  f"MiB of boards) cycled on the GPU",
+            "parallelism": f"dp{world} (independent shards, one NCCL weight broadcast)"}
+
+
 def metric_name(cfg: dict) -> str:
-    net = {gz.TICTACTOE: "TicTacToe", gz.CONNECT4: "Connect4", gz.CHESS: "Chess"}[cfg["game"]]
-    kind = "GAT" if cfg["kind"] == gz.GAT else "ResNet"
+    net = {TICTACTOE: "TicTacToe", CONNECT4: "Connect4", CHESS: "Chess"}[cfg["game"]]
+    kind = "GAT" if cfg["kind"] == GAT else "ResNet"
     return f"leaf evals/sec ({net} {kind}, b={cfg['batch']})"
 
 
@@ -68,16 +110,25 @@ def resnet_gemm_flops() -> float:
     return f
 
 
+GAT_SHAPES = {TICTACTOE: dict(nodes=9, features=4, layers=4, policy_per_node=1),
+              CONNECT4: dict(nodes=42, features=4, layers=6, policy_per_node=1),
+              CHESS: dict(nodes=64, features=18, layers=8, policy_per_node=73)}
+
+
 def gat_gemm_flops(game: int) -> float:
     """Algorithmic GEMM FLOPs per position: projections + head GEMMs."""
-    s = gz.game_shape(game)
-    f = 2.0 * s.nodes * (s.features * 256 + (s.layers - 1) * 256 * 256)
+    s = GAT_SHAPES[game]
+    f = 2.0 * s["nodes"] * (s["features"] * 256 + (s["layers"] - 1) * 256 * 256)
     f += 2.0 * 256 * 64 + 2.0 * 64  # value head
-    if game == gz.CONNECT4:
+    if game == CONNECT4:
         f += 2.0 * 7 * 256
     else:
-        f += 2.0 * s.nodes * 256 * s.policy_per_node
+        f += 2.0 * s["nodes"] * 256 * s["policy_per_node"]
     return f
+
+
+def flops_per_position(cfg: dict) -> float:
+    return gat_gemm_flops(cfg["game"]) if cfg["kind"] == GAT else resnet_gemm_flops()
 
 
 def measured_peak() -> tuple[float, str]:
@@ -156,21 +207,53 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-def cpu_baseline(cfg: dict, w: np.ndarray, seconds: float = 10.0) -> dict:
+def oracle_inputs(cfg: dict, n: int, seed: int, first: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """Positions from the oracle's own generator (bit-identical to the
+    product's for TicTacToe and Connect4).  Chess has no legal-move generator
+    in the oracle: random piece placements of the same record format stand
+    in (the forward's cost does not depend on the position)."""
+    import oracle
+
+    if cfg["game"] != CHESS:
+        return oracle.synth_positions(cfg["game"], n, seed, first)
+    rng = np.random.default_rng(seed + first)
+    b = np.zeros((n, 66), np.int8)
+    for i in range(n):
+        sq = rng.choice(64, size=int(rng.integers(2, 33)), replace=False)
+        b[i, sq] = rng.choice([-6, -5, -4, -3, -2, -1, 1, 2, 3, 4, 5, 6], size=sq.size)
+        b[i, 64] = rng.integers(0, 16)
+        b[i, 65] = -1
+    return b, rng.choice([-1, 1], size=n).astype(np.int8)
+
+
+def oracle_weights(cfg: dict) -> np.ndarray:
+    import oracle
+
+    seed = shard_seed(cfg["index"], 0)
+    return oracle.synth_gat_weights(cfg["game"], seed) if cfg["kind"] == GAT else oracle.synth_res_weights(seed)
+
+
+def oracle_forward(cfg: dict, w: np.ndarray, threads: int):
+    import oracle
+
+    if cfg["kind"] == GAT:
+        return lambda b, s: oracle.gat_forward(cfg["game"], w, b, s, threads=threads, native=True)
+    return lambda b, s: oracle.resnet_forward(w, b, s, threads=threads, native=True)
+
+
+def cpu_baseline(cfg: dict, seconds: float = 10.0) -> dict:
     """The oracle (C++ restatement of the same math, AVX2 build) on all host
-    cores over a bounded sample of the same workload."""
+    cores over a bounded sample of the same workload (inputs and weights
+    from the oracle's generator)."""
     import oracle
 
     threads = oracle.cpu_threads()
-    game = cfg["game"]
+    fwd = oracle_forward(cfg, oracle_weights(cfg), threads)
     chunk = 32 * threads
     done, t0, i = 0, time.perf_counter(), 0
     while True:
-        boards, side = gz.synth_positions(game, chunk, seed=gzd.shard_seed(cfg["index"], 0) + 77, first=i * chunk)
-        if cfg["kind"] == gz.GAT:
-            oracle.gat_forward(game, w, boards, side, threads=threads, native=True)
-        else:
-            oracle.resnet_forward(w, boards, side, threads=threads, native=True)
+        boards, side = oracle_inputs(cfg, chunk, shard_seed(cfg["index"], 0) + 77, first=i * chunk)
+        fwd(boards, side)
         done += chunk
         i += 1
         el = time.perf_counter() - t0
@@ -182,25 +265,23 @@ def cpu_baseline(cfg: dict, w: np.ndarray, seconds: float = 10.0) -> dict:
 
 
 def reference_arm(args, cfg: dict) -> None:
-    info = gzd.rank_info()
-    if info.rank != 0:
+    """The CPU restatement on the host cores (rank 0 only): the reference's
+    own network code does not build.  Uses the oracle alone."""
+    rank, _, _ = rank_env()
+    if rank != 0:
         return
     import oracle
 
     threads = oracle.cpu_threads()
-    game = cfg["game"]
-    w = gz.synth_weights(game, cfg["kind"], seed=gzd.shard_seed(cfg["index"], 0))
-    fwd = (lambda b, s: oracle.gat_forward(game, w, b, s, threads=threads, native=True)) if cfg["kind"] == gz.GAT \
-        else (lambda b, s: oracle.resnet_forward(w, b, s, threads=threads, native=True))
+    fwd = oracle_forward(cfg, oracle_weights(cfg), threads)
     # size one step so the whole run stays within a couple of minutes
     probe_n = 4 * threads
-    b, s = gz.synth_positions(game, probe_n, seed=1)
+    b, s = oracle_inputs(cfg, probe_n, 1)
     t0 = time.perf_counter()
     fwd(b, s)
     rate = probe_n / (time.perf_counter() - t0)
     per_step = int(max(threads, min(cfg["batch"], rate * min(2.0, 100.0 / max(1, args.steps + args.warmup)))))
-    boards, side = gz.synth_positions(game, per_step * (args.steps + args.warmup),
-                                      seed=gzd.shard_seed(cfg["index"], 0))
+    boards, side = oracle_inputs(cfg, per_step * (args.steps + args.warmup), shard_seed(cfg["index"], 0))
     for k in range(args.warmup):
         sl = slice(k * per_step, (k + 1) * per_step)
         fwd(boards[sl], side[sl])
@@ -210,15 +291,15 @@ def reference_arm(args, cfg: dict) -> None:
         fwd(boards[sl], side[sl])
     el = time.perf_counter() - t0
     value = per_step * args.steps / el
+    sample = (f"{per_step} positions per step of the same workload (inputs and weights from the oracle's "
+              f"generator); the reference's own network code does not build, so its CPU restatement "
+              f"(oracle/oracle.cpp) runs")
     line = {
-        "impl": "reference", "metric": metric_name(cfg), "value": value, "unit": "leaf evals/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+        "impl": "reference", "metric": metric_name(cfg), "value": value, "unit": "leaf evals/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": cfg["workload"], "batch_per_gpu": cfg["batch"],
-                   "sample_per_step": per_step},
-        "cpu_baseline": {"value": value, "unit": "leaf evals/s", "cores": threads, "kind": "port",
-                         "sample": f"{per_step} positions per step of the same workload; the reference's own "
-                                   f"network code does not build, so its CPU restatement (oracle/oracle.cpp) runs"},
+        "config": config_block(cfg, args.gpus),
+        "cpu_baseline": {"value": value, "unit": "leaf evals/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "leaf evals/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -282,9 +363,100 @@ def mcts_bench(net, device, game: int, trees: int, sims: int, leaves: int, moves
     return out
 
 
+def _import_product():
+    """The product package and its multi-GPU helpers (loads libgraphzero_b200.so)."""
+    global gz, gzd
+    import graphzero_b200 as gz
+    from graphzero_b200 import dist as gzd
+
+
+def device_timed(cfg: dict, net, dev: int, rank: int, steps: int, warmup: int, stream) -> dict:
+    """Device-timed forward passes over a pool of distinct batches (more
+    board bytes than L2) resident in HBM: total time and the mean per-launch
+    time from CUDA events on the launching stream, both max over ranks, and
+    the SM clocks sampled during the timed region."""
+    import torch
+
+    game, B = cfg["game"], cfg["batch"]
+    s = gz.game_shape(game)
+    seed = shard_seed(cfg["index"], rank)
+    base_n = 16384 if game == CHESS else 65536  # chess playouts are slow to generate
+    base_b, base_s = gz.synth_positions(game, base_n, seed=seed)
+    n_batches = pool_batches(cfg)
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    idx = torch.randint(0, base_n, (n_batches * B,), generator=g).to(f"cuda:{dev}")
+    pool_b = torch.from_numpy(base_b).to(f"cuda:{dev}")[idx].contiguous()
+    pool_s = torch.from_numpy(base_s).to(f"cuda:{dev}")[idx].contiguous()
+    pi = torch.empty((B, s.actions), device=f"cuda:{dev}")
+    v = torch.empty(B, device=f"cuda:{dev}")
+
+    def step(k):
+        j = k % n_batches
+        net.predict_batch(pool_b[j * B].data_ptr(), pool_s[j * B].data_ptr(), B, pi, v, stream)
+
+    for k in range(warmup):
+        step(k)
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    t_begin, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gzd.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev) as clocks:
+        t_begin.record(stream)
+        for k in range(steps):
+            starts[k].record(stream)
+            step(warmup + k)
+            ends[k].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    gzd.barrier()
+    net.check()
+    elapsed = t_begin.elapsed_time(t_end) / 1e3
+    kernel_s = statistics.mean(a.elapsed_time(b) for a, b in zip(starts, ends)) / 1e3
+    del pool_b, pool_s
+    return {"elapsed": gzd.max_over_ranks(elapsed, device=f"cuda:{dev}"),
+            "kernel_s": gzd.max_over_ranks(kernel_s, device=f"cuda:{dev}"),
+            "base": (base_b, base_s), "clocks": clocks.summary()}
+
+
+def roofline(cfg: dict, kernel_name: str, kernel_s: float) -> dict:
+    """Achieved GEMM FLOP/s of one launch against the measured bf16 tensor
+    peak (the fp16 rate is the same), or the nominal fp32 CUDA-core peak for
+    the fp32 SIMT kernel."""
+    B = cfg["batch"]
+    flops = flops_per_position(cfg) * B
+    achieved = flops / kernel_s / 1e12
+    if kernel_name.endswith("fp32"):
+        peak, src, bound = FP32_PEAK_TFLOPS, "nominal fp32 CUDA-core peak (148 SMs x 128 lanes x 2 x 1.965 GHz)", "fp32"
+    else:
+        (peak, src), bound = measured_peak(), "tensor"
+    return {"bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": ncu_traffic(kernel_name, f"batch{B}"), "kernel": kernel_name, "kernel_ms": kernel_s * 1e3,
+            "flops_per_launch": flops, "peak_source": src}
+
+
+def other_config(name: str, dev: int, stream, with_cpu: bool) -> dict:
+    """One more leaf-evaluation workload on this GPU (one rank): value,
+    roofline and a bounded CPU baseline sample."""
+    cfg = CONFIGS[name]
+    net = gz.Net(cfg["game"], cfg["kind"], device=dev, precision=cfg["precision"], max_batch=cfg["batch"])
+    net.load_weights(gz.synth_weights(cfg["game"], cfg["kind"], seed=shard_seed(cfg["index"], 0)))
+    r = device_timed(cfg, net, dev, 0, cfg["steps"], 5, stream)
+    out = {"metric": metric_name(cfg), "value": cfg["batch"] * cfg["steps"] / r["elapsed"], "unit": "leaf evals/s",
+           "steps": cfg["steps"], "warmup": 5, "ms_per_step": r["elapsed"] / cfg["steps"] * 1e3,
+           "config": config_block(cfg, 1), "roofline": roofline(cfg, net.kernel_name, r["kernel_s"]),
+           "clocks": r["clocks"], "gpu_launches": cfg["steps"]}
+    net.close()
+    if with_cpu:
+        out["cpu_baseline"] = cpu_baseline(cfg, seconds=8.0)
+    return out
+
+
 def ours(args, cfg: dict) -> None:
     import torch
 
+    _import_product()
     info = gzd.rank_info()
     dev = info.local_rank
     torch.cuda.set_device(dev)
@@ -295,7 +467,7 @@ def ours(args, cfg: dict) -> None:
 
     # ---- network, weights from rank 0 over NCCL ----
     net = gz.Net(game, cfg["kind"], device=dev, precision=cfg["precision"], max_batch=B)
-    w = gz.synth_weights(game, cfg["kind"], seed=gzd.shard_seed(cfg["index"], 0))
+    w = gz.synth_weights(game, cfg["kind"], seed=shard_seed(cfg["index"], 0))
     comm = None
     assert net.weight_count() == w.size
     if multi:
@@ -309,45 +481,11 @@ def ours(args, cfg: dict) -> None:
     else:
         net.load_weights(w)
 
-    # ---- inputs: a pool of distinct batches larger than L2, resident in HBM ----
-    seed = gzd.shard_seed(cfg["index"], info.rank)
-    base_n = 16384 if game == gz.CHESS else 65536  # chess playouts are slow to generate
-    base_b, base_s = gz.synth_positions(game, base_n, seed=seed)
-    n_batches = max(8, math.ceil(1.05 * L2_BYTES / (B * s.board_bytes)))
-    g = torch.Generator(device="cpu").manual_seed(seed)
-    idx = torch.randint(0, base_n, (n_batches * B,), generator=g).to(f"cuda:{dev}")
-    pool_b = torch.from_numpy(base_b).to(f"cuda:{dev}")[idx].contiguous()
-    pool_s = torch.from_numpy(base_s).to(f"cuda:{dev}")[idx].contiguous()
-    pi = torch.empty((B, s.actions), device=f"cuda:{dev}")
-    v = torch.empty(B, device=f"cuda:{dev}")
-
-    def step(k):
-        j = k % n_batches
-        net.predict_batch(pool_b[j * B].data_ptr(), pool_s[j * B].data_ptr(), B, pi, v, stream)
-
-    for k in range(args.warmup):
-        step(k)
-    torch.cuda.synchronize()
-
     # ---- timed region (device time, max over ranks) ----
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    t_begin, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    gzd.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(dev) as clocks:
-        t_begin.record(stream)
-        for k in range(args.steps):
-            starts[k].record(stream)
-            step(args.warmup + k)
-            ends[k].record(stream)
-        t_end.record(stream)
-        torch.cuda.synchronize()
-    gzd.barrier()
-    elapsed = t_begin.elapsed_time(t_end) / 1e3
-    kernel_s = statistics.mean(a.elapsed_time(b) for a, b in zip(starts, ends)) / 1e3
-    elapsed = gzd.max_over_ranks(elapsed, device=f"cuda:{dev}")
-    kernel_s = gzd.max_over_ranks(kernel_s, device=f"cuda:{dev}")
+    r = device_timed(cfg, net, dev, info.rank, args.steps, args.warmup, stream)
+    elapsed, kernel_s = r["elapsed"], r["kernel_s"]
+    base_b, base_s = r["base"]
+    base_n = base_s.shape[0]
     value = B * args.steps * info.world / elapsed
 
     # ---- end to end through the host-buffer call ----
@@ -376,45 +514,36 @@ def ours(args, cfg: dict) -> None:
 
     # ---- batched search throughput (secondary metric) ----
     mcts = None
-    if game == gz.CONNECT4 and cfg["kind"] == gz.GAT and args.mcts_moves > 0:
+    if game == CONNECT4 and cfg["kind"] == GAT and args.mcts_moves > 0:
         mcts = mcts_bench(net, dev, game, trees=1024, sims=800, leaves=4, moves=args.mcts_moves,
-                          seed=seed)
+                          seed=shard_seed(cfg["index"], info.rank))
 
     if comm is not None:
         gz.nccl_comm_destroy(comm)
+    kernel_name = net.kernel_name
+    net.close()
     if info.rank == 0:
-        flops = (gat_gemm_flops(game) if cfg["kind"] == gz.GAT else resnet_gemm_flops()) * B
-        peak, peak_src = measured_peak()
-        achieved = flops / kernel_s / 1e12
-        kernel_name = net.kernel_name
-        traffic = ncu_traffic(kernel_name, f"batch{B}")
         line = {
             "metric": metric_name(cfg),
             "value": value, "unit": "leaf evals/s", "n_gpus": info.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": kernel_name.rsplit("_", 1)[-1].replace("fp", "f"),
             "data": "synthetic",
-            "config": {"workload": cfg["workload"], "batch_per_gpu": B, "global_batch": B * info.world,
-                       "positions": "uniform random legal playouts (seeded per rank)",
-                       "weights": "Glorot-uniform from seed, bf16-representable",
-                       "l2": f"inputs larger than L2: {n_batches} distinct batches "
-                             f"({n_batches * B * s.board_bytes / 2**20:.0f} MiB of boards) cycled",
-                       "parallelism": f"dp{info.world} (independent shards, one NCCL weight broadcast)"},
+            "config": config_block(cfg, info.world),
             "e2e": e2e,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "kernel": kernel_name, "kernel_ms": kernel_s * 1e3,
-                         "flops_per_launch": flops, "peak_source": peak_src},
-            "clocks": clocks.summary(),
+            "roofline": roofline(cfg, kernel_name, kernel_s),
+            "clocks": r["clocks"],
             "gpu_launches": args.steps,
         }
         if mcts:
             line["mcts"] = mcts
         if info.world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(cfg, w)
+            line["cpu_baseline"] = cpu_baseline(cfg)
+        if info.world == 1 and args.config == "c1" and not args.no_other_configs:
+            line["configs"] = {name: other_config(name, dev, stream, not args.no_cpu_baseline)
+                               for name in ("c0", "c2", "c3")}
         print(json.dumps(line), flush=True)
     gzd.barrier()
-    net.close()
     if multi:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -429,6 +558,7 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
     ap.add_argument("--mcts-moves", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.config]

@@ -74,10 +74,22 @@ def build_library(force: bool = False) -> Path:
     return LIB
 
 
+def reference_dir() -> Path | None:
+    """The reference checkout whose rule functions oracle/_ref is compiled
+    from: $GZ_REFERENCE_DIR, else a `reference` directory beside this
+    repository; None when neither exists."""
+    cand = os.environ.get("GZ_REFERENCE_DIR") or str(ROOT.parent / "reference")
+    return Path(cand) if (Path(cand) / "games" / "connect4" / "connect4.cu").exists() else None
+
+
 def build_oracle() -> None:
     """Build the CPU oracle (test infrastructure) and, where the reference tree
     is present, its rule functions under oracle/_ref."""
-    r = subprocess.run(["make", "-s", "-C", str(ROOT / "oracle")], capture_output=True, text=True)
+    cmd = ["make", "-s", "-C", str(ROOT / "oracle")]
+    ref = reference_dir()
+    if ref is not None:
+        cmd.append(f"REF={ref}")
+    r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"oracle build failed:\n{r.stdout}\n{r.stderr}")
 

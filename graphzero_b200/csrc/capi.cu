@@ -44,6 +44,13 @@ gz_status gz::set_last_error(gz_status s, const char* fmt, ...) {
   return s;
 }
 
+gz_status gz::forward_error_status(int err, const char* who) {
+  if (!err) return GZ_OK;
+  if (err == 2) return set_last_error(GZ_ERR_CUDA, "%s: dynamic shared memory base not 1024-byte aligned", who);
+  return set_last_error(GZ_ERR_TIMEOUT, "%s: a bounded wait inside the kernel gave up (outputs of that launch are invalid)",
+                        who);
+}
+
 namespace {
 
 #define GZ_CUDA(call)                                                                                  \
@@ -139,11 +146,17 @@ struct gz_selfplay {
 
 namespace {
 
+// GZ_PREC_AUTO resolved at creation: the fp32 SIMT kernel where no
+// tensor-core kernel exists (TicTacToe), else the tensor-core kernel with
+// fp16 operands (kAutoFp16).
+int resolve_precision(int game, int kind, int precision) {
+  if (precision != GZ_PREC_AUTO) return precision;
+  if (kind == GZ_NET_GAT && (game == kTicTacToe || gat_tc_packed_bytes(game) == 0)) return GZ_PREC_FP32;
+  return kAutoFp16 ? GZ_PREC_FP16 : GZ_PREC_BF16;
+}
+
 bool use_tensor_cores(const gz_net* n) {
-  if (n->kind != GZ_NET_GAT) return false;
-  if (n->precision == GZ_PREC_FP32) return false;
-  if (n->precision == GZ_PREC_BF16 || n->precision == GZ_PREC_FP16) return true;
-  return n->game != kTicTacToe && gat_tc_packed_bytes(n->game) > 0;  // AUTO
+  return n->kind == GZ_NET_GAT && (n->precision == GZ_PREC_BF16 || n->precision == GZ_PREC_FP16);
 }
 
 gz_status prepare_weights(gz_net* n, cudaStream_t s) {
@@ -327,7 +340,7 @@ gz_status gz_net_create(const gz_net_config* cfg, int device, gz_net** out) {
   gz_net* n = new gz_net();
   n->game = cfg->game;
   n->kind = cfg->kind;
-  n->precision = cfg->precision;
+  n->precision = resolve_precision(cfg->game, cfg->kind, cfg->precision);
   n->device = device;
   n->max_batch = cfg->max_batch > 0 ? cfg->max_batch : 1;
   n->weight_count = gz_weight_count(cfg->game, cfg->kind);
@@ -505,8 +518,7 @@ gz_status gz_net_predict_batch(gz_net* n, const int8_t* boards, const int8_t* si
 static gz_status forward_error(gz_net* n, int err) {
   if (!err) return GZ_OK;
   GZ_CUDA(cudaMemset(n->d_err, 0, sizeof(int)));
-  if (err == 2) return fail(GZ_ERR_CUDA, "forward kernel: dynamic shared memory base not 1024-byte aligned");
-  return fail(GZ_ERR_TIMEOUT, "a bounded wait inside the forward kernel gave up (outputs of that launch are invalid)");
+  return gz::forward_error_status(err, "forward kernel");
 }
 
 gz_status gz_net_check(gz_net* n) {

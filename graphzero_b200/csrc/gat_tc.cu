@@ -23,10 +23,11 @@
 //               operand in shared memory; the result overwrites the head's
 //               accumulator columns
 //   3. out / z + bias, ELU, stored as the next layer's X tile (128-byte
-//      swizzled, K-major) -- or, after the last layer, stored as fp16 in the
-//      same layout and read once: mean-pooled into the value head (256->64
-//      ReLU, 64->1 tanh) and column-pooled into the policy head (256->1 per
-//      column, softmax over 7), sums in fp32.
+//      swizzled, K-major; fp16 rounded to nearest, or bf16 stochastically
+//      rounded) -- or, after the last layer, summed in fp32 per (position,
+//      board column) straight from the registers: the column sums feed the
+//      policy head (256->1 per column, softmax over 7), their totals the
+//      value head (256->64 ReLU, 64->1 tanh).
 // The next layer's projection does not wait for the head loop: heads c and
 // c + 4 write K chunk c of the next X tile, and each chunk's MMAs are issued
 // as soon as it exists, into a third accumulator block (tensor memory holds
@@ -114,7 +115,13 @@ constexpr int kSmBar = kSmVec + 2 * kVecFloats * 4;
 // full, empty, sc_full, acc_a, acc_b, x_ready[4], req[2][2], done2[2][2], drain[3]
 constexpr int kNumBars = 2 * kWSlots + 3 + 4 + 4 + 4 + 3;
 constexpr int kSmMisc = kSmBar + kNumBars * 8;
-constexpr int kSmemBytes = kSmMisc + 16;
+// Last layer: each head's per (position, board column) sums of the
+// activations, fp32, as two shares [2][3 positions x 7 columns][32 features]
+// (column_partials).  Heads 0, 4, 1, 5 (t = 0, 1) keep them here, heads 2, 6,
+// 3, 7 in X chunks 2-3 (read by the projection until its second half is done).
+constexpr int kShareBytes = 2 * kGPT * 7 * 32 * 4;  // one head
+constexpr int kSmCol = (kSmMisc + 16 + 15) & ~15;
+constexpr int kSmemBytes = kSmCol + 4 * kShareBytes;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 static_assert(kSmW % 1024 == 0 && kWChunk % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 // Last-layer head scratch: node means and policy partial sums in the t-score
@@ -125,6 +132,12 @@ constexpr int kSmLgW = kSmMean + kGPT * 256 * 4;         // [8 warps][3 x 7] flo
 static_assert(kSmLgW + kEpiWarps * kGPT * 7 * 4 <= kSmVec, "head sums fit in the t-score region");
 constexpr int kXZPart = 3 * 16384;                       // X tile offset of [8 warps][3][64] floats
 static_assert(kXZPart + kEpiWarps * kGPT * 64 * 4 <= 4 * 16384, "value partials fit in the X tile");
+// Last layer: each epilogue warp transposes a head's 32 x 32 activations
+// through 4 KB of the X tile (K chunks 0-1, no longer read once the layer's
+// first-half projection is complete).
+constexpr int kXScratch = 4096;
+static_assert(kEpiWarps * kXScratch <= 2 * 16384, "transpose scratch fits in X chunks 0-1");
+static_assert(2 * 16384 + 4 * kShareBytes <= 4 * 16384, "column-sum shares of heads t = 2, 3 fit in X chunks 2-3");
 
 // Offsets (floats) into the fp32 weight blob for Connect4 (gat_layout order).
 struct C4Off {
@@ -218,6 +231,42 @@ __device__ __forceinline__ float2 elu2_log2e(float2 u) {
   const float2 em = make_float2(ex2_approx(-fabsf(u.x)), ex2_approx(-fabsf(u.y)));
   const float2 m = __ffma2_rn(em, make_float2(kLog2e, kLog2e), make_float2(-kLog2e, -kLog2e));
   return make_float2(fmaxf(m.x, u.x), fmaxf(m.y, u.y));
+}
+
+// Last layer, per head: lane d of the epilogue warp with lane quarter QD
+// reads feature d of the warp's 32 node rows from the warp's transpose
+// scratch (row n: 32 floats, 16-byte units XOR-swizzled by n % 8, so that the
+// row writes and the column reads are free of bank conflicts) and sums them
+// per (position, board column) in row order.  Every column of position p has
+// rows in exactly two warps, lane quarters p and p + 1; the sums go to
+// part[share][p * 7 + c][d] with share 0 the lower warp's (QD = p) and share 1
+// the upper warp's (QD = p + 1).
+// Column-sum shares of head 4g + t (bytes from the shared-memory base).
+__host__ __device__ constexpr int share_offset(int g, int t) {
+  return (t < 2 ? kSmCol + t * 2 * kShareBytes : kSmX + 2 * 16384 + (t - 2) * 2 * kShareBytes) + g * kShareBytes;
+}
+
+template <int QD>
+__device__ __forceinline__ void column_partials(const uint8_t* scr, int d, float* part) {
+  float v[32];
+#pragma unroll
+  for (int n = 0; n < 32; ++n) v[n] = *(const float*)(scr + n * 128 + (((d >> 2) ^ (n & 7)) << 4) + (d & 3) * 4);
+#pragma unroll
+  for (int pc = 0; pc < kGPT * 7; ++pc) {
+    const int pos = pc / 7;
+    if (pos != QD && pos != QD - 1) continue;
+    float sum = 0.f;
+    bool any = false;
+#pragma unroll
+    for (int n = 0; n < 32; ++n) {
+      const int i = 32 * QD + n;
+      if (i < kGPT * kN && (i / kN) * 7 + (i % kN) % 7 == pc) {
+        sum = any ? sum + v[n] : v[n];
+        any = true;
+      }
+    }
+    part[((QD - pos) * kGPT * 7 + pc) * 32 + d] = sum;
+  }
 }
 
 // The e rows of a tile's position p live in tensor memory relative to the
@@ -594,17 +643,21 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
             y[2 * k + 1] = elu2_log2e(__ffma2_rn(make_float2(o[4 * k + 2], o[4 * k + 3]), iv, make_float2(bv.z, bv.w)));
           }
           if constexpr (!last) {
-            // the next layer's operand, stochastically rounded (see round_seed)
+            // the next layer's operand: fp16 rounded to nearest; bf16 (8
+            // significant bits) stochastically rounded (see round_seed)
             // K chunk t of the next X tile holds heads t (units 0-3) and
             // t + 4 (units 4-7)
-            const uint32_t seed = round_seed(li, l, h);
+            constexpr bool kSr = std::is_same<OpT, __nv_bfloat16>::value;
+            const uint32_t seed = kSr ? round_seed(li, l, h) : 0u;
             uint8_t* xrow = sX + t * 16384 + (i >> 3) * 1024 + (i & 7) * 128;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const int unit = (4 * g + u) ^ (i & 7);
               uint32_t q[4];
 #pragma unroll
-              for (int m = 0; m < 4; ++m) q[m] = OpType<OpT>::pack_sr(y[4 * u + m].x, y[4 * u + m].y, seed ^ pair_mix(4 * u + m));
+              for (int m = 0; m < 4; ++m)
+                q[m] = kSr ? OpType<OpT>::pack_sr(y[4 * u + m].x, y[4 * u + m].y, seed ^ pair_mix(4 * u + m))
+                           : OpType<OpT>::pack(y[4 * u + m].x, y[4 * u + m].y);
               *(uint4*)(xrow + unit * 16) = make_uint4(q[0], q[1], q[2], q[3]);
             }
             fence_proxy_async_smem();  // X writes -> the next projection's async proxy
@@ -612,17 +665,25 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&x_ready[t]);
           } else {
-            // last layer: the activations as fp16 (rounded to nearest) in the
-            // X tile's layout; the pooling reads them once all heads are done
-            uint8_t* xrow = sX + t * 16384 + (i >> 3) * 1024 + (i & 7) * 128;
+            // last layer: the fp32 activations are summed per (position,
+            // board column) in fp32: transposed through the warp's scratch
+            // into this warp's share of the head's column sums
+            // (column_partials); the pooling adds the two shares of every
+            // sum in a fixed order, so the result is deterministic
+            uint8_t* scr = sX + warp * kXScratch;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int unit = (4 * g + u) ^ (i & 7);
-              uint32_t q[4];
-#pragma unroll
-              for (int m = 0; m < 4; ++m) q[m] = OpType<__half>::pack(y[4 * u + m].x, y[4 * u + m].y);
-              *(uint4*)(xrow + unit * 16) = make_uint4(q[0], q[1], q[2], q[3]);
+            for (int j = 0; j < 8; ++j)
+              *(float4*)(scr + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                  make_float4(y[2 * j].x, y[2 * j].y, y[2 * j + 1].x, y[2 * j + 1].y);
+            __syncwarp();
+            float* part = (float*)(smem + share_offset(g, t));  // [2][21][32] floats
+            switch (qd) {
+              case 0: column_partials<0>(scr, lane, part); break;
+              case 1: column_partials<1>(scr, lane, part); break;
+              case 2: column_partials<2>(scr, lane, part); break;
+              default: column_partials<3>(scr, lane, part); break;
             }
+            __syncwarp();       // the scratch is rewritten by the next head
             tc_fence_before();  // this head's tensor-memory reads precede the next tile's projection
           }
         };
@@ -722,13 +783,12 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
             hb[5] = __ldg(p.w + C4Off::b_v2);
           }
           fetch_cell(tile + gridDim.x);  // the next tile's encode input
-          named_bar_sync(1, kEpiWarps * 32);  // every head's activations written
+          named_bar_sync(1, kEpiWarps * 32);  // every head's column sums complete
           float* mean = (float*)(smem + kSmMean);  // [3][256] node means
           float* lgw = (float*)(smem + kSmLgW);    // [warp][3 x 7] policy partial sums
           {
             const int f = threadIdx.x, hf = f >> 5;
-            const uint8_t* col = sX + (hf & 3) * 16384 + (f & 7) * 2;
-            const int unit0 = 4 * (hf >> 2) + ((f & 31) >> 3);
+            const float* cs = (const float*)(smem + share_offset(hf >> 2, hf & 3)) + (f & 31);
             float lp[kGPT * 7];
             const float wpf = __ldg(p.w + C4Off::w_pi + f) * (kLn2 / 6.0f);
 #pragma unroll
@@ -736,15 +796,9 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
               float tot = 0.f;
 #pragma unroll
               for (int c = 0; c < 7; ++c) {
-                float cs = 0.f;
-#pragma unroll
-                for (int r = 0; r < 6; ++r) {
-                  const int row = pg * kN + r * 7 + c;
-                  const __half x = *(const __half*)(col + (row >> 3) * 1024 + (row & 7) * 128 + ((unit0 ^ (row & 7)) << 4));
-                  cs += __half2float(x);
-                }
-                tot += cs;
-                lp[pg * 7 + c] = cs * wpf;
+                const float x = cs[(pg * 7 + c) * 32] + cs[(kGPT * 7 + pg * 7 + c) * 32];
+                tot += x;
+                lp[pg * 7 + c] = x * wpf;
               }
               mean[pg * 256 + f] = tot * (kLn2 / kN);
             }

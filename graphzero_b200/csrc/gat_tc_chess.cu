@@ -490,9 +490,11 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
             y[2 * k] = elu2_log2e(__ffma2_rn(make_float2(o[4 * k], o[4 * k + 1]), iv, make_float2(bv.x, bv.y)));
             y[2 * k + 1] = elu2_log2e(__ffma2_rn(make_float2(o[4 * k + 2], o[4 * k + 3]), iv, make_float2(bv.z, bv.w)));
           }
-          // next layer's operand (the last layer's feeds the policy MMA)
+          // next layer's operand (the last layer's feeds the policy MMA):
+          // fp16 rounded to nearest, bf16 stochastically rounded (round_seed)
           {
-            const uint32_t seed = round_seed(sq, l, h);
+            constexpr bool kSr = std::is_same<OpT, __nv_bfloat16>::value;
+            const uint32_t seed = kSr ? round_seed(sq, l, h) : 0u;
             uint8_t* xrow = sX + (h >> 1) * 16384 + (i >> 3) * 1024 + (i & 7) * 128;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
@@ -500,7 +502,8 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
               uint32_t qv[4];
 #pragma unroll
               for (int m = 0; m < 4; ++m)
-                qv[m] = OpType<OpT>::pack_sr(y[4 * u + m].x, y[4 * u + m].y, seed ^ pair_mix(4 * u + m));
+                qv[m] = kSr ? OpType<OpT>::pack_sr(y[4 * u + m].x, y[4 * u + m].y, seed ^ pair_mix(4 * u + m))
+                            : OpType<OpT>::pack(y[4 * u + m].x, y[4 * u + m].y);
               *(uint4*)(xrow + unit * 16) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
             }
           }

@@ -13,6 +13,17 @@ namespace gz {
 // and returns `s`.
 gz_status set_last_error(gz_status s, const char* fmt, ...);
 
+// The operand format GZ_PREC_AUTO picks for the tensor-core kernels: fp16
+// (11 significant bits, the same tensor-core rate as bf16).  Its rounding
+// error is 6-8x smaller than bf16's on these networks; activations must stay
+// below 65504 in magnitude (GZ_PREC_BF16 has the fp32 range).
+constexpr bool kAutoFp16 = true;
+
+// Status of a forward kernel's error word: 0 ok, 2 the dynamic shared
+// memory base was not 1024-byte aligned (GZ_ERR_CUDA), anything else a
+// bounded wait that gave up (GZ_ERR_TIMEOUT).  `who` prefixes the message.
+gz_status forward_error_status(int err, const char* who);
+
 // fp32 SIMT fused GAT forward (all layers + heads, one launch).
 //   boards [n][BOARD] int8, side [n] int8 (+1 / -1),
 //   weights: fp32 blob in gat_layout() order,
@@ -21,7 +32,7 @@ gz_status set_last_error(gz_status s, const char* fmt, ...);
 cudaError_t launch_gat_simt(int game, const float* d_weights, const int* d_csr, const int8_t* d_boards,
                             const int8_t* d_side, int n, float* d_pi, float* d_v, cudaStream_t stream);
 
-// bf16 tensor-core (tcgen05) GAT forward for Connect4 and chess.
+// Tensor-core (tcgen05) GAT forward for Connect4 and chess, bf16 or fp16 operands.
 // gat_tc_packed_bytes(game) is 0 when the game has no tensor-core kernel.
 size_t gat_tc_packed_bytes(int game);
 // Converts the fp32 blob into the kernel's operand layout (bf16 or fp16
@@ -38,7 +49,7 @@ cudaError_t launch_chess_tc_pack(int fp16, const float* d_weights, void* d_packe
 cudaError_t launch_chess_tc(int fp16, const void* d_packed, const float* d_weights, const int8_t* d_boards,
                             const int8_t* d_side, int n, float* d_pi, float* d_v, int* d_err, cudaStream_t stream);
 
-// bf16 tensor-core Connect4 ResNet forward (implicit-GEMM 3x3 convolutions).
+// Tensor-core Connect4 ResNet forward (implicit-GEMM 3x3 convolutions), bf16 or fp16 operands.
 size_t resnet_tc_packed_bytes();
 cudaError_t launch_resnet_tc_pack(int fp16, const float* d_weights, void* d_packed, cudaStream_t stream);
 cudaError_t launch_resnet_tc(int fp16, const void* d_packed, const float* d_weights, const int8_t* d_boards,

@@ -8,7 +8,7 @@
 // allocates); it passes host weights, positions and output buffers, and this
 // entry point stages everything through one file-scope device array:
 //
-//   fp32 weight blob | packed bf16 weight tiles | boards | side | pi | v | error word
+//   fp32 weight blob | packed weight tiles | boards | side | pi | v | error word
 //
 // All of it is device memory reserved when the library is loaded, on every
 // GPU the process uses, until the process exits.  Positions per call are
@@ -18,6 +18,19 @@
 // overlap in time (two host threads, or two devices sharing nothing but this
 // entry point) on the same device race on the array and must be serialised
 // by the caller.
+//
+// Each call uploads the whole 1.4 MB fp32 weight blob and repacks it (one
+// small kernel) before the forward pass, and runs on the device's legacy
+// default stream, which also waits for the work of every blocking stream of
+// the process on that device.  The kernel and operand format are those of a
+// gz_net created with GZ_PREC_AUTO, so both give identical outputs.
+//
+// The array's device address is looked up on the first call on a device
+// (cudaGetSymbolAddress with that device current) and kept per device
+// together with the identity of the CUDA context it belongs to; after a
+// cudaDeviceReset the next call finds a new context and looks the address up
+// again.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
@@ -51,9 +64,38 @@ constexpr size_t kScratchBytes = align256(kOffErr + sizeof(int));
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kScratchBytes];
 
 // Device address of g_noalloc_scratch per device, looked up on the first call
-// on that device (with that device current).
+// on that device (with that device current), and the id of the context it
+// was looked up in.
 uint8_t* g_scratch_addr[64];
+unsigned long long g_scratch_ctx[64];
 std::mutex g_setup_mutex;
+
+// Id of the calling thread's current CUDA context (unique over the process's
+// lifetime), or 0 if the driver cannot tell; through the runtime's driver
+// entry points, so the library needs no link to libcuda.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = (GetCurrent)f;
+    f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = (GetId)f;
+    cudaGetLastError();
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 }  // namespace
 }  // namespace gz
@@ -84,12 +126,17 @@ gz_status gz_gat_c4_predict_noalloc(int device, const float* h_weights, size_t n
   uint8_t* base = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (!g_scratch_addr[device]) {
+    const unsigned long long ctx = current_context_id();
+    if (!g_scratch_addr[device] || ctx == 0 || ctx != g_scratch_ctx[device]) {
       void* ptr = nullptr;
       const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      g_scratch_addr[device] = nullptr;
       if (e != cudaSuccess || !ptr)
         st = set_last_error(GZ_ERR_CUDA, "cudaGetSymbolAddress of the scratch array: %s", cudaGetErrorString(e));
-      else g_scratch_addr[device] = (uint8_t*)ptr;
+      else {
+        g_scratch_addr[device] = (uint8_t*)ptr;
+        g_scratch_ctx[device] = ctx;
+      }
     }
     base = g_scratch_addr[device];
   }
@@ -106,15 +153,15 @@ gz_status gz_gat_c4_predict_noalloc(int device, const float* h_weights, size_t n
     if (e == cudaSuccess) e = cudaMemcpyAsync(d_boards, h_boards, (size_t)n * kC4Board, cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d_side, h_side, (size_t)n, cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(d_err, 0, sizeof(int), s);  // the error word starts at zero
-    if (e == cudaSuccess) e = launch_gat_tc_pack(kConnect4, /*fp16=*/0, d_w, d_packed, s);
-    if (e == cudaSuccess) e = launch_gat_tc(kConnect4, /*fp16=*/0, d_packed, d_w, d_boards, d_side, n, d_pi, d_v, d_err, s);
+    if (e == cudaSuccess) e = launch_gat_tc_pack(kConnect4, kAutoFp16, d_w, d_packed, s);
+    if (e == cudaSuccess) e = launch_gat_tc(kConnect4, kAutoFp16, d_packed, d_w, d_boards, d_side, n, d_pi, d_v, d_err, s);
     if (e == cudaSuccess) e = cudaMemcpyAsync(h_pi, d_pi, (size_t)n * kC4Actions * sizeof(float), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaMemcpyAsync(h_v, d_v, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost, s);
     int err = 0;
     if (e == cudaSuccess) e = cudaMemcpyAsync(&err, d_err, sizeof(int), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) st = set_last_error(GZ_ERR_CUDA, "gz_gat_c4_predict_noalloc: %s", cudaGetErrorString(e));
-    else if (err) st = set_last_error(GZ_ERR_TIMEOUT, "gz_gat_c4_predict_noalloc: a bounded wait in the kernel gave up");
+    else if (err) st = forward_error_status(err, "gz_gat_c4_predict_noalloc");
   }
   cudaSetDevice(prev);
   return st;

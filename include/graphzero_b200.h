@@ -45,10 +45,14 @@ typedef enum {
 typedef enum { GZ_GAME_TICTACTOE = 0, GZ_GAME_CONNECT4 = 1, GZ_GAME_CHESS = 2 } gz_game;
 typedef enum { GZ_NET_GAT = 0, GZ_NET_RESNET = 1 } gz_net_kind;
 
-/* Arithmetic of the forward pass.  AUTO: fp32 SIMT for TicTacToe, bf16
- * tensor-core operands with fp32 accumulation for Connect4 and chess.
- * FP16: fp16 tensor-core operands (same speed, 3 more mantissa bits; for
- * weights whose heads amplify activation rounding).  FP32: SIMT fp32. */
+/* Arithmetic of the forward pass.  AUTO: fp32 SIMT for TicTacToe, fp16
+ * tensor-core operands with fp32 accumulation for the Connect4 GAT, the
+ * chess GAT and the Connect4 ResNet.  FP16: fp16 tensor-core operands (11
+ * significant bits, activations rounded to nearest; activations must stay
+ * below 65504 in magnitude).  BF16: bf16 tensor-core operands (8 significant
+ * bits, fp32 range; activations stochastically rounded), the same speed.
+ * FP32: SIMT fp32 (GAT only).  gz_net_kernel_name() names the resolved
+ * kernel and format. */
 typedef enum { GZ_PREC_AUTO = 0, GZ_PREC_FP32 = 1, GZ_PREC_BF16 = 2, GZ_PREC_FP16 = 3 } gz_precision;
 
 typedef struct gz_net gz_net;
@@ -277,16 +281,20 @@ gz_status gz_train_examples_load(const char* path, gz_train_example* out, int64_
  * memory (a plugin inside a host application that fixes the device-memory
  * budget at start-up; a latency-critical loop that cannot pay for
  * cudaMalloc/cudaFree, which synchronise the device): Connect4 GAT leaf
- * evaluation (bf16 tensor-core kernel) from host weights (the Connect4 GAT
- * blob), host positions int8 [n][42] + side [n], into host pi [n][7], v [n].
+ * evaluation (the tensor-core kernel and operand format of a net created with
+ * GZ_PREC_AUTO) from host weights (the Connect4 GAT blob), host positions
+ * int8 [n][42] + side [n], into host pi [n][7], v [n].
  * It calls no cudaMalloc/cudaFree: all device staging lives in one static
  * device array of gz_gat_c4_noalloc_scratch_bytes() (about 2.3 MB), reserved
  * on every GPU that loads the library until the process exits.  n is limited
  * to gz_gat_c4_noalloc_max_batch() (4096); larger n returns
  * GZ_ERR_INVALID_ARG.  The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current, so make that first
- * call before any stream capture.  All calls share the array: calls that
- * overlap in time on one device race and must be serialised by the caller.
+ * call before any stream capture; after a cudaDeviceReset the next call looks
+ * it up again.  All calls share the array: calls that overlap in time on one
+ * device race and must be serialised by the caller.  Every call uploads the
+ * 1.4 MB weight blob and repacks it before the forward pass, on the device's
+ * legacy default stream (which waits for the process's blocking streams).
  * Synchronous (returns when the outputs are in host memory). */
 gz_status gz_gat_c4_predict_noalloc(int device, const float* h_weights, size_t n_weights, const int8_t* h_boards,
                                     const int8_t* h_side, int n, float* h_pi, float* h_v);

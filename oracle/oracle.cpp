@@ -463,9 +463,143 @@ int puct_pick(const OMcts& m, const OTree& t, int s) {
   return best;
 }
 
+// ------------------------------------------------------ synthetic inputs ----
+// Seeded Glorot weights, BN parameters and random legal positions: the same
+// splitmix64 streams as the product's generator (one stream per blob, one
+// per position index), so the same seed gives bit-identical data and the CPU
+// baseline can build its inputs without the product library.  The reference
+// seeds cuRAND with time(NULL) (networks/gat/gat.cu:769), so it has no
+// reproducible generator to follow.
+struct Mix {
+  uint64_t s;
+  explicit Mix(uint64_t seed) : s(seed) {}
+  uint64_t next() {  // splitmix64 (Steele, Lea, Flood 2014)
+    uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+  }
+  float uniform() { return (float)(next() >> 40) * (1.0f / 16777216.0f); }
+  uint32_t below(uint32_t n) { return (uint32_t)(((next() >> 32) * (uint64_t)n) >> 32); }
+  float normal() {  // Box-Muller on u1 in (0, 1], u2 in [0, 1)
+    double u1 = ((double)(next() >> 11) + 1.0) * (1.0 / 9007199254740992.0);
+    double u2 = (double)(next() >> 11) * (1.0 / 9007199254740992.0);
+    return (float)(std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2));
+  }
+};
+
+uint64_t stream_seed(uint64_t seed, uint64_t stream) { return Mix(seed ^ (stream * 0xD1B54A32D192ED03ull)).next(); }
+
+float bf16_nearest(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u) return x;
+  u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+  memcpy(&x, &u, 4);
+  return x;
+}
+
+struct Gen {
+  Mix r;
+  float bias_scale;
+  bool bf16;
+  float q(float v) const { return bf16 ? bf16_nearest(v) : v; }
+  void glorot(float* w, size_t n, int fan_in, int fan_out) {
+    float lim = std::sqrt(6.0f / (float)(fan_in + fan_out));
+    for (size_t i = 0; i < n; ++i) w[i] = q((2.0f * r.uniform() - 1.0f) * lim);
+  }
+  void bias(float* w, size_t n) {
+    for (size_t i = 0; i < n; ++i) w[i] = q(bias_scale == 0.0f ? 0.0f : (2.0f * r.uniform() - 1.0f) * bias_scale);
+  }
+  void bn(float* b, int C) {  // gamma ~ U(0.8, 1.2), beta, mean ~ N(0, 0.1), var ~ U(0.5, 1.5)
+    for (int c = 0; c < C; ++c) b[c] = 0.8f + 0.4f * r.uniform();
+    for (int c = 0; c < C; ++c) b[C + c] = 0.1f * r.normal();
+    for (int c = 0; c < C; ++c) b[2 * C + c] = 0.1f * r.normal();
+    for (int c = 0; c < C; ++c) b[3 * C + c] = 0.5f + r.uniform();
+    for (int i = 0; i < 4 * C; ++i) b[i] = q(b[i]);
+  }
+};
+
 }  // namespace
 
 extern "C" {
+
+// GAT weights (gat_off layout), Glorot-uniform, biases U(+-bias_scale).
+int orc_synth_gat_weights(int game, uint64_t seed, float bias_scale, int bf16_exact, float* out) {
+  if (game < 0 || game > 2 || !out) return -1;
+  Shape s = shape_of(game);
+  GatOff o = gat_off(game);
+  Gen g{Mix(stream_seed(seed, 0x6A7)), bias_scale, bf16_exact != 0};
+  for (int l = 0; l < s.L; ++l) {
+    int fin = l ? H : s.F;
+    g.glorot(out + o.W[l], (size_t)fin * H, fin, H);
+    g.bias(out + o.b[l], H);
+    g.glorot(out + o.a[l], NH * 2 * HD, 2 * HD, 1);
+  }
+  g.glorot(out + o.w_pi, (size_t)H * s.P, H, s.P);
+  g.bias(out + o.b_pi, s.P);
+  g.glorot(out + o.W_v1, (size_t)H * VH, H, VH);
+  g.bias(out + o.b_v1, VH);
+  g.glorot(out + o.w_v2, VH, VH, 1);
+  g.bias(out + o.b_v2, 1);
+  return 0;
+}
+
+// Connect4 ResNet weights (res_off layout).
+int orc_synth_res_weights(uint64_t seed, int bf16_exact, float* out) {
+  if (!out) return -1;
+  ResOff o = res_off();
+  const int C = 128;
+  Gen g{Mix(stream_seed(seed, 0x5E5)), 0.0f, bf16_exact != 0};
+  g.glorot(out + o.stem_w, (size_t)C * 9 * 3, 9 * 3, 9 * C);
+  g.bn(out + o.stem_bn, C);
+  for (int k = 0; k < 10; ++k) {
+    g.glorot(out + o.c1[k], (size_t)C * 9 * C, 9 * C, 9 * C);
+    g.bn(out + o.b1[k], C);
+    g.glorot(out + o.c2[k], (size_t)C * 9 * C, 9 * C, 9 * C);
+    g.bn(out + o.b2[k], C);
+  }
+  g.glorot(out + o.pol_w, 2 * C, C, 2);
+  g.bn(out + o.pol_bn, 2);
+  g.glorot(out + o.pol_fc, 84 * 7, 84, 7);
+  g.bias(out + o.pol_fc_b, 7);
+  g.glorot(out + o.val_w, C, C, 1);
+  g.bn(out + o.val_bn, 1);
+  g.glorot(out + o.val_fc1, 42 * 128, 42, 128);
+  g.bias(out + o.val_fc1_b, 128);
+  g.glorot(out + o.val_fc2, 128, 128, 1);
+  g.bias(out + o.val_fc2_b, 1);
+  return 0;
+}
+
+// Random legal TicTacToe / Connect4 positions first .. first + n - 1 of the
+// stream `seed`: k ~ U{0..N-1} uniformly random legal moves from the empty
+// board, stopping before a move that would end the game.
+int orc_synth_positions(int game, uint64_t seed, uint64_t first, int n, int8_t* boards, int8_t* side) {
+  if (game != 0 && game != 1) return -1;
+  Shape s = shape_of(game);
+  for (int i = 0; i < n; ++i) {
+    int8_t* b = boards + (size_t)i * s.board_bytes;
+    Mix r(stream_seed(seed, 0x9051 + first + (uint64_t)i));
+    memset(b, 0, (size_t)s.board_bytes);
+    int k = (int)r.below((uint32_t)(s.N - 1) + 1), sd = 1;
+    for (int ply = 0; ply < k; ++ply) {
+      int moves[9], m = 0;
+      for (int a = 0; a < s.A; ++a)
+        if (legal(game, b, a)) moves[m++] = a;
+      if (m == 0) break;
+      int a = moves[r.below((uint32_t)m)];
+      int8_t trial[64];
+      memcpy(trial, b, (size_t)s.N);
+      apply_move(game, trial, a, sd);
+      if (outcome(game, trial, sd) != 0) break;
+      memcpy(b, trial, (size_t)s.N);
+      sd = -sd;
+    }
+    side[i] = (int8_t)sd;
+  }
+  return 0;
+}
 
 int orc_shape(int game, int* out) {
   Shape s = shape_of(game);

@@ -46,6 +46,9 @@ def _load(path: Path):
         "orc_res_weight_count": (C.c_size_t, []),
         "orc_gat_forward": (C.c_int, [C.c_int, _f32p, _i8p, _i8p, C.c_int, _f32p, _f32p, C.c_int, C.c_int]),
         "orc_resnet_forward": (C.c_int, [_f32p, _i8p, _i8p, C.c_int, _f32p, _f32p, C.c_int, C.c_int]),
+        "orc_synth_gat_weights": (C.c_int, [C.c_int, C.c_uint64, C.c_float, C.c_int, _f32p]),
+        "orc_synth_res_weights": (C.c_int, [C.c_uint64, C.c_int, _f32p]),
+        "orc_synth_positions": (C.c_int, [C.c_int, C.c_uint64, C.c_uint64, C.c_int, _i8p, _i8p]),
         "orc_apply": (C.c_int, [C.c_int, _i8p, C.c_int, C.c_int]),
         "orc_legal": (C.c_int, [C.c_int, _i8p, C.c_int]),
         "orc_has_won": (C.c_int, [C.c_int, _i8p, C.c_int]),
@@ -144,6 +147,30 @@ def resnet_forward(w: np.ndarray, boards: np.ndarray, side: np.ndarray, threads:
                               _p(pi, C.c_float), _p(v, C.c_float), threads, int(f64))
     assert rc == 0
     return pi, v
+
+
+def synth_gat_weights(game: int, seed: int, bias_scale: float = 0.0, bf16_exact: bool = True) -> np.ndarray:
+    """Seeded GAT weight blob (the same streams as the product's generator)."""
+    w = np.zeros(lib().orc_gat_weight_count(game), np.float32)
+    assert lib().orc_synth_gat_weights(game, seed, bias_scale, int(bf16_exact), _p(w, C.c_float)) == 0
+    return w
+
+
+def synth_res_weights(seed: int, bf16_exact: bool = True) -> np.ndarray:
+    """Seeded Connect4 ResNet weight blob."""
+    w = np.zeros(lib().orc_res_weight_count(), np.float32)
+    assert lib().orc_synth_res_weights(seed, int(bf16_exact), _p(w, C.c_float)) == 0
+    return w
+
+
+def synth_positions(game: int, n: int, seed: int, first: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """Random legal TicTacToe / Connect4 positions (the product generator's
+    streams)."""
+    s = shape(game)
+    b = np.zeros((n, s["board_bytes"]), np.int8)
+    sd = np.zeros(n, np.int8)
+    assert lib().orc_synth_positions(game, seed, first, n, _p(b, C.c_int8), _p(sd, C.c_int8)) == 0
+    return b, sd
 
 
 def apply(game: int, board: np.ndarray, action: int, player: int) -> int:

@@ -12,13 +12,15 @@ from helpers import sharpen
 pytestmark = pytest.mark.gpu
 
 
-def make(game, trees, leaves, cap, seed):
+def make(game, trees, leaves, cap, seed, precision=gz.PREC_FP32, empty_roots=0):
     w = sharpen(game, gz.synth_weights(game, seed=seed, bias_scale=0.4))
-    net = gz.Net(game, precision=gz.PREC_FP32, max_batch=trees * leaves)
+    net = gz.Net(game, precision=precision, max_batch=trees * leaves)
     net.load_weights(w)
     m = gz.Mcts(game, trees, leaves, c_puct=1.5, virtual_loss=3, node_capacity=cap, dirichlet_eps=0.0)
     o = oracle.Mcts(game, trees, leaves, c_puct=1.5, virtual_loss=3, node_capacity=cap)
     boards, side = gz.synth_positions(game, trees, seed=seed + 1)
+    boards[:empty_roots] = 0  # games from the start, as in self-play
+    side[:empty_roots] = 1
     m.reset_roots(torch.from_numpy(boards).cuda(), torch.from_numpy(side).cuda())
     o.set_roots(boards, side)
     return net, m, o
@@ -61,6 +63,26 @@ def test_search_is_bit_exact(cuda, game, trees, leaves, waves):
     # every later selection passes through a root edge.
     visits, _ = m.root_stats()
     assert (visits.sum(1) == (waves - 1) * leaves).all()
+
+
+def test_search_at_selfplay_shape_is_bit_exact(cuda):
+    """The self-play search shape: 1024 trees, 4 leaves per tree (leaf batch
+    4096), one whole move of 800 simulations (200 waves), evaluations from
+    the tensor-core network (the default operand format), c_puct 1.5,
+    virtual loss 3, Dirichlet noise off; half of the games at the start
+    position.  The oracle, fed the same evaluations, selects the same leaves
+    every wave and ends with bit-identical visit counts and value sums."""
+    game, trees, leaves = gz.CONNECT4, 1024, 4
+    A = gz.game_shape(game).actions
+    net, m, o = make(game, trees, leaves, cap=(800 + 1) * 3, seed=51, precision=gz.PREC_AUTO, empty_roots=512)
+    assert net.kernel_name == "gat_tc_fp16"
+    for _ in range(800 // leaves):
+        wave(net, m, o, A)
+    compare(m, o)
+    visits, _ = m.root_stats()
+    assert (visits.sum(1) == 800 - leaves).all()
+    m.check()
+    net.check()
 
 
 def test_search_with_moves_is_bit_exact(cuda):
