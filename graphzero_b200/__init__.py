@@ -52,6 +52,17 @@ class MctsConfig(C.Structure):
                 ("dirichlet_eps", C.c_float), ("seed", C.c_uint64)]
 
 
+class TrainConfig(C.Structure):
+    """gz_train_config: Adam hyper-parameters, batch size, passes, order seed."""
+    _fields_ = [("learning_rate", C.c_float), ("weight_decay", C.c_float), ("beta1", C.c_float),
+                ("beta2", C.c_float), ("eps", C.c_float), ("batch_size", C.c_int), ("epochs", C.c_int),
+                ("seed", C.c_uint64)]
+
+
+class TrainStats(C.Structure):
+    _fields_ = [("policy_loss", C.c_float), ("value_loss", C.c_float), ("steps", C.c_int64)]
+
+
 # name -> (restype, argtypes)
 _SIGS = {
     "gz_status_string": (C.c_char_p, [C.c_int]),
@@ -112,6 +123,15 @@ _SIGS = {
     "gz_train_examples_load": (C.c_int, [C.c_char_p, _vp, C.c_int64, _i32p, C.c_int, C.POINTER(C.c_int),
                                          C.POINTER(C.c_int64)]),
     "gz_selftest_wait_timeout": (C.c_int, [C.c_int, C.c_int]),
+    "gz_train_config_default": (None, [C.POINTER(TrainConfig)]),
+    "gz_net_loss_grad": (C.c_int, [_vp, _vp, _vp, _vp, _vp, C.c_int, _vp, _f32p, _vp]),
+    "gz_net_train_step": (C.c_int, [_vp, _vp, _vp, _vp, _vp, C.c_int, C.POINTER(TrainConfig), _vp, C.c_int, _f32p,
+                                    _vp]),
+    "gz_net_train": (C.c_int, [_vp, _vp, C.c_int64, C.POINTER(TrainConfig), _vp, C.c_int, C.c_int,
+                               C.POINTER(TrainStats)]),
+    "gz_train_batch_indices": (C.c_int, [C.c_int64, C.POINTER(TrainConfig), C.c_int, C.c_int64, C.c_int, C.c_int,
+                                         C.POINTER(C.c_int64)]),
+    "gz_train_bucket_range": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     "gz_gat_c4_predict_noalloc": (C.c_int, [C.c_int, _f32p, C.c_size_t, _i8p, _i8p, C.c_int, _f32p, _f32p]),
     "gz_gat_c4_noalloc_scratch_bytes": (C.c_size_t, []),
     "gz_gat_c4_noalloc_max_batch": (C.c_int, []),
@@ -350,6 +370,60 @@ class Net:
 
     def broadcast(self, comm: int, root: int = 0, stream=None) -> None:
         _check(_lib.gz_net_broadcast(self._h, comm, root, _stream(stream)))
+
+    def loss_grad(self, d_boards, d_side, d_pi, d_v, n: int, d_grad=None, stream=None) -> tuple[float, float]:
+        """Loss terms (policy cross-entropy, value squared error; batch means)
+        of one batch of device buffers; the gradient (weight layout) into
+        d_grad when given.  No update."""
+        loss = np.zeros(2, np.float32)
+        _check(_lib.gz_net_loss_grad(self._h, _dev(d_boards), _dev(d_side), _dev(d_pi), _dev(d_v), n,
+                                     _dev(d_grad) if d_grad is not None else None, _ptr(loss, C.c_float),
+                                     _stream(stream)))
+        return float(loss[0]), float(loss[1])
+
+    def train_step(self, d_boards, d_side, d_pi, d_v, n: int, cfg: TrainConfig | None = None, comm: int | None = None,
+                   world: int = 1, stream=None) -> tuple[float, float]:
+        """One Adam step on one batch of device buffers (gradients averaged
+        over the ranks of `comm`); returns this batch's loss terms."""
+        cfg = cfg or train_config()
+        loss = np.zeros(2, np.float32)
+        _check(_lib.gz_net_train_step(self._h, _dev(d_boards), _dev(d_side), _dev(d_pi), _dev(d_v), n, C.byref(cfg),
+                                      comm, world, _ptr(loss, C.c_float), _stream(stream)))
+        return float(loss[0]), float(loss[1])
+
+    def train(self, examples: np.ndarray, cfg: TrainConfig | None = None, comm: int | None = None, rank: int = 0,
+              world: int = 1) -> TrainStats:
+        """INeuralNet::train over EXAMPLE_DTYPE records (canonical boards)."""
+        ex = np.ascontiguousarray(examples, dtype=EXAMPLE_DTYPE)
+        cfg = cfg or train_config()
+        st = TrainStats()
+        _check(_lib.gz_net_train(self._h, ex.ctypes.data if ex.size else None, ex.size, C.byref(cfg), comm, rank,
+                                 world, C.byref(st)))
+        return st
+
+
+def train_config(**kw) -> TrainConfig:
+    """The reference's training defaults (gz_train_config_default), with
+    fields overridden by keyword."""
+    c = TrainConfig()
+    _lib.gz_train_config_default(C.byref(c))
+    for k, val in kw.items():
+        setattr(c, k, val)
+    return c
+
+
+def train_batch_indices(n: int, cfg: TrainConfig, epoch: int, step: int, rank: int = 0, world: int = 1) -> np.ndarray:
+    """Example indices of one rank's batch (gz_net_train's order)."""
+    out = np.zeros(cfg.batch_size, np.int64)
+    _check(_lib.gz_train_batch_indices(n, C.byref(cfg), epoch, step, rank, world, _ptr(out, C.c_int64)))
+    return out
+
+
+def train_bucket_range(game: int, k: int) -> tuple[int, int]:
+    """(offset, length) in floats of gradient bucket k (layers, then the heads)."""
+    off, cnt = C.c_size_t(), C.c_size_t()
+    _check(_lib.gz_train_bucket_range(game, k, C.byref(off), C.byref(cnt)))
+    return off.value, cnt.value
 
 
 def create_neural_net(net_type: str, game: int | str, device: int = 0, **kw) -> Net:

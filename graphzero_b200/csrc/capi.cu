@@ -19,6 +19,7 @@
 #include "gz_sm100.h"
 #include "gz_synth.h"
 #include "gz_chess.h"
+#include "gz_train.h"
 
 using namespace gz;
 
@@ -86,6 +87,7 @@ struct Nccl {
   ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*errorString)(ncclResult_t) = nullptr;
 };
 
@@ -101,6 +103,7 @@ Nccl* nccl() {
     n.commInitRank = (decltype(n.commInitRank))dlsym(n.h, "ncclCommInitRank");
     n.commDestroy = (decltype(n.commDestroy))dlsym(n.h, "ncclCommDestroy");
     n.broadcast = (decltype(n.broadcast))dlsym(n.h, "ncclBroadcast");
+    n.allReduce = (decltype(n.allReduce))dlsym(n.h, "ncclAllReduce");
     n.errorString = (decltype(n.errorString))dlsym(n.h, "ncclGetErrorString");
   });
   if (!n.h || !n.getUniqueId || !n.commInitRank || !n.commDestroy || !n.broadcast) return nullptr;
@@ -125,6 +128,7 @@ struct gz_net {
   // the events "inputs copied", "forward done", "outputs copied"
   cudaStream_t copy_stream = nullptr;
   cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_fwd[2] = {nullptr, nullptr}, ev_out[2] = {nullptr, nullptr};
+  gz::train::State* tr = nullptr;  // training state, created by the first training call
 };
 
 struct gz_mcts {
@@ -397,6 +401,10 @@ gz_status gz_net_destroy(gz_net* n) {
   DeviceGuard g(n->device);
   if (n->stream) cudaStreamSynchronize(n->stream);
   if (n->copy_stream) cudaStreamSynchronize(n->copy_stream);
+  if (n->tr) {
+    gz::train::free_state(*n->tr);
+    delete n->tr;
+  }
   cudaFree(n->d_weights);
   cudaFree(n->d_csr);
   cudaFree(n->d_tc);
@@ -689,6 +697,238 @@ gz_status gz_net_broadcast(gz_net* n, void* comm, int root, void* stream) {
   ncclResult_t r = c->broadcast(n->d_weights, n->d_weights, n->weight_count, ncclFloat32, root, (ncclComm_t)comm, s);
   if (r != ncclSuccess) return fail(GZ_ERR_NCCL, "ncclBroadcast: %s", c->errorString ? c->errorString(r) : "?");
   return prepare_weights(n, s);
+}
+
+}  // extern "C"
+
+int gz::net_game(const gz_net* n) { return n ? n->game : -1; }
+
+gz_status gz::nccl_broadcast_floats(void* comm, float* d_buf, size_t count, int root, void* stream) {
+  Nccl* c = nccl();
+  if (!c) return fail(GZ_ERR_NCCL, "libnccl.so.2 not loadable");
+  if (!comm) return fail(GZ_ERR_INVALID_ARG, "null communicator");
+  const ncclResult_t r = c->broadcast(d_buf, d_buf, count, ncclFloat32, root, (ncclComm_t)comm, (cudaStream_t)stream);
+  if (r != ncclSuccess) return fail(GZ_ERR_NCCL, "ncclBroadcast: %s", c->errorString ? c->errorString(r) : "?");
+  return GZ_OK;
+}
+
+extern "C" {
+
+// ---------------------------------------------------------------- training --
+namespace {
+
+gz_status ensure_train(gz_net* n, int batch) {
+  if (n->kind != GZ_NET_GAT) return fail(GZ_ERR_UNSUPPORTED, "training is built for the GAT nets");
+  if (batch <= 0) return fail(GZ_ERR_INVALID_ARG, "batch of %d positions", batch);
+  if (!n->tr) n->tr = new gz::train::State();
+  const cudaError_t e = gz::train::ensure_state(*n->tr, n->game, batch);
+  if (e != cudaSuccess)
+    return fail(GZ_ERR_CUDA, "training buffers for %d positions: %s", batch, cudaGetErrorString(e));
+  return GZ_OK;
+}
+
+bool valid_train_config(const gz_train_config* c) {
+  return c && c->batch_size > 0 && c->epochs >= 0 && c->learning_rate >= 0.f && c->weight_decay >= 0.f &&
+         c->beta1 >= 0.f && c->beta1 < 1.f && c->beta2 >= 0.f && c->beta2 < 1.f && c->eps > 0.f;
+}
+
+// Forward + backward of one batch on `s`; with a communicator the gradient
+// buckets are summed over the ranks on the training state's side stream as
+// the backward pass completes them; with `update` an Adam step (gradients
+// averaged over the ranks) and a repack of the tensor-core weights follow.
+gz_status train_batch(gz_net* n, const int8_t* boards, const int8_t* side, const float* pi, const float* v, int cnt,
+                      const gz_train_config* cfg, void* comm, int world, bool update, float* h_loss,
+                      cudaStream_t s) {
+  gz::train::State& st = *n->tr;
+  Nccl* c = nullptr;
+  if (comm && world > 1) {
+    c = nccl();
+    if (!c || !c->allReduce) return fail(GZ_ERR_NCCL, "libnccl.so.2 not loadable");
+  }
+  ncclResult_t nr = ncclSuccess;
+  auto bucket_done = [&](int k) -> cudaError_t {
+    if (!c) return cudaSuccess;
+    cudaError_t e = cudaEventRecord(st.ev_bucket[k], s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st.comm_stream, st.ev_bucket[k], 0);
+    if (e != cudaSuccess) return e;
+    size_t off = 0, count = 0;
+    gz::train::bucket_range(n->game, k, &off, &count);
+    if (nr == ncclSuccess)
+      nr = c->allReduce(st.grad + off, st.grad + off, count, ncclFloat32, ncclSum, (ncclComm_t)comm, st.comm_stream);
+    return cudaSuccess;
+  };
+  const cudaError_t e = gz::train::loss_and_grad(st, n->d_weights, boards, side, pi, v, cnt, s, bucket_done);
+  if (e != cudaSuccess) return fail(GZ_ERR_CUDA, "training step: %s", cudaGetErrorString(e));
+  if (nr != ncclSuccess) return fail(GZ_ERR_NCCL, "ncclAllReduce: %s", c->errorString ? c->errorString(nr) : "?");
+  if (c) {
+    GZ_CUDA(cudaEventRecord(st.ev_comm, st.comm_stream));
+    GZ_CUDA(cudaStreamWaitEvent(s, st.ev_comm, 0));
+  }
+  if (update) {
+    const gz::train::AdamParams p{cfg->learning_rate, cfg->beta1, cfg->beta2, cfg->eps, cfg->weight_decay,
+                                  c ? 1.f / (float)world : 1.f};
+    GZ_CUDA(gz::train::adam_step(st, n->d_weights, p, s));
+    const gz_status ps = prepare_weights(n, s);
+    if (ps != GZ_OK) return ps;
+  }
+  if (h_loss) GZ_CUDA(cudaMemcpyAsync(h_loss, st.loss, 2 * sizeof(float), cudaMemcpyDeviceToHost, s));
+  GZ_CUDA(cudaStreamSynchronize(s));
+  return GZ_OK;
+}
+
+// Example order of pass `epoch`: a Fisher-Yates shuffle of 0 .. n-1 from a
+// splitmix64 stream of (seed, epoch).
+void epoch_order(int64_t n, uint64_t seed, int epoch, std::vector<int64_t>& order) {
+  order.resize((size_t)n);
+  for (int64_t i = 0; i < n; ++i) order[(size_t)i] = i;
+  SplitMix r(mix_seed(seed, 0x7A1ull + (uint64_t)epoch));
+  for (int64_t i = n - 1; i > 0; --i) {
+    const int64_t j = (int64_t)(r.next() % (uint64_t)(i + 1));
+    std::swap(order[(size_t)i], order[(size_t)j]);
+  }
+}
+
+}  // namespace
+
+void gz_train_config_default(gz_train_config* c) {
+  if (!c) return;
+  c->learning_rate = 1e-3f;
+  c->weight_decay = 1e-4f;
+  c->beta1 = 0.9f;
+  c->beta2 = 0.999f;
+  c->eps = 1e-8f;
+  c->batch_size = 64;
+  c->epochs = 10;
+  c->seed = 0x6A5Aull;
+}
+
+gz_status gz_net_loss_grad(gz_net* n, const int8_t* d_boards, const int8_t* d_side, const float* d_pi,
+                           const float* d_v, int cnt, float* d_grad, float h_loss[2], void* stream) {
+  if (!n || (cnt > 0 && (!d_boards || !d_side || !d_pi || !d_v))) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  if (cnt <= 0) return fail(GZ_ERR_INVALID_ARG, "batch of %d positions", cnt);
+  GZ_DEVICE(n->device);
+  gz_status st = ensure_train(n, cnt);
+  if (st != GZ_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  st = train_batch(n, d_boards, d_side, d_pi, d_v, cnt, nullptr, nullptr, 1, false, h_loss, s);
+  if (st != GZ_OK) return st;
+  if (d_grad) {
+    GZ_CUDA(cudaMemcpyAsync(d_grad, n->tr->grad, n->weight_count * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    GZ_CUDA(cudaStreamSynchronize(s));
+  }
+  return GZ_OK;
+}
+
+gz_status gz_net_train_step(gz_net* n, const int8_t* d_boards, const int8_t* d_side, const float* d_pi,
+                            const float* d_v, int cnt, const gz_train_config* cfg, void* comm, int world,
+                            float h_loss[2], void* stream) {
+  if (!n || (cnt > 0 && (!d_boards || !d_side || !d_pi || !d_v))) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  if (!valid_train_config(cfg)) return fail(GZ_ERR_INVALID_ARG, "bad training configuration");
+  if (cnt <= 0 || world < 1) return fail(GZ_ERR_INVALID_ARG, "batch of %d positions, world %d", cnt, world);
+  GZ_DEVICE(n->device);
+  const gz_status st = ensure_train(n, cnt);
+  if (st != GZ_OK) return st;
+  return train_batch(n, d_boards, d_side, d_pi, d_v, cnt, cfg, comm, world, true, h_loss, (cudaStream_t)stream);
+}
+
+gz_status gz_train_batch_indices(int64_t n, const gz_train_config* cfg, int epoch, int64_t step, int rank, int world,
+                                 int64_t* out) {
+  if (!valid_train_config(cfg) || !out || world < 1 || rank < 0 || rank >= world || epoch < 0 || step < 0)
+    return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  const int64_t B = cfg->batch_size, block = B * world;
+  if (n < 0 || (step + 1) * block > n)
+    return fail(GZ_ERR_INVALID_ARG, "step %lld of a pass over %lld examples (%lld per step)", (long long)step,
+                (long long)n, (long long)block);
+  std::vector<int64_t> order;
+  epoch_order(n, cfg->seed, epoch, order);
+  for (int64_t k = 0; k < B; ++k) out[k] = order[(size_t)(step * block + rank * B + k)];
+  return GZ_OK;
+}
+
+gz_status gz_train_bucket_range(int game, int k, size_t* offset, size_t* count) {
+  if (!valid_game(game) || !offset || !count || k < 0 || k >= gz::train::bucket_count(game))
+    return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  gz::train::bucket_range(game, k, offset, count);
+  return GZ_OK;
+}
+
+gz_status gz_net_train(gz_net* n, const gz_train_example* ex, int64_t count, const gz_train_config* cfg, void* comm,
+                       int rank, int world, gz_train_stats* stats) {
+  if (!n || (count > 0 && !ex)) return fail(GZ_ERR_INVALID_ARG, "null argument");
+  if (!valid_train_config(cfg)) return fail(GZ_ERR_INVALID_ARG, "bad training configuration");
+  if (world < 1 || rank < 0 || rank >= world) return fail(GZ_ERR_INVALID_ARG, "rank %d of %d", rank, world);
+  if (n->game != kTicTacToe && n->game != kConnect4)
+    return fail(GZ_ERR_UNSUPPORTED, "training examples hold TicTacToe or Connect4 boards");
+  if (n->kind != GZ_NET_GAT) return fail(GZ_ERR_UNSUPPORTED, "training is built for the GAT nets");
+  GZ_DEVICE(n->device);
+  const GameShape sh = game_shape(n->game);
+  const int B = cfg->batch_size, A = sh.actions, N = sh.nodes;
+  // canonical boards (own stones +1) -> board and side to move, as gz_net_predict
+  std::vector<int8_t> boards((size_t)count * N), side((size_t)count);
+  for (int64_t i = 0; i < count; ++i) {
+    int own = 0, opp = 0;
+    for (int k = 0; k < N; ++k) {
+      const int x = ex[i].board[k];
+      if (x < -1 || x > 1) return fail(GZ_ERR_INVALID_ARG, "example %lld: cell %d = %d", (long long)i, k, x);
+      own += x == 1;
+      opp += x == -1;
+    }
+    const int sd = own == opp ? 1 : -1;
+    side[(size_t)i] = (int8_t)sd;
+    for (int k = 0; k < N; ++k) boards[(size_t)i * N + k] = (int8_t)(ex[i].board[k] * sd);
+  }
+  const int64_t steps = count / ((int64_t)B * world);
+  gz_status st = ensure_train(n, B);
+  if (st != GZ_OK) return st;
+  // per-step staging: host (page-locked) and device
+  const size_t bytes = (size_t)B * (N + 1) + (size_t)B * (A + 1) * sizeof(float);
+  uint8_t *h = nullptr, *d = nullptr;
+  GZ_CUDA(cudaMallocHost(&h, bytes));
+  if (cudaMalloc(&d, bytes) != cudaSuccess) {
+    cudaFreeHost(h);
+    return fail(GZ_ERR_CUDA, "cudaMalloc of %zu bytes of training staging", bytes);
+  }
+  int8_t* hb = (int8_t*)h;
+  int8_t* hs = hb + (size_t)B * N;
+  float* hp = (float*)(h + (size_t)B * (N + 1));
+  float* hv = hp + (size_t)B * A;
+  const size_t off_pi = (size_t)B * (N + 1);
+  float ploss = 0.f, vloss = 0.f;
+  std::vector<int64_t> order;
+  for (int ep = 0; ep < cfg->epochs && st == GZ_OK; ++ep) {
+    epoch_order(count, cfg->seed, ep, order);
+    double sp = 0.0, sv = 0.0;
+    for (int64_t k = 0; k < steps && st == GZ_OK; ++k) {
+      for (int j = 0; j < B; ++j) {
+        const int64_t i = order[(size_t)(k * B * world + (int64_t)rank * B + j)];
+        memcpy(hb + (size_t)j * N, boards.data() + (size_t)i * N, (size_t)N);
+        hs[j] = side[(size_t)i];
+        memcpy(hp + (size_t)j * A, ex[i].pi, (size_t)A * sizeof(float));
+        hv[j] = ex[i].v;
+      }
+      float loss[2] = {0.f, 0.f};
+      if (cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, n->stream) != cudaSuccess) {
+        st = fail(GZ_ERR_CUDA, "training batch upload");
+        break;
+      }
+      st = train_batch(n, (const int8_t*)d, (const int8_t*)(d + (size_t)B * N), (const float*)(d + off_pi),
+                       (const float*)(d + off_pi) + (size_t)B * A, B, cfg, comm, world, true, loss, n->stream);
+      sp += loss[0];
+      sv += loss[1];
+    }
+    if (steps > 0) {
+      ploss = (float)(sp / (double)steps);
+      vloss = (float)(sv / (double)steps);
+    }
+  }
+  cudaFreeHost(h);
+  cudaFree(d);
+  if (stats) {
+    stats->policy_loss = ploss;
+    stats->value_loss = vloss;
+    stats->steps = n->tr->step;
+  }
+  return st;
 }
 
 // ------------------------------------------------------ failure detection --

@@ -24,6 +24,12 @@ constexpr bool kAutoFp16 = true;
 // bounded wait that gave up (GZ_ERR_TIMEOUT).  `who` prefixes the message.
 gz_status forward_error_status(int err, const char* who);
 
+// Game of a net (for the INeuralNet shim).
+int net_game(const gz_net* net);
+// ncclBroadcast of `count` floats from `root`, in place (NCCL loaded at run
+// time); for the INeuralNet shim's train_distributed.
+gz_status nccl_broadcast_floats(void* comm, float* d_buf, size_t count, int root, void* stream);
+
 // fp32 SIMT fused GAT forward (all layers + heads, one launch).
 //   boards [n][BOARD] int8, side [n] int8 (+1 / -1),
 //   weights: fp32 blob in gat_layout() order,

@@ -12,6 +12,7 @@
 #include "../../include/graphzero_b200.h"
 #include "../../include/graphzero_b200_compat.h"
 #include "gz_games.h"
+#include "gz_internal.h"
 #include "gz_synth.h"
 
 using namespace gz;
@@ -153,8 +154,44 @@ gz_net* net_of(INeuralNet* self) { return ((NetImpl*)self)->net; }
 
 void n_init(INeuralNet*, const IGame*) {}
 
-void n_train(INeuralNet*, TrainingExample*, int) {
-  fprintf(stderr, "graphzero_b200: training is not part of this library (INeuralNet::train)\n");
+// TrainingExample (networks/neural_network.h:10-14: canonical board and
+// policy as float arrays, value) -> the library's example record.
+bool to_records(gz_net* net, const float* const* boards, const float* const* pis, const float* vs, int n,
+                std::vector<gz_train_example>& out) {
+  int32_t shape[9];
+  if (gz_game_shape(gz::net_game(net), shape) != GZ_OK) return false;
+  const int nodes = shape[0], actions = shape[3];
+  out.assign((size_t)n, gz_train_example{});
+  for (int i = 0; i < n; ++i) {
+    for (int k = 0; k < nodes; ++k) out[(size_t)i].board[k] = (int32_t)boards[i][k];
+    for (int k = 0; k < actions; ++k) out[(size_t)i].pi[k] = pis[i][k];
+    out[(size_t)i].v = vs[i];
+  }
+  return true;
+}
+
+// INeuralNet::train (gat.cu:82-148): the reference's defaults (10 passes,
+// batches of 64, Adam 1e-3), one line of losses per call as it prints them.
+void n_train(INeuralNet* self, TrainingExample* ex, int n) {
+  gz_net* net = net_of(self);
+  if (!ex || n <= 0) return;
+  std::vector<const float*> b((size_t)n), p((size_t)n);
+  std::vector<float> v((size_t)n);
+  for (int i = 0; i < n; ++i) {
+    b[(size_t)i] = ex[i].board;
+    p[(size_t)i] = ex[i].pi;
+    v[(size_t)i] = ex[i].v;
+  }
+  std::vector<gz_train_example> rec;
+  gz_train_config cfg;
+  gz_train_config_default(&cfg);
+  gz_train_stats st{};
+  if (!to_records(net, b.data(), p.data(), v.data(), n, rec) ||
+      gz_net_train(net, rec.data(), n, &cfg, nullptr, 0, 1, &st) != GZ_OK) {
+    fprintf(stderr, "graphzero_b200: train failed: %s\n", gz_last_error());
+    return;
+  }
+  printf("Average Policy Loss: %f, Average Value Loss: %f\n", st.policy_loss, st.value_loss);
 }
 
 void n_predict(INeuralNet* self, const float* board, float* pi, float* v) {
@@ -184,8 +221,43 @@ void n_destroy(INeuralNet* self) {
   free(ni);
 }
 
-void n_train_distributed(INeuralNet*, float*, float*, float*, int, int, int, void*, void*) {
-  fprintf(stderr, "graphzero_b200: training is not part of this library (INeuralNet::train_distributed)\n");
+// INeuralNet::train_distributed (gat.cu:381-543): device arrays of canonical
+// boards [n][nodes], policies [n][actions] and values [n].  Like the
+// reference, rank 0's examples are broadcast first; every rank then trains
+// on its slice of each step with the gradients all-reduced (data parallel;
+// the reference's layer split across ranks is not kept).
+void n_train_distributed(INeuralNet* self, float* d_boards, float* d_pis, float* d_vs, int n, int rank, int world,
+                         void* comm, void* stream) {
+  gz_net* net = net_of(self);
+  int32_t shape[9];
+  if (n <= 0 || gz_game_shape(gz::net_game(net), shape) != GZ_OK) return;
+  const int nodes = shape[0], actions = shape[3];
+  std::vector<float> hb((size_t)n * nodes), hp((size_t)n * actions), hv((size_t)n);
+  if (gz::nccl_broadcast_floats(comm, d_boards, hb.size(), 0, stream) != GZ_OK ||
+      gz::nccl_broadcast_floats(comm, d_pis, hp.size(), 0, stream) != GZ_OK ||
+      gz::nccl_broadcast_floats(comm, d_vs, hv.size(), 0, stream) != GZ_OK ||
+      cudaMemcpyAsync(hb.data(), d_boards, hb.size() * 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream) ||
+      cudaMemcpyAsync(hp.data(), d_pis, hp.size() * 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream) ||
+      cudaMemcpyAsync(hv.data(), d_vs, hv.size() * 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream) ||
+      cudaStreamSynchronize((cudaStream_t)stream)) {
+    fprintf(stderr, "graphzero_b200: train_distributed: example broadcast failed: %s\n", gz_last_error());
+    return;
+  }
+  std::vector<const float*> b((size_t)n), p((size_t)n);
+  for (int i = 0; i < n; ++i) {
+    b[(size_t)i] = hb.data() + (size_t)i * nodes;
+    p[(size_t)i] = hp.data() + (size_t)i * actions;
+  }
+  std::vector<gz_train_example> rec;
+  gz_train_config cfg;
+  gz_train_config_default(&cfg);
+  gz_train_stats st{};
+  if (!to_records(net, b.data(), p.data(), hv.data(), n, rec) ||
+      gz_net_train(net, rec.data(), n, &cfg, comm, rank, world, &st) != GZ_OK) {
+    fprintf(stderr, "graphzero_b200: train_distributed failed: %s\n", gz_last_error());
+    return;
+  }
+  if (rank == 0) printf("Average Policy Loss: %f, Average Value Loss: %f\n", st.policy_loss, st.value_loss);
 }
 
 void n_broadcast(INeuralNet* self, int, int, void* comm, void* stream) {

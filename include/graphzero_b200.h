@@ -134,8 +134,9 @@ gz_status gz_net_create(const gz_net_config* cfg, int device, gz_net** out);
 /* INeuralNet::destroy (neural_network.h:25). */
 gz_status gz_net_destroy(gz_net* net);
 size_t gz_net_weight_count(const gz_net* net);
-/* Name of the forward kernel this handle launches: "gat_tc_bf16",
- * "gat_tc_fp16", "gat_simt_fp32" or "resnet_tc_bf16". */
+/* Name of the forward kernel and operand format this handle uses:
+ * "gat_tc_fp16", "gat_tc_bf16", "gat_simt_fp32", "resnet_tc_fp16" or
+ * "resnet_tc_bf16". */
 const char* gz_net_kernel_name(const gz_net* net);
 /* Weights as one fp32 blob in the documented layout (the replacement for the
  * reference's per-tensor cudaMalloc + cuRAND init, gat.cu:720-789). */
@@ -275,6 +276,69 @@ gz_status gz_train_examples_save(const char* path, int n_iters, const gz_train_e
  * malformed file, GZ_ERR_CAPACITY if capacity or max_iters is too small. */
 gz_status gz_train_examples_load(const char* path, gz_train_example* out, int64_t capacity, int32_t* counts,
                                  int max_iters, int* n_iters, int64_t* total);
+
+/* ---- training (GAT nets) ---------------------------------------------------
+ * Loss per position: -sum_a pi_a log p_a + (z - v)^2, averaged over the
+ * batch (the reference's loss gradients, networks/gat/gat.cu:1040-1109:
+ * softmax cross-entropy p - pi, value MSE 2 (v - z)).  fp32 forward and
+ * backward on CUDA cores, every reduction in a fixed order (a step is
+ * reproducible bit for bit), then Adam as torch::optim::Adam with weight
+ * decay added to the gradient (gat.cu:71).  After every step the net's
+ * tensor-core weights are repacked, so predictions use the new weights. */
+typedef struct {
+  float learning_rate; /* 1e-3 (gat.cu:712) */
+  float weight_decay;  /* 1e-4 (gat.cu:713) */
+  float beta1, beta2;  /* 0.9, 0.999 */
+  float eps;           /* 1e-8 */
+  int batch_size;      /* positions per rank per step, 64 (gat.cu:716) */
+  int epochs;          /* 10 (gat.cu:717) */
+  uint64_t seed;       /* example order: a fresh permutation per epoch */
+} gz_train_config;
+typedef struct {
+  float policy_loss; /* mean over the last epoch's steps (this rank's batches) */
+  float value_loss;
+  int64_t steps;     /* optimizer steps taken by the net so far */
+} gz_train_stats;
+/* The reference's defaults (gat.cu:702-718 init_model_config). */
+void gz_train_config_default(gz_train_config* cfg);
+/* Loss and gradient of one batch, no update: device boards [n][board bytes],
+ * side [n], target policies pi [n][actions], target values v [n].  The
+ * gradient (gz_net_weight_count floats, the weight blob's layout) goes to
+ * d_grad when it is not NULL, the two loss terms to h_loss (policy, value)
+ * when it is not NULL.  GAT nets of every game; GZ_ERR_UNSUPPORTED for the
+ * ResNet.  Synchronises. */
+gz_status gz_net_loss_grad(gz_net* net, const int8_t* d_boards, const int8_t* d_side, const float* d_pi,
+                           const float* d_v, int n, float* d_grad, float h_loss[2], void* stream);
+/* One optimizer step on one batch (device buffers as above).  With a
+ * communicator (ncclComm_t, world > 1) every rank passes its own batch: the
+ * gradient buckets (one per layer, one for the heads) are all-reduced on a
+ * side stream as the backward pass completes them, averaged, and every rank
+ * applies the same update (INeuralNet::train_distributed, gat.cu:381-543,
+ * whose gradient all-reduce is at 496-514).  h_loss (may be NULL) gets this
+ * rank's two loss terms.  Synchronises. */
+gz_status gz_net_train_step(gz_net* net, const int8_t* d_boards, const int8_t* d_side, const float* d_pi,
+                            const float* d_v, int n, const gz_train_config* cfg, void* nccl_comm, int world,
+                            float h_loss[2], void* stream);
+/* INeuralNet::train (gat.cu:82-148): `epochs` passes over n host examples
+ * (canonical boards as self-play writes them; TicTacToe and Connect4), each
+ * pass in a fresh seeded order, floor(n / (batch_size * world)) steps per
+ * pass, the last partial batch dropped as in the reference.  With a
+ * communicator every rank must hold the same examples: step k of a pass
+ * gives rank r the r-th batch_size slice of the k-th batch_size * world
+ * block of the order.  stats may be NULL. */
+gz_status gz_net_train(gz_net* net, const gz_train_example* examples, int64_t n, const gz_train_config* cfg,
+                       void* nccl_comm, int rank, int world, gz_train_stats* stats);
+/* The positions of step `step` of pass `epoch` that rank `rank` trains on
+ * (gz_net_train's order), as example indices into out[batch_size]; host
+ * only, for callers that stage their own batches. */
+gz_status gz_train_batch_indices(int64_t n, const gz_train_config* cfg, int epoch, int64_t step, int rank, int world,
+                                 int64_t* out);
+/* Gradient bucket k of a GAT net of `game` (k < layers: layer k's W, b and a;
+ * k == layers: the policy and value heads), as an offset and a length in
+ * floats of the weight layout; gz_net_train_step all-reduces the buckets
+ * from the heads down to layer 0, each as soon as the backward pass has
+ * produced it.  Host only. */
+gz_status gz_train_bucket_range(int game, int k, size_t* offset, size_t* count);
 
 /* ---- allocation-free leaf evaluation --------------------------------------
  * No counterpart in the reference.  For callers that may not allocate device

@@ -152,3 +152,51 @@ def chess_boards(n: int, seed: int) -> tuple[np.ndarray, np.ndarray]:
         b[i, 65] = rng.choice([-1, int(rng.integers(16, 24)), int(rng.integers(40, 48))])
     side = rng.choice([-1, 1], size=n).astype(np.int8)
     return b, side
+
+
+def torch_gat_loss(game: int, w: np.ndarray, boards: np.ndarray, side: np.ndarray, pi: np.ndarray, v: np.ndarray,
+                   dtype=torch.float64) -> tuple[float, float, np.ndarray]:
+    """Training loss of the GAT (mean policy cross-entropy, mean squared value
+    error) and its gradient with respect to the flat weight blob, by torch
+    autograd on an independent restatement of the forward."""
+    s = gz.game_shape(game)
+    o = gat_blob_views(game)
+    rp, col = gz.game_graph(game)
+    B, N = len(side), s.nodes
+    flat = torch.tensor(w.astype(np.float64), dtype=dtype, requires_grad=True)
+
+    def t(k):
+        p, sh = o[k]
+        return flat[p:p + int(np.prod(sh))].view(sh)
+
+    X = torch_features(game, boards, side).to(dtype)
+    src = torch.repeat_interleave(torch.arange(N), torch.tensor(np.diff(rp).astype(np.int64)))
+    dst = torch.tensor(col.astype(np.int64))
+    for l in range(s.layers):
+        Wh = X @ t(f"W{l}")
+        Whh = Wh.view(B, N, 8, 32)
+        a = t(f"a{l}")
+        ss = (Whh * a[:, 0]).sum(-1)
+        sn = (Whh * a[:, 1]).sum(-1)
+        e = torch.nn.functional.leaky_relu(ss[:, src] + sn[:, dst], 0.2)
+        m = torch.full((B, N, 8), -torch.inf, dtype=dtype).scatter_reduce(
+            1, src.view(1, -1, 1).expand(B, -1, 8), e, "amax").detach()
+        p = torch.exp(e - m[:, src])
+        z = torch.zeros(B, N, 8, dtype=dtype).index_add(1, src, p)
+        al = p / z[:, src]
+        out = torch.zeros(B, N, 8, 32, dtype=dtype).index_add(1, src, al.unsqueeze(-1) * Whh[:, dst])
+        X = torch.nn.functional.elu(out.reshape(B, N, 256) + t(f"b{l}"))
+    g = X.mean(1)
+    hv = torch.relu(g @ t("W_v1") + t("b_v1"))
+    val = torch.tanh(hv @ t("w_v2") + t("b_v2"))
+    if game == gz.TICTACTOE:
+        lg = (X @ t("w_pi")).squeeze(-1) + t("b_pi")
+    elif game == gz.CONNECT4:
+        lg = (X.view(B, 6, 7, 256).mean(1) @ t("w_pi")).squeeze(-1) + t("b_pi")
+    else:
+        lg = (X @ t("w_pi") + t("b_pi")).reshape(B, -1)
+    tp = torch.tensor(pi, dtype=dtype)
+    lp = -(tp * torch.log_softmax(lg, -1)).sum(-1).mean()
+    lv = ((torch.tensor(v, dtype=dtype) - val) ** 2).mean()
+    (lp + lv).backward()
+    return float(lp.detach()), float(lv.detach()), flat.grad.numpy()
