@@ -80,6 +80,7 @@ __host__ __device__ constexpr int chess_max_degree() {
   return m;
 }
 static_assert(chess_max_degree() <= kMaxDeg, "neighbour table width");
+static_assert(kMaxDeg % 4 == 0, "neighbour rows are read as words");
 
 // Shared memory map (bytes).
 constexpr int kStageStride = 144;                       // 32 used words + pad (conflict-free 16 B reads)
@@ -88,7 +89,10 @@ constexpr int kSmW = kSmX + 4 * 16384;
 constexpr int kSmB2 = kSmW + kWSlots * kWChunk;
 constexpr int kSmStage = kSmB2 + 4 * 8192;
 constexpr int kSmTsc = kSmStage + 2 * 128 * kStageStride;
-constexpr int kSmVec = kSmTsc + 2 * 130 * 16;  // t scores: [group][position][64 squares + pad row][4 heads]
+// t scores: [group][position][head][64 squares + pad], head-major so that a
+// head's loads of 32 lanes' neighbours are single words (random squares spread
+// over the 32 banks instead of 16-byte groups of 8)
+constexpr int kSmVec = kSmTsc + 2 * 130 * 16;
 constexpr int kVecFloats = 256;
 constexpr int kSmNbr = kSmVec + 2 * kVecFloats * 4;     // [64 squares][kMaxDeg] neighbour squares, 64 = none (pad)
 constexpr int kSmPool = kSmNbr + 64 * kMaxDeg;                    // [2 groups][4 quarters][32] node sums of one head
@@ -171,10 +175,6 @@ __device__ __forceinline__ uint32_t round_seed(int li, int l, int h) {
   return x;
 }
 __host__ __device__ constexpr uint32_t pair_mix(int m) { return (uint32_t)(m + 1) * 0x9E3779B9u ^ 0x7F4A7C15u; }
-
-__device__ __forceinline__ float comp(const float4& v, int k) {
-  return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
-}
 
 // Activations are carried multiplied by log2(e) from the first ELU on (the
 // next projection, its attention scores, the softmax and the policy softmax
@@ -278,8 +278,8 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
   for (int i = threadIdx.x; i < 2 * 128 * kStageStride / 4; i += blockDim.x) ((uint32_t*)(smem + kSmStage))[i] = 0u;
   // the pad row (square 64) of every (group, position) t-score table is -inf:
   // absent neighbours point at it and get weight 0
-  if (threadIdx.x < 16)
-    ((float*)(smem + kSmTsc))[((threadIdx.x >> 3) * 130 + ((threadIdx.x >> 2) & 1) * 65 + 64) * 4 + (threadIdx.x & 3)] = -INFINITY;
+  if (threadIdx.x < 16)  // (group, position, head) = threadIdx.x
+    ((float*)(smem + kSmTsc))[threadIdx.x * 65 + 64] = -INFINITY;
   if (threadIdx.x < 64) {  // neighbour table of square s (the chess board graph, build_graph_csr order)
     const int s = threadIdx.x;
     int d = 0;
@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
     const uint32_t tlane = tmem + ((uint32_t)(32 * qd) << 16);
     const int jw0 = 64 * pg;             // first node of this row's position: its e window
     uint8_t* srow = smem + kSmStage + (g * 128 + i) * kStageStride;
-    const float4* tsc = (const float4*)(smem + kSmTsc) + g * 130 + pg * 65;  // this row's position
+    const float* tsc = (const float*)(smem + kSmTsc) + (g * kGPT + pg) * 4 * 65;  // this row's position, head 0
     const uint8_t* my_nbr = nbr + sq * kMaxDeg;
     const int gbar = 3 + g;
     uint32_t aph = 0, pph = 0, dph[2] = {0, 0};
@@ -459,8 +459,9 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
           tmem_ld_wait();
 #pragma unroll
           for (int t = 0; t < 4; ++t) s[t] = hi[2 * t] + lo[2 * t];
-          ((float4*)(smem + kSmTsc))[g * 130 + pg * 65 + sq] =
-              make_float4(hi[1] + lo[1], hi[3] + lo[3], hi[5] + lo[5], hi[7] + lo[7]);
+          float* tw = (float*)(smem + kSmTsc) + (g * kGPT + pg) * 4 * 65 + sq;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) tw[t * 65] = hi[2 * t + 1] + lo[2 * t + 1];
         }
         tc_fence_before();
         named_bar_sync(1, kEpiWarps * 32);
@@ -550,12 +551,19 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
                              OpType<__half>::pack(wh[8 * ng + 4], wh[8 * ng + 5]), OpType<__half>::pack(wh[8 * ng + 6], wh[8 * ng + 7]));
           }
           {  // P2: softmax numerators over the square's neighbours -> e row (fp16)
-            // LeakyReLU is monotonic: the largest logit is lrelu(s + max_j t_j)
+            // LeakyReLU is monotonic: the largest logit is lrelu(s + max_j t_j).
+            // The square's neighbour list (36 bytes) is read as nine words
+            // into registers once per head: the stores below clobber memory,
+            // so byte loads would be repeated in the second loop.
+            uint32_t nb4[kMaxDeg / 4];
+#pragma unroll
+            for (int w = 0; w < kMaxDeg / 4; ++w) nb4[w] = ((const uint32_t*)my_nbr)[w];
+            auto nbr_k = [&](int k) { return (nb4[k >> 2] >> (8 * (k & 3))) & 0xffu; };
             float tj[kMaxDeg];
             float tmax = -INFINITY;
 #pragma unroll
             for (int k = 0; k < kMaxDeg; ++k) {
-              tj[k] = comp(tsc[my_nbr[k]], t);  // absent neighbours: the pad row, -inf
+              tj[k] = tsc[t * 65 + nbr_k(k)];  // absent neighbours: the pad entry, -inf
               tmax = fmaxf(tmax, tj[k]);
             }
             const float xm = s[t] + tmax;
@@ -568,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
               const __half e = __float2half_rn(ex2_approx(fmaxf(x, kLeakySlope * x) + c));
               z += __half2float(e);
               // absent neighbours write the pad half-word (64) of the row
-              asm volatile("st.shared.b16 [%0], %1;" ::"r"(sbase + 2 * my_nbr[k]), "h"(__half_as_ushort(e)) : "memory");
+              asm volatile("st.shared.b16 [%0], %1;" ::"r"(sbase + 2 * nbr_k(k)), "h"(__half_as_ushort(e)) : "memory");
             }
             // layer 0 reads the raw features: its Wh carries no log2(e) yet
             inv[t] = rcp_approx(z) * (l == 0 ? kLog2e : 1.f);
