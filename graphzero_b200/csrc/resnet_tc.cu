@@ -53,36 +53,47 @@ constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
 constexpr int kWChunk = 16384;              // 128 co rows x 64 ci x 2 B
 constexpr int kChunksPerTile = 9 + (kConvs - 1) * 18;
-// The ring moves one 64-channel chunk (16 KB) per copy, four slots deep: a
-// tap's two chunks land in two slots, and up to two taps' copies are in
-// flight while the MMAs of the current one run (measured on B200: faster
-// than two 32 KB slots holding a whole tap each, whose single copy in flight
-// exposed its L2 latency at every tap).  The weights are re-streamed for
-// every tile.
-constexpr int kWSlot = kWChunk;
-constexpr int kWSlots = 4;
+// The ring moves one tap (both 64-channel chunks, 32 KB) per copy, three
+// slots deep: two taps' copies are in flight while the MMAs of the current
+// one run.  Measured on B200: 32 KB bulk copies stream about 77 bytes per
+// cycle per SM from L2 against 45 for 16 KB copies, and a tile's tower
+// needs about 62 (the weights are re-streamed for every tile); two 32 KB
+// slots exposed a copy's latency at every tap, four 16 KB slots its
+// bandwidth.
+constexpr int kWSlot = 2 * kWChunk;
+constexpr int kWSlots = 3;
 constexpr uint32_t kTmemCols = 256;         // slot s accumulates in columns [128 s, 128 s + 128)
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
-constexpr int kGuard = 8;                   // guard rows before and after
-constexpr int kChunkRows = kRows + 2 * kGuard;
-constexpr int kActChunk = kChunkRows * 128; // one 64-channel K chunk, 18 KB
+constexpr int kActChunk = kRows * 128;      // one 64-channel K chunk, 16 KB
 constexpr int kActBytes = 2 * kActChunk;    // 128 channels
 
-// Shared memory map.  Slot s's activations start at s * kSlotBytes.
-constexpr int kSmA0 = 0;                          // block input / residual
-constexpr int kSmA1 = kSmA0 + kActBytes;          // intermediate (and the stem input)
-constexpr int kSlotBytes = 2 * kActBytes;
-constexpr int kSmW = 2 * kSlotBytes;              // weight ring
-constexpr int kSmBn = kSmW + kWSlots * kWSlot;    // [2 parity][scale 128, shift 128]
-constexpr int kSmHead = kSmBn + 2 * 2 * kC * 4;   // [2 halves][128 rows][3] partial head dots
-constexpr int kSmFeat = kSmHead + 2 * kRows * 3 * 4;  // [3 pos][84 policy + 42 value] features
-constexpr int kSmHid = kSmFeat + kGPT * 128 * 4;  // [3][128] value hidden
-constexpr int kSmLogit = kSmHid + kGPT * 128 * 4; // [3][8]
-constexpr int kSmBar = kSmLogit + kGPT * 8 * 4;
+// Shared memory map.  The folded BN parameters, barriers and the like come
+// first; then the activations, slot s's at kSmAct + s * kSlotBytes, back to
+// back; then the weight ring.  A tap's shifted view of a buffer starts up to
+// 8 rows before its first row or ends up to 8 rows after its last: those
+// rows belong to the neighbouring buffer (or to the regions before and after
+// the activations) and feed only output rows the tap's mask disables, so
+// the buffers need no guard rows.
+constexpr int kSmBn = 0;                          // [2 parity][scale 128, shift 128]
+constexpr int kSmBar = kSmBn + 2 * 2 * kC * 4;
 constexpr int kNumBars = 2 * kWSlots + 5;         // full, empty, acc_full[2], act_ready[2], drain
 constexpr int kSmMisc = kSmBar + kNumBars * 8;
-constexpr int kSmemBytes = kSmMisc + 16;
-static_assert(kSmA1 % 1024 == 0 && kSmW % 1024 == 0 && kActChunk % 1024 == 0, "swizzle alignment");
+constexpr int kSmAct = 3072;
+constexpr int kSmA0 = 0;                          // block input / residual (offsets inside a slot)
+constexpr int kSmA1 = kSmA0 + kActBytes;          // intermediate (and the stem input)
+constexpr int kSlotBytes = 2 * kActBytes;
+constexpr int kSmW = kSmAct + 2 * kSlotBytes;     // weight ring
+constexpr int kSmemBytes = kSmW + kWSlots * kWSlot;
+// Head scratch during the last convolution's epilogue, inside the slot's A1
+// buffer (that convolution's input, dead once its accumulator is complete).
+constexpr int kHdHead = 0;                          // [2 halves][128 rows][3] partial head dots
+constexpr int kHdFeat = kHdHead + 2 * kRows * 3 * 4;  // [3 pos][84 policy + 42 value] features
+constexpr int kHdHid = kHdFeat + kGPT * 128 * 4;    // [3][128] value hidden
+constexpr int kHdLogit = kHdHid + kGPT * 128 * 4;   // [3][8]
+static_assert(kHdLogit + kGPT * 8 * 4 <= kActBytes, "head scratch fits in an activation buffer");
+static_assert(kSmMisc + 16 <= kSmAct, "header region");
+static_assert(kSmAct >= 1024, "room before the first buffer for a tap's 8-row lead");
+static_assert(kSmAct % 1024 == 0 && kSmW % 1024 == 0 && kActChunk % 1024 == 0, "swizzle alignment");
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 // Packed layout (bytes) after the weight chunks: per conv, scale[128] and
@@ -184,11 +195,6 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
   const int lane = threadIdx.x & 31;
   const ResLayout RL = res_layout();
 
-  // Guard rows of the activation buffers hold finite values (zeros).
-  for (int i = threadIdx.x; i < 4 * kActBytes / 16; i += blockDim.x) {
-    const int byte = i * 16, row = (byte % kActChunk) / 128;
-    if (row < kGuard || row >= kGuard + kRows) *(uint4*)(smem + byte) = make_uint4(0, 0, 0, 0);
-  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kWSlots; ++s) {
       mbar_init(&full[s], 1);
@@ -217,18 +223,16 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
       bool ok = true;
       // consumption order: per tile pair, per conv, slot A's nine taps then slot B's
       for (int ta = blockIdx.x; ta < p.num_tiles && ok; ta += 2 * gridDim.x)
-        for (int u = 0; u < 18 * kConvs && ok; ++u) {
+        for (int u = 0; u < 18 * kConvs && ok; ++u, ++q) {
           const int cv = u / 18, t = u % 9;
-          // stem tap: one chunk; block conv tap: its two adjacent chunks, one slot each
-          const int nchunk = cv == 0 ? 1 : 2;
-          for (int h = 0; h < nchunk && ok; ++h, ++q) {
-            const int s = q % kWSlots;
-            const int c = cv == 0 ? t : 9 + (cv - 1) * 18 + 2 * t + h;
-            ok = mbar_wait(&empty[s], ((q / kWSlots) & 1) ^ 1, abort_flag, kWaitLimitNs);
-            if (!ok) break;
-            mbar_arrive_expect_tx(&full[s], kWChunk);
-            bulk_g2s(smem + kSmW + s * kWSlot, p.packed + (size_t)c * kWChunk, kWChunk, &full[s]);
-          }
+          // stem tap: one 16 KB chunk; block conv tap: its two adjacent chunks in one copy
+          const int c = cv == 0 ? t : 9 + (cv - 1) * 18 + 2 * t;
+          const uint32_t bytes = cv == 0 ? kWChunk : 2 * kWChunk;
+          const int s = q % kWSlots;
+          ok = mbar_wait(&empty[s], ((q / kWSlots) & 1) ^ 1, abort_flag, kWaitLimitNs);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&full[s], bytes);
+          bulk_g2s(smem + kSmW + s * kWSlot, p.packed + (size_t)c * kWChunk, bytes, &full[s]);
         }
       for (uint32_t k = (q > kWSlots ? q - kWSlots : 0); k < q; ++k)
         mbar_wait(&full[k % kWSlots], (k / kWSlots) & 1, abort_flag, kWaitLimitNs);
@@ -249,33 +253,33 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
           tc_fence_after();
           const uint32_t dt = tmem + (uint32_t)(128 * sl);
           // input buffer: stem reads A1 (input planes), block conv1 reads A0, conv2 reads A1
-          const uint32_t in = smem_u32(smem + sl * kSlotBytes + ((cv == 0 || (cv & 1) == 0) ? kSmA1 : kSmA0));
+          const uint32_t in = smem_u32(smem + kSmAct + sl * kSlotBytes + ((cv == 0 || (cv & 1) == 0) ? kSmA1 : kSmA0));
           const int nchunk = cv == 0 ? 1 : 2;
           // One thread issues every MMA, so its own instruction stream bounds
           // the MMA rate: the taps are unrolled (masks stay in registers) and
           // descriptors advance by adding (byte offset >> 4) to the start
           // address field (shared addresses stay below 2^18: no carry).
-          const uint64_t in_desc = sw128_desc_shifted(in + kGuard * 128);
+          const uint64_t in_desc = sw128_desc_shifted(in);
           const uint64_t w_desc = sw128_desc(smem_u32(smem + kSmW));
 #pragma unroll
           for (int t = 0; t < 9; ++t) {
             const int shift = 7 * tap_dy(t) + tap_dx(t);  // rows; x 128 bytes
             if (!ok) break;
-            for (int c = 0; c < nchunk && ok; ++c) {  // 64-channel K chunks of this tap, one slot each
-              const int s = q % kWSlots;
-              ok = mbar_wait(&full[s], (q / kWSlots) & 1, abort_flag, kWaitLimitNs);
-              ++q;
-              if (!ok) break;
-              tc_fence_after();
-              const uint64_t wd = w_desc + (uint64_t)((s * kWSlot) >> 4);
+            const int s = q % kWSlots;  // this tap's weights: one slot
+            ok = mbar_wait(&full[s], (q / kWSlots) & 1, abort_flag, kWaitLimitNs);
+            ++q;
+            if (!ok) break;
+            tc_fence_after();
+            for (int c = 0; c < nchunk; ++c) {  // 64-channel K chunks of this tap
+              const uint64_t wd = w_desc + (uint64_t)((s * kWSlot + c * kWChunk) >> 4);
               const uint64_t ad = in_desc + (uint64_t)((c * kActChunk + shift * 128) >> 4);
               mma_f16_ss_masked(dt, ad, wd, idesc, (t | c) != 0, kMask.m[t]);
               if (cv != 0) {
 #pragma unroll
                 for (int kk = 1; kk < 4; ++kk) mma_f16_ss_masked(dt, ad + kk * 2, wd + kk * 2, idesc, 1, kMask.m[t]);
               }
-              mma_commit(&empty[s]);
             }
+            mma_commit(&empty[s]);
           }
           if (ok) mma_commit(&acc_full[sl]);
         }
@@ -307,8 +311,8 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
           f2 = sd == 1 ? 1.f : 0.f;
         }
         if (hf == 0) {
-          uint8_t* row = smem + sl * kSlotBytes + kSmA1 + (kGuard + r) * 128;
-          const int rs = (kGuard + r) & 7;
+          uint8_t* row = smem + kSmAct + sl * kSlotBytes + kSmA1 + r * 128;
+          const int rs = r & 7;
           *(uint4*)(row + ((0 ^ rs) << 4)) = make_uint4(ResOp<OpT>::pack(f0, f1), ResOp<OpT>::pack(f2, 0.f), 0u, 0u);
           *(uint4*)(row + ((1 ^ rs) << 4)) = make_uint4(0u, 0u, 0u, 0u);
         }
@@ -327,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
         ++accph[sl];
         if (!ok) break;
         tc_fence_after();
-        uint8_t* const sbase = smem + sl * kSlotBytes;
+        uint8_t* const sbase = smem + kSmAct + sl * kSlotBytes;
         const uint32_t tslot = tlane + (uint32_t)(128 * sl);
         const bool second = cv > 0 && (cv & 1) == 0;  // second conv of a block: residual add
         const bool last = cv == kConvs - 1;
@@ -352,9 +356,9 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
             y[4 * k + 3] = fmaf(acc[4 * k + 3], sc.w, sh.w);
           }
           // row r, channels c0..c0+31: K chunk c0/64, 16-byte units (c0%64)/8 + u
-          const int rs = (kGuard + r) & 7;
-          uint8_t* orow = outb + (c0 >> 6) * kActChunk + (kGuard + r) * 128;
-          const uint8_t* rrow = sbase + kSmA0 + (c0 >> 6) * kActChunk + (kGuard + r) * 128;
+          const int rs = r & 7;
+          uint8_t* orow = outb + (c0 >> 6) * kActChunk + r * 128;
+          const uint8_t* rrow = sbase + kSmA0 + (c0 >> 6) * kActChunk + r * 128;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int unit = ((((c0 & 63) >> 3) + u) ^ rs) << 4;
@@ -393,12 +397,12 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
         }
         // ---------------- heads (fp32) ----------------
         tc_fence_before();
-        float* part = (float*)(smem + kSmHead);
+        float* part = (float*)(sbase + kSmA1 + kHdHead);
         part[(hf * kRows + r) * 3 + 0] = hp0;
         part[(hf * kRows + r) * 3 + 1] = hp1;
         part[(hf * kRows + r) * 3 + 2] = hv;
         named_bar_sync(1, kEpiWarps * 32);
-        float* feat = (float*)(smem + kSmFeat);  // [3][128]: 84 policy, 42 value
+        float* feat = (float*)(sbase + kSmA1 + kHdFeat);  // [3][128]: 84 policy, 42 value
         const int tid = threadIdx.x;
         if (tid < kGPT * kN) {
           const int g = tid / kN, li = tid % kN, row = tid;
@@ -414,8 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
           feat[g * 128 + 84 + li] = (x - __ldg(vb + 2)) * sc + __ldg(vb + 1);
         }
         named_bar_sync(1, kEpiWarps * 32);
-        float* hid = (float*)(smem + kSmHid);
-        float* logit = (float*)(smem + kSmLogit);
+        float* hid = (float*)(sbase + kSmA1 + kHdHid);
+        float* logit = (float*)(sbase + kSmA1 + kHdLogit);
         for (int t = tid; t < kGPT * kResValueHidden; t += kEpiWarps * 32) {
           const int g = t / kResValueHidden, u = t % kResValueHidden;
           float a = __ldg(p.w + RL.val_fc1_b + u);
