@@ -26,7 +26,7 @@ namespace {
 constexpr int kThreads = 256;  // one thread per hidden column
 
 template <int G> struct SimtCfg;
-template <> struct SimtCfg<kTicTacToe> { static constexpr int GPC = 4; };  // graphs per CTA
+template <> struct SimtCfg<kTicTacToe> { static constexpr int GPC = 1; };  // graphs per CTA
 template <> struct SimtCfg<kConnect4> { static constexpr int GPC = 1; };
 template <> struct SimtCfg<kChess> { static constexpr int GPC = 1; };
 
@@ -93,8 +93,49 @@ __global__ void __launch_bounds__(kThreads) gat_simt_kernel(const float* __restr
       float acc[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) acc[r] = 0.f;
-      for (int k = 0; k < fin; ++k) {
-        float wk = __ldg(W + (size_t)k * kHidden + c);
+      // W[k][c] for 16 K steps at a time, the next 16 loaded while these are
+      // used (an L2 round trip per K step otherwise); X read as 16-byte
+      // broadcasts (rows are 1 KB apart); the FMA order is k ascending
+      int k = 0;
+      if (fin % 16 == 0) {
+        float wn[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) wn[j] = __ldg(W + (size_t)j * kHidden + c);
+        for (; k < fin; k += 16) {
+          float wc[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) wc[j] = wn[j];
+          if (k + 16 < fin) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) wn[j] = __ldg(W + (size_t)(k + 16 + j) * kHidden + c);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              const float4 x = *(const float4*)(X + r * kHidden + k + 4 * q);
+              acc[r] = fmaf(x.x, wc[4 * q], acc[r]);
+              acc[r] = fmaf(x.y, wc[4 * q + 1], acc[r]);
+              acc[r] = fmaf(x.z, wc[4 * q + 2], acc[r]);
+              acc[r] = fmaf(x.w, wc[4 * q + 3], acc[r]);
+            }
+          }
+        }
+      }
+      for (; k + 4 <= fin; k += 4) {
+        const float w0 = __ldg(W + (size_t)k * kHidden + c), w1 = __ldg(W + (size_t)(k + 1) * kHidden + c);
+        const float w2 = __ldg(W + (size_t)(k + 2) * kHidden + c), w3 = __ldg(W + (size_t)(k + 3) * kHidden + c);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const float4 x = *(const float4*)(X + r * kHidden + k);
+          acc[r] = fmaf(x.x, w0, acc[r]);
+          acc[r] = fmaf(x.y, w1, acc[r]);
+          acc[r] = fmaf(x.z, w2, acc[r]);
+          acc[r] = fmaf(x.w, w3, acc[r]);
+        }
+      }
+      for (; k < fin; ++k) {
+        const float wk = __ldg(W + (size_t)k * kHidden + c);
 #pragma unroll
         for (int r = 0; r < R; ++r) acc[r] = fmaf(X[r * kHidden + k], wk, acc[r]);
       }
