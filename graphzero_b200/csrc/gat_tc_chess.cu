@@ -574,9 +574,11 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
             for (int k = 0; k < kMaxDeg; ++k) {
               const float x = s[t] + tj[k];
               const __half e = __float2half_rn(ex2_approx(fmaxf(x, kLeakySlope * x) + c));
-              z += __half2float(e);
-              // absent neighbours write the pad half-word (64) of the row
-              asm volatile("st.shared.b16 [%0], %1;" ::"r"(sbase + 2 * nbr_k(k)), "h"(__half_as_ushort(e)) : "memory");
+              z += __half2float(e);  // absent neighbours: e = 0
+              // only real neighbours store (all absent ones would hit the same
+              // bank group of their rows: up to 12 four-way conflicted stores)
+              if (nbr_k(k) != 64u)
+                asm volatile("st.shared.b16 [%0], %1;" ::"r"(sbase + 2 * nbr_k(k)), "h"(__half_as_ushort(e)) : "memory");
             }
             // layer 0 reads the raw features: its Wh carries no log2(e) yet
             inv[t] = rcp_approx(z) * (l == 0 ? kLog2e : 1.f);
