@@ -572,28 +572,33 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
         eside = p.side[pos];
       }
     };
-    fetch_cell(blockIdx.x);
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-      // -- encode the tile's positions into X chunk 0 (features 0..15) --
-      {
-        uint32_t wv[4] = {0, 0, 0, 0};
-        if (ehalf == 0 && egj < kGPT && tile * kGPT + egj < p.n) {
-          const int8_t cell[1] = {(int8_t)ecell};
-          float f[4];
-          encode_node(kConnect4, cell, eside, 0, f);
-          wv[0] = OpType<OpT>::pack(f[0], f[1]);
-          wv[1] = OpType<OpT>::pack(f[2], f[3]);
-        }
-        *(uint4*)(sX + sw128_offset(ej, ehalf * 8)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    // encode a tile's positions into X chunk 0 (features 0..15) and release
+    // its layer-0 projection.  The first tile is encoded here, every later
+    // one during the previous tile's last layer, before its pooling, so that
+    // the layer-0 projection and scores run under the pooling and the heads.
+    auto encode = [&](int tile) {
+      uint32_t wv[4] = {0, 0, 0, 0};
+      if (ehalf == 0 && egj < kGPT && tile * kGPT + egj < p.n) {
+        const int8_t cell[1] = {(int8_t)ecell};
+        float f[4];
+        encode_node(kConnect4, cell, eside, 0, f);
+        wv[0] = OpType<OpT>::pack(f[0], f[1]);
+        wv[1] = OpType<OpT>::pack(f[2], f[3]);
       }
+      *(uint4*)(sX + sw128_offset(ej, ehalf * 8)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&x_ready[0]);
+    };
+    fetch_cell(blockIdx.x);
+    encode(blockIdx.x);
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
 
       // One layer.  `last` is a compile-time flag, so the last layer's head
       // code does not share registers with the head loop of the others.
       auto layer = [&](int l, auto last_tag) -> bool {
         constexpr bool last = decltype(last_tag)::value;
+        if constexpr (last) fetch_cell(tile + gridDim.x);  // the next tile's cells, used after the head loop
         // per-layer bias into shared memory, by layer parity
         float* vec = (float*)(smem + kSmVec) + (l & 1) * kVecFloats;
         vec[threadIdx.x] = __ldg(p.w + C4Off::b(l) + threadIdx.x) * kLog2e;
@@ -782,8 +787,8 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
             hb[4] = __ldg(p.w + C4Off::b_pi);
             hb[5] = __ldg(p.w + C4Off::b_v2);
           }
-          fetch_cell(tile + gridDim.x);  // the next tile's encode input
-          named_bar_sync(1, kEpiWarps * 32);  // every head's column sums complete
+          named_bar_sync(1, kEpiWarps * 32);  // every head's column sums complete; transpose scratch free
+          if (tile + (int)gridDim.x < p.num_tiles) encode(tile + gridDim.x);
           float* mean = (float*)(smem + kSmMean);  // [3][256] node means
           float* lgw = (float*)(smem + kSmLgW);    // [warp][3 x 7] policy partial sums
           {
@@ -861,7 +866,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
               if (lane == 0) p.v[pos] = tanhf(vv + hb[5]);
             }
           }
-          named_bar_sync(1, kEpiWarps * 32);  // head scratch (X tile) free for the next encode
+          named_bar_sync(1, kEpiWarps * 32);  // head scratch (t-score region, X chunk 3) read by all before the next tile
           // the node means overwrote group 0's "no neighbour" t-score row: restore it
           if (threadIdx.x < 4) ((float*)(smem + kSmTsc))[128 * 4 + threadIdx.x] = -INFINITY;
         }
