@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1) resnet_tc_kernel(ResParams p) {
                              ResOp<OpT>::pack(y[8 * u + 4], y[8 * u + 5]), ResOp<OpT>::pack(y[8 * u + 6], y[8 * u + 7]));
           }
           if (last) {
-#pragma unroll 4
+#pragma unroll
             for (int e = 0; e < 32; ++e) {
               hp0 = fmaf(y[e], __ldg(p.w + RL.pol_w + c0 + e), hp0);
               hp1 = fmaf(y[e], __ldg(p.w + RL.pol_w + kC + c0 + e), hp1);
