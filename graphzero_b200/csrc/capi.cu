@@ -1000,7 +1000,7 @@ gz_status gz_mcts_create(const gz_mcts_config* cfg, int device, gz_mcts** out) {
   d.dir_alpha = cfg->dirichlet_alpha;
   d.dir_eps = cfg->dirichlet_eps;
   d.seed = cfg->seed;
-  const size_t T = (size_t)d.trees, NC = T * d.node_cap, EC = T * d.edge_cap, L = T * d.leaves;
+  const size_t T = (size_t)d.trees, EC = T * d.edge_cap, L = T * d.leaves;
   gz_status st = GZ_OK;
   auto alloc = [&](auto** p, size_t bytes) {
     if (st != GZ_OK) return;
@@ -1008,24 +1008,28 @@ gz_status gz_mcts_create(const gz_mcts_config* cfg, int device, gz_mcts** out) {
     if (e != cudaSuccess) st = fail(GZ_ERR_CUDA, "cudaMalloc %zu bytes: %s", bytes, cudaGetErrorString(e));
     else m->allocs.push_back((void*)*p);
   };
-  alloc(&d.n, NC * 4); alloc(&d.vl, NC * 4); alloc(&d.first_edge, NC * 4); alloc(&d.n_edges, NC);
-  alloc(&d.side, NC); alloc(&d.expanded, NC); alloc(&d.terminal, NC); alloc(&d.term_value, NC * 4);
-  alloc(&d.board, NC * kMctsBoardStride);
-  alloc(&d.P, EC * 4); alloc(&d.W, EC * 4); alloc(&d.Nv, EC * 4); alloc(&d.VL, EC * 4); alloc(&d.child, EC * 4);
-  alloc(&d.action, EC);
-  alloc(&d.root, T * 4); alloc(&d.node_count, T * 4); alloc(&d.edge_count, T * 4); alloc(&d.move_no, T * 4);
-  alloc(&d.path_nodes, L * kMctsMaxDepth * 4); alloc(&d.path_edges, L * kMctsMaxDepth * 4); alloc(&d.path_len, L * 4);
+  alloc(&d.tree, T * sizeof(MctsTree));
+  alloc(&d.edges, EC * sizeof(MctsEdge));
+  alloc(&d.path_edges, L * kMctsMaxDepth * 4); alloc(&d.path_len, L * 4); alloc(&d.leaf_legal, L * 4);
   alloc(&d.leaf_board, L * d.N); alloc(&d.leaf_side, L); alloc(&d.leaf_terminal, L);
   alloc(&d.err, 4);
   alloc(&m->d_pi, L * d.A * 4); alloc(&m->d_v, L * 4);
   alloc(&m->d_tmp, T * 4 * 2);
   if (st == GZ_OK) {
+    // empty roots (no position loaded: an all-zero board, first player to move)
+    std::vector<MctsTree> h(T);
+    for (MctsTree& tr : h) {
+      memset(&tr, 0, sizeof tr);
+      tr.fe = -1;
+      tr.meta = (uint32_t)kNodeCreated << 16;
+      tr.node_count = 1;
+      tr.side = 1;
+    }
     cudaError_t e = cudaMemset(d.err, 0, 4);
-    if (e == cudaSuccess) e = cudaMemset(d.root, 0, T * 4);
-    if (e == cudaSuccess) e = cudaMemset(d.node_count, 0, T * 4);
-    if (e == cudaSuccess) e = cudaMemset(d.expanded, 0, NC);
+    if (e == cudaSuccess) e = cudaMemcpy(d.tree, h.data(), T * sizeof(MctsTree), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(d.path_len, 0, L * 4);
-    if (e == cudaSuccess) e = cudaMemset(d.path_nodes, 0, L * kMctsMaxDepth * 4);
+    if (e == cudaSuccess) e = cudaMemset(d.path_edges, 0, L * kMctsMaxDepth * 4);
+    if (e == cudaSuccess) e = cudaMemset(d.leaf_legal, 0, L * 4);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) st = fail(GZ_ERR_CUDA, "init: %s", cudaGetErrorString(e));
   }

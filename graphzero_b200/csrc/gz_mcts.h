@@ -1,8 +1,15 @@
-// Device-side state of the batched PUCT search (structure of arrays).
+// Device-side state of the batched PUCT search.
 //
-// Every tree owns a private pool of nodes and edges; indices are local to the
-// tree (global = tree * cap + local).  A node keeps its position so a leaf can
-// be encoded without replaying the path.  This replaces the reference's
+// Every tree owns one contiguous pool of edge records, so a warp walking its
+// tree touches one region of memory (a few pages, not one page per field
+// array).  A node exists only through the edge that leads to it: that edge
+// carries the child's statistics (its visit and in-flight counts are the
+// edge's, since every path through the child passes the edge) and, once the
+// child is expanded, where the child's own edges start and how many there
+// are.  A selection level is therefore one round of loads: the current node's
+// edges.  The root's fields live in the per-tree record, with its position;
+// positions below the root are not stored (a selection replays its actions
+// on the root position in registers).  This replaces the reference's
 // MCTSNode with fixed 218-entry child arrays and child pointers
 // (mcts/mcts.cuh:25-36).
 #pragma once
@@ -16,38 +23,53 @@ namespace gz {
 constexpr int kMctsBoardStride = 48;  // bytes per stored position (>= 42, 16-aligned)
 constexpr int kMctsMaxDepth = 48;     // >= longest game (42 plies) + 1
 
+// Child flags (MctsEdge::meta bits 16-23, MctsTree::meta likewise).
+enum : uint32_t {
+  kNodeCreated = 1u,   // the child exists (counts against node_capacity)
+  kNodeExpanded = 2u,  // its edges exist
+  kNodeTerminal = 4u,  // the game is over at the child
+  kNodeLoss = 8u,      // terminal with a loss for the child's player to move (value -1; else 0)
+};
+
+__host__ __device__ __forceinline__ uint32_t meta_action(uint32_t m) { return m & 0xffu; }
+__host__ __device__ __forceinline__ int meta_edges(uint32_t m) { return (int)((m >> 8) & 0xffu); }
+__host__ __device__ __forceinline__ uint32_t meta_flags(uint32_t m) { return (m >> 16) & 0xffu; }
+
+struct alignas(16) MctsEdge {  // 32 bytes: one per (expanded node, legal action)
+  float P;                     // prior (legal-renormalised, root noise mixed in)
+  float W;                     // value sum, from the view of the player to move at the parent
+  int32_t Nv;                  // completed visits (= the child's)
+  int32_t VL;                  // selections in flight (= the child's)
+  int32_t child_fe;            // the child's first edge, once expanded
+  uint32_t meta;               // action | child edge count << 8 | child flags << 16
+  int32_t pad[2];
+};
+static_assert(sizeof(MctsEdge) == 32, "edge record");
+
+struct alignas(16) MctsTree {  // 128 bytes per tree
+  int8_t board[kMctsBoardStride];  // root position
+  int32_t fe;                      // root's first edge
+  uint32_t meta;                   // root's edge count << 8 | flags << 16
+  int32_t n, vl;                   // root's completed visits and selections in flight
+  int32_t node_count, edge_count;  // pool use (nodes are counted, not stored)
+  int32_t move_no;                 // moves played since the game started
+  int32_t side;                    // player to move at the root
+  int32_t pad[12];
+};
+static_assert(sizeof(MctsTree) == 128, "tree record");
+
 struct MctsDev {
   int game, trees, leaves, vl_k, node_cap, edge_cap, N, A;
   float c_puct, dir_alpha, dir_eps;
   unsigned long long seed;
-  // nodes [trees * node_cap]
-  int* n;           // completed backups through the node
-  int* vl;          // selections in flight through the node
-  int* first_edge;  // local edge index of the first child edge
-  int8_t* n_edges;
-  int8_t* side;     // player to move at the node
-  int8_t* expanded;
-  int8_t* terminal;
-  float* term_value;  // value for the player to move at a terminal node
-  int8_t* board;      // [trees * node_cap][kMctsBoardStride]
-  // edges [trees * edge_cap]
-  float* P;
-  float* W;  // value sum from the perspective of the player to move at the parent
-  int* Nv;   // visit count
-  int* VL;   // virtual visits in flight
-  int* child;
-  int8_t* action;
-  // per tree
-  int* root;
-  int* node_count;
-  int* edge_count;
-  int* move_no;
-  // selection paths [trees][leaves][kMctsMaxDepth]
-  int* path_nodes;
-  int* path_edges;
-  int* path_len;  // [trees][leaves]
-  // leaf batch (network input) [trees * leaves]
-  int8_t* leaf_board;  // [trees * leaves][N]
+  MctsTree* tree;   // [trees]
+  MctsEdge* edges;  // [trees][edge_cap]
+  // selections of the current wave, slot = tree * leaves + k
+  int* path_edges;     // [slots][kMctsMaxDepth] edge chosen at each level
+  int* path_len;       // [slots]
+  uint32_t* leaf_legal;  // [slots] legal actions at the leaf (bit a)
+  // leaf batch (network input) [slots]
+  int8_t* leaf_board;  // [slots][N]
   int8_t* leaf_side;
   int8_t* leaf_terminal;
   int* err;  // first error code seen by a kernel (0 = none)

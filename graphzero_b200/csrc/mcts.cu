@@ -9,6 +9,13 @@
 // visit counts are bit-identical to a sequential CPU run of the same
 // algorithm fed the same evaluations.
 //
+// Memory: a tree is one contiguous pool of 32-byte edge records (gz_mcts.h).
+// A selection level loads the current node's edges (one record per lane, one
+// round of loads) and nothing else: the chosen edge already carries the
+// child's counts, flags and first edge.  The position is carried down the
+// path in registers, two cells per lane, and the rules run warp-wide on it
+// (ballots over the cells), so creating a leaf reads no stored position.
+//
 // Reference semantics (self_play/self_play.cu):
 //   score    Q + c_puct * P * sqrt(N_parent) / (1 + n)           720-736
 //   expand   children for the legal actions, P from the policy  698-718, 627-629
@@ -69,63 +76,127 @@ __device__ float sample_gamma(float alpha, unsigned long long seed, unsigned lon
 
 __device__ __forceinline__ void set_err(int* err, int code) { atomicCAS(err, 0, code); }
 
-__device__ void init_node(const MctsDev& d, size_t gnode, const int8_t* board, int side, int terminal, float tv) {
-  d.n[gnode] = 0;
-  d.vl[gnode] = 0;
-  d.first_edge[gnode] = -1;
-  d.n_edges[gnode] = 0;
-  d.side[gnode] = (int8_t)side;
-  d.expanded[gnode] = 0;
-  d.terminal[gnode] = (int8_t)terminal;
-  d.term_value[gnode] = tv;
-  int8_t* dst = d.board + gnode * kMctsBoardStride;
-  for (int i = 0; i < kMctsBoardStride; ++i) dst[i] = i < d.N ? board[i] : 0;
+__device__ __forceinline__ uint32_t make_meta(uint32_t action, int n_edges, uint32_t flags) {
+  return action | ((uint32_t)n_edges << 8) | (flags << 16);
+}
+
+// ---------------------------------------------------------------------------
+// Warp-wide rules on a position held two cells per lane: lane j holds cell j
+// (`lo`) and cell 32 + j (`hi`), 0 where the board has no such cell.  They
+// restate gz_games.h's apply_action / outcome_after / action_legal with
+// ballots; every lane must call them.
+// ---------------------------------------------------------------------------
+
+// Apply action a for player p; returns the square written or -1 (apply_action).
+__device__ __forceinline__ int warp_apply(int game, int N, int& lo, int& hi, int a, int p, int lane) {
+  if (game == kConnect4) {
+    // the lowest empty cell of column a: the empty cell r * 7 + a with the largest r
+    const unsigned mlo = __ballot_sync(kFull, lane < N && lane % 7 == a && lo == 0);
+    const unsigned mhi = __ballot_sync(kFull, lane + 32 < N && (lane + 32) % 7 == a && hi == 0);
+    const int sq = mhi ? 63 - __clz(mhi) : (mlo ? 31 - __clz(mlo) : -1);
+    if (sq == lane) lo = p;
+    if (sq == lane + 32) hi = p;
+    return sq;
+  }
+  const int cell = __shfl_sync(kFull, lo, a & 31);
+  if (a < 0 || a >= N || cell != 0) return -1;
+  if (lane == a) lo = p;
+  return a;
+}
+
+// Outcome after player p wrote `sq`: 1 = p won, 2 = draw (board full), 0 = the
+// game continues (outcome_after: Connect4 counts the lines through sq,
+// TicTacToe tests all eight lines).
+__device__ __forceinline__ int warp_outcome(int game, int N, int lo, int hi, int sq, int p, int lane) {
+  const unsigned long long mine =
+      (unsigned long long)__ballot_sync(kFull, lane < N && lo == p) |
+      ((unsigned long long)__ballot_sync(kFull, lane + 32 < N && hi == p) << 32);
+  const unsigned filled = __ballot_sync(kFull, lane < N && lo != 0);
+  bool win = false;
+  if (game == kConnect4) {
+    // lane j < 16: the window of four in direction j / 4 that holds sq at
+    // position j % 4
+    if (lane < 16 && sq >= 0) {
+      const int dir = lane >> 2, off = lane & 3;
+      const int dr = dir == 0 ? 0 : 1, dc = dir == 0 ? 1 : (dir == 1 ? 0 : (dir == 2 ? 1 : -1));
+      const int r0 = sq / 7 - off * dr, c0 = sq % 7 - off * dc;
+      win = true;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int r = r0 + k * dr, c = c0 + k * dc;
+        win = win && r >= 0 && r < 6 && c >= 0 && c < 7 && ((mine >> (r * 7 + c)) & 1ull);
+      }
+    }
+  } else if (lane < 8) {
+    // rows (lanes 0-2), columns (3-5), diagonals (6, 7)
+    const int a = lane < 3 ? 3 * lane : (lane < 6 ? lane - 3 : (lane == 6 ? 0 : 2));
+    const int st = lane < 3 ? 1 : (lane < 6 ? 3 : (lane == 6 ? 4 : 2));
+    win = ((mine >> a) & 1ull) && ((mine >> (a + st)) & 1ull) && ((mine >> (a + 2 * st)) & 1ull);
+  }
+  if (__any_sync(kFull, win)) return 1;
+  const unsigned need = game == kConnect4 ? 0x7fu : 0x1ffu;  // Connect4: full iff the top row is
+  return (filled & need) == need ? 2 : 0;
+}
+
+// Legal actions (action_legal): cell a empty, a < A (the top row for Connect4).
+__device__ __forceinline__ uint32_t warp_legal(int A, int lo, int lane) {
+  return __ballot_sync(kFull, lane < A && lo == 0);
+}
+
+__device__ void reset_tree(MctsTree* tr, const int8_t* board, int N, int side, int move_no) {
+  for (int i = 0; i < kMctsBoardStride; ++i) tr->board[i] = i < N ? board[i] : (int8_t)0;
+  tr->fe = -1;
+  tr->meta = make_meta(0, 0, kNodeCreated);
+  tr->n = 0;
+  tr->vl = 0;
+  tr->node_count = 1;
+  tr->edge_count = 0;
+  tr->move_no = move_no;
+  tr->side = side;
 }
 
 __global__ void reset_kernel(MctsDev d, const int8_t* __restrict__ boards, const int8_t* __restrict__ side) {
-  int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= d.trees) return;
-  d.root[t] = 0;
-  d.node_count[t] = 1;
-  d.edge_count[t] = 0;
-  d.move_no[t] = 0;
-  init_node(d, (size_t)t * d.node_cap, boards + (size_t)t * d.N, side[t], 0, 0.0f);
+  reset_tree(d.tree + t, boards + (size_t)t * d.N, d.N, side[t], 0);
 }
 
 __global__ void select_kernel(MctsDev d) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= d.trees) return;
-  const size_t nb = (size_t)t * d.node_cap, eb = (size_t)t * d.edge_cap;
+  MctsTree* tr = d.tree + t;
+  MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
+  const int N = d.N;
+  // the root's record: one 128-byte line
+  const int r_fe = tr->fe;
+  const uint32_t r_meta = tr->meta;
+  const int r_n = tr->n, r_side = tr->side;
+  int r_vl = tr->vl;
+  int node_count = tr->node_count;
+  const int r_lo = lane < N ? tr->board[lane] : 0;
+  const int r_hi = lane + 32 < N ? tr->board[lane + 32] : 0;
   for (int k = 0; k < d.leaves; ++k) {
     const size_t slot = (size_t)t * d.leaves + k;
-    int* pn = d.path_nodes + slot * kMctsMaxDepth;
     int* pe = d.path_edges + slot * kMctsMaxDepth;
-    int s = d.root[t];
-    int depth = 0;
-    if (lane == 0) pn[0] = s;
-    while (true) {
-      // the node's fields in one round of loads (read before the test: the
-      // fields of an unexpanded node are read and not used)
-      const size_t gs = nb + s;
-      const int8_t expanded = d.expanded[gs], terminal = d.terminal[gs];
-      const int ne = d.n_edges[gs], fe = d.first_edge[gs];
-      const int vl_s = d.vl[gs];
-      const int np = d.n[gs] + d.vl_k * vl_s;
-      if (!expanded || terminal) break;
+    int fe = r_fe, ne = meta_edges(r_meta);
+    uint32_t flags = meta_flags(r_meta);
+    int np = r_n + d.vl_k * r_vl;  // N_parent with the virtual visits in flight
+    r_vl += 1;
+    int lo = r_lo, hi = r_hi, side = r_side, depth = 0;
+    while ((flags & kNodeExpanded) && !(flags & kNodeTerminal)) {
       const float sq = __fsqrt_rn((float)np);
       float u = -INFINITY;
       int idx = 0x7fffffff;
-      int child = -1;  // this lane's edge's child and virtual visits, loaded with its statistics
-      int vl_e = 0;
-      if (lane < ne) {
-        const size_t e = eb + fe + lane;
-        child = d.child[e];
-        vl_e = d.VL[e];
-        const int vlk = d.vl_k * vl_e;
-        const int nev = d.Nv[e] + vlk;
-        const float q = nev > 0 ? __fdiv_rn(__fsub_rn(d.W[e], (float)vlk), (float)nev) : 0.0f;
-        const float u1 = __fmul_rn(d.c_puct, d.P[e]);
+      int4 ra = make_int4(0, 0, 0, 0), rb = make_int4(0, 0, 0, 0);
+      if (lane < ne) {  // this lane's edge: P, W, Nv, VL | child_fe, meta
+        const int4* rec = (const int4*)(E + fe + lane);
+        ra = rec[0];
+        rb = rec[1];
+        const int vlk = d.vl_k * ra.w;
+        const int nev = ra.z + vlk;
+        const float q = nev > 0 ? __fdiv_rn(__fsub_rn(__int_as_float(ra.y), (float)vlk), (float)nev) : 0.0f;
+        const float u1 = __fmul_rn(d.c_puct, __int_as_float(ra.x));
         const float u2 = __fmul_rn(u1, sq);
         const float u3 = __fdiv_rn(u2, __fadd_rn(1.0f, (float)nev));
         u = __fadd_rn(q, u3);
@@ -138,51 +209,51 @@ __global__ void select_kernel(MctsDev d) {
         if (uo > u || (uo == u && io < idx)) { u = uo; idx = io; }
       }
       const int e = fe + idx;
-      int c = __shfl_sync(kFull, child, idx);
-      const int vl_c = __shfl_sync(kFull, vl_e, idx);
-      if (lane == 0) {  // virtual visits: the values loaded above, stored back incremented
-        d.vl[nb + s] = vl_s + 1;
-        d.VL[eb + e] = vl_c + 1;
-        if (c < 0) {
-          c = d.node_count[t];
-          if (c >= d.node_cap) {
-            set_err(d.err, kMctsNodeCap);
-            c = -1;
-          } else {
-            d.node_count[t] = c + 1;
-            int8_t b[kMctsBoardStride];
-            const int8_t* pb = d.board + (nb + s) * kMctsBoardStride;
-            for (int i = 0; i < kMctsBoardStride; ++i) b[i] = pb[i];
-            const int mover = d.side[nb + s];
-            const int sq_written = apply_action(d.game, b, d.action[eb + e], mover);
-            const int oc = outcome_after(d.game, b, sq_written, mover);
-            init_node(d, nb + c, b, -mover, oc != 0, oc == 1 ? -1.0f : 0.0f);
-            d.child[eb + e] = c;
-          }
-        }
-        if (depth + 1 >= kMctsMaxDepth) {
-          set_err(d.err, kMctsDepth);
-          c = -1;
-        }
-        if (c >= 0) {
-          pe[depth] = e;
-          pn[depth + 1] = c;
-        }
+      const int c_nv = __shfl_sync(kFull, ra.z, idx), c_vl = __shfl_sync(kFull, ra.w, idx);
+      const int c_fe = __shfl_sync(kFull, rb.x, idx);
+      const uint32_t c_meta = (uint32_t)__shfl_sync(kFull, rb.y, idx);
+      uint32_t cflags = meta_flags(c_meta);
+      if (!(cflags & kNodeCreated) && node_count >= d.node_cap) {
+        if (lane == 0) set_err(d.err, kMctsNodeCap);
+        break;
       }
-      c = __shfl_sync(kFull, c, 0);
-      __syncwarp();
-      if (c < 0) break;
+      if (depth + 1 >= kMctsMaxDepth) {
+        if (lane == 0) set_err(d.err, kMctsDepth);
+        break;
+      }
+      if (lane == 0) {  // a virtual visit on the edge (and so on the child); the path
+        E[e].VL = c_vl + 1;
+        pe[depth] = e;
+      }
+      const int mover = side;
+      const int sqw = warp_apply(d.game, N, lo, hi, (int)meta_action(c_meta), mover, lane);
+      side = -side;
       ++depth;
-      s = c;
+      if (!(cflags & kNodeCreated)) {  // a new node: counted, and the game may end there
+        ++node_count;
+        const int oc = warp_outcome(d.game, N, lo, hi, sqw, mover, lane);
+        cflags = kNodeCreated | (oc != 0 ? kNodeTerminal : 0u) | (oc == 1 ? kNodeLoss : 0u);
+        if (lane == 0) E[e].meta = make_meta(meta_action(c_meta), 0, cflags);
+      }
+      flags = cflags;
+      fe = c_fe;
+      ne = meta_edges(c_meta);
+      np = c_nv + d.vl_k * c_vl;
     }
+    const uint32_t legal = warp_legal(d.A, lo, lane);
     if (lane == 0) {
-      d.vl[nb + s] += 1;
       d.path_len[slot] = depth;
-      d.leaf_side[slot] = d.side[nb + s];
-      d.leaf_terminal[slot] = d.terminal[nb + s];
+      d.leaf_side[slot] = (int8_t)side;
+      d.leaf_terminal[slot] = (flags & kNodeTerminal) ? 1 : 0;
+      d.leaf_legal[slot] = legal;
     }
-    for (int i = lane; i < d.N; i += 32) d.leaf_board[slot * d.N + i] = d.board[(nb + s) * kMctsBoardStride + i];
-    __syncwarp();
+    int8_t* lb = d.leaf_board + slot * N;
+    if (lane < N) lb[lane] = (int8_t)lo;
+    if (lane + 32 < N) lb[lane + 32] = (int8_t)hi;
+  }
+  if (lane == 0) {
+    tr->vl = r_vl;
+    tr->node_count = node_count;
   }
 }
 
@@ -190,23 +261,32 @@ __global__ void backup_kernel(MctsDev d, const float* __restrict__ pi, const flo
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= d.trees) return;
-  const size_t nb = (size_t)t * d.node_cap, eb = (size_t)t * d.edge_cap;
+  MctsTree* tr = d.tree + t;
+  MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
+  int r_fe = tr->fe;
+  uint32_t r_meta = tr->meta;
+  int r_n = tr->n, r_vl = tr->vl, edge_count = tr->edge_count;
+  const int move_no = tr->move_no;
   for (int k = 0; k < d.leaves; ++k) {
     const size_t slot = (size_t)t * d.leaves + k;
-    const int* pn = d.path_nodes + slot * kMctsMaxDepth;
     const int* pe = d.path_edges + slot * kMctsMaxDepth;
     const int len = d.path_len[slot];
-    const int leaf = pn[len];
-    const size_t gl = nb + leaf;
+    // the path's edges, level i in lane i % 32
+    const int e0 = lane < len ? pe[lane] : -1;
+    const int e1 = lane + 32 < len ? pe[lane + 32] : -1;
+    const int le = len > 0 ? __shfl_sync(kFull, len - 1 < 32 ? e0 : e1, (len - 1) & 31) : -1;  // edge into the leaf
+    uint32_t lmeta = r_meta;
+    if (len > 0 && lane == 0) lmeta = E[le].meta;  // read and written by lane 0 only
+    lmeta = __shfl_sync(kFull, lmeta, 0);
+    const uint32_t lflags = meta_flags(lmeta);
     float val;
-    if (d.terminal[gl]) {
-      val = d.term_value[gl];
+    if (lflags & kNodeTerminal) {
+      val = (lflags & kNodeLoss) ? -1.0f : 0.0f;
     } else {
       val = value[slot];
-      if (!d.expanded[gl]) {
-        const int8_t* bd = d.board + gl * kMctsBoardStride;
+      if (!(lflags & kNodeExpanded)) {
         const float* p = pi + slot * d.A;
-        const bool lg = lane < d.A && action_legal(d.game, bd, lane);
+        const bool lg = lane < d.A && ((d.leaf_legal[slot] >> lane) & 1u);
         const unsigned mask = __ballot_sync(kFull, lg);
         const int cnt = __popc(mask);
         float sum = 0.0f;
@@ -214,85 +294,95 @@ __global__ void backup_kernel(MctsDev d, const float* __restrict__ pi, const flo
         if (lane == 0) {
           for (int a = 0; a < d.A; ++a)
             if ((mask >> a) & 1u) sum = __fadd_rn(sum, p[a]);
-          fe = d.edge_count[t];
+          fe = edge_count;
           if (fe + cnt > d.edge_cap) {
             set_err(d.err, kMctsEdgeCap);
             fe = -1;
           } else {
-            d.edge_count[t] = fe + cnt;
+            edge_count = fe + cnt;
           }
         }
         sum = __shfl_sync(kFull, sum, 0);
         fe = __shfl_sync(kFull, fe, 0);
         if (fe >= 0) {
           if (lg) {
-            const size_t e = eb + fe + __popc(mask & ((1u << lane) - 1u));
-            d.P[e] = __fdiv_rn(p[lane], sum);
-            d.W[e] = 0.0f;
-            d.Nv[e] = 0;
-            d.VL[e] = 0;
-            d.child[e] = -1;
-            d.action[e] = (int8_t)lane;
+            int4* rec = (int4*)(E + fe + __popc(mask & ((1u << lane) - 1u)));
+            rec[0] = make_int4(__float_as_int(__fdiv_rn(p[lane], sum)), __float_as_int(0.0f), 0, 0);
+            rec[1] = make_int4(-1, (int)make_meta((uint32_t)lane, 0, 0), 0, 0);
           }
           __syncwarp();
           if (lane == 0) {
-            if (d.dir_eps > 0.0f && leaf == d.root[t] && cnt > 0) {
+            if (d.dir_eps > 0.0f && len == 0 && cnt > 0) {
               // Root exploration noise: P = (1 - eps) P + eps Dir(alpha).
               float g[32], gs = 0.0f;
               for (int j = 0; j < cnt; ++j) {
-                g[j] = sample_gamma(d.dir_alpha, d.seed, (unsigned long long)t, ((unsigned long long)d.move_no[t] << 8) | j);
+                g[j] = sample_gamma(d.dir_alpha, d.seed, (unsigned long long)t, ((unsigned long long)move_no << 8) | j);
                 gs += g[j];
               }
-              for (int j = 0; j < cnt; ++j) {
-                const size_t e = eb + fe + j;
-                d.P[e] = (1.0f - d.dir_eps) * d.P[e] + d.dir_eps * (gs > 0.0f ? g[j] / gs : 1.0f / cnt);
-              }
+              for (int j = 0; j < cnt; ++j)
+                E[fe + j].P = (1.0f - d.dir_eps) * E[fe + j].P + d.dir_eps * (gs > 0.0f ? g[j] / gs : 1.0f / cnt);
             }
-            d.first_edge[gl] = fe;
-            d.n_edges[gl] = (int8_t)cnt;
-            d.expanded[gl] = 1;
+            const uint32_t nm = make_meta(meta_action(lmeta), cnt, lflags | kNodeExpanded);
+            if (len > 0) {
+              E[le].child_fe = fe;
+              E[le].meta = nm;
+            } else {
+              r_fe = fe;
+              r_meta = nm;
+            }
           }
+          r_fe = __shfl_sync(kFull, r_fe, 0);
+          r_meta = __shfl_sync(kFull, r_meta, 0);
         }
       }
     }
     __syncwarp();
-    // The path's levels touch distinct nodes and edges, so the lanes update
-    // them at once; the value at level i is -val for i = len - 1 and changes
-    // sign every level up (the same additions as a walk from the leaf, and
-    // the leaves of a tree still back up in order).
-    if (lane == 0) {
-      d.n[gl] += 1;
-      d.vl[gl] -= 1;
+    // Every level's edge gets the visit, the value and its virtual visit
+    // back; the levels are distinct edges, so the lanes update them at once.
+    // The value at level i is -val for i = len - 1 and changes sign every
+    // level up (the same additions as a walk from the leaf; the leaves of a
+    // tree still back up in order, and level i is always lane i % 32).
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int i = lane + 32 * h, e = h ? e1 : e0;
+      if (i < len) {
+        const float x = ((len - 1 - i) & 1) ? val : -val;
+        int4* rec = (int4*)(E + e);
+        int4 s = rec[0];
+        s.y = __float_as_int(__fadd_rn(__int_as_float(s.y), x));
+        s.z += 1;
+        s.w -= 1;
+        rec[0] = s;
+      }
     }
-    for (int i = lane; i < len; i += 32) {
-      const float x = ((len - 1 - i) & 1) ? val : -val;
-      const size_t e = eb + pe[i];
-      d.Nv[e] += 1;
-      d.W[e] = __fadd_rn(d.W[e], x);
-      d.VL[e] -= 1;
-      const size_t gs = nb + pn[i];
-      d.n[gs] += 1;
-      d.vl[gs] -= 1;
-    }
+    r_n += 1;
+    r_vl -= 1;
     __syncwarp();
+  }
+  if (lane == 0) {
+    tr->fe = r_fe;
+    tr->meta = r_meta;
+    tr->n = r_n;
+    tr->vl = r_vl;
+    tr->edge_count = edge_count;
   }
 }
 
 __global__ void root_visits_kernel(MctsDev d, int32_t* __restrict__ visits, float* __restrict__ wsum) {
-  int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= d.trees) return;
-  const size_t nb = (size_t)t * d.node_cap, eb = (size_t)t * d.edge_cap;
+  const MctsTree* tr = d.tree + t;
+  const MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
   for (int a = 0; a < d.A; ++a) {
     visits[(size_t)t * d.A + a] = 0;
     if (wsum) wsum[(size_t)t * d.A + a] = 0.0f;
   }
-  const int r = d.root[t];
-  if (!d.expanded[nb + r]) return;
-  const int fe = d.first_edge[nb + r], ne = d.n_edges[nb + r];
+  if (!(meta_flags(tr->meta) & kNodeExpanded)) return;
+  const int fe = tr->fe, ne = meta_edges(tr->meta);
   for (int k = 0; k < ne; ++k) {
-    const size_t e = eb + fe + k;
-    visits[(size_t)t * d.A + d.action[e]] = d.Nv[e];
-    if (wsum) wsum[(size_t)t * d.A + d.action[e]] = d.W[e];
+    const MctsEdge& e = E[fe + k];
+    visits[(size_t)t * d.A + meta_action(e.meta)] = e.Nv;
+    if (wsum) wsum[(size_t)t * d.A + meta_action(e.meta)] = e.W;
   }
 }
 
@@ -301,37 +391,36 @@ __global__ void root_visits_kernel(MctsDev d, int32_t* __restrict__ visits, floa
 // sampling an action with probability N_a / sum N; afterwards the most visited
 // action (lowest action on ties).  Integer arithmetic only.
 __global__ void choose_kernel(MctsDev d, int temp_moves, int32_t* __restrict__ actions) {
-  int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= d.trees) return;
-  const size_t nb = (size_t)t * d.node_cap, eb = (size_t)t * d.edge_cap;
-  const int r = d.root[t];
-  const int fe = d.first_edge[nb + r], ne = d.expanded[nb + r] ? (int)d.n_edges[nb + r] : 0;
+  const MctsTree* tr = d.tree + t;
+  const MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
+  const int fe = tr->fe, ne = (meta_flags(tr->meta) & kNodeExpanded) ? meta_edges(tr->meta) : 0;
   int pick = -1;
   if (ne > 0) {
     long long total = 0;
     int best = 0;
     for (int k = 0; k < ne; ++k) {
-      int nv = d.Nv[eb + fe + k];
+      const int nv = E[fe + k].Nv;
       total += nv;
-      if (nv > d.Nv[eb + fe + best]) best = k;
+      if (nv > E[fe + best].Nv) best = k;
     }
     pick = best;
-    if (d.move_no[t] < temp_moves && total > 0) {
-      unsigned long long h = rng64(d.seed, (unsigned long long)t, (unsigned long long)d.move_no[t], 0xC4);
-      long long x = (long long)(((h >> 32) * (unsigned long long)total) >> 32);
+    if (tr->move_no < temp_moves && total > 0) {
+      const unsigned long long h = rng64(d.seed, (unsigned long long)t, (unsigned long long)tr->move_no, 0xC4);
+      const long long x = (long long)(((h >> 32) * (unsigned long long)total) >> 32);
       long long cum = 0;
       for (int k = 0; k < ne; ++k) {
-        cum += d.Nv[eb + fe + k];
+        cum += E[fe + k].Nv;
         if (cum > x) { pick = k; break; }
       }
     }
   }
   if (pick >= 0) {
-    actions[t] = d.action[eb + fe + pick];
+    actions[t] = (int32_t)meta_action(E[fe + pick].meta);
   } else {  // unexpanded root: first legal action
-    const int8_t* bd = d.board + (nb + r) * kMctsBoardStride;
     int a = 0;
-    while (a < d.A - 1 && !action_legal(d.game, bd, a)) ++a;
+    while (a < d.A - 1 && !action_legal(d.game, tr->board, a)) ++a;
     actions[t] = a;
   }
 }
@@ -341,47 +430,44 @@ __global__ void choose_kernel(MctsDev d, int temp_moves, int32_t* __restrict__ a
 // otherwise the pool restarts from the new position.  A finished game
 // restarts from the empty board with the first player to move.
 __global__ void play_kernel(MctsDev d, const int32_t* __restrict__ actions, int reserve, int8_t* __restrict__ done) {
-  int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= d.trees) return;
-  const size_t nb = (size_t)t * d.node_cap, eb = (size_t)t * d.edge_cap;
-  const int r = d.root[t];
+  MctsTree* tr = d.tree + t;
+  const MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
   const int a = actions[t];
-  int child = -1;
-  if (d.expanded[nb + r]) {
-    const int fe = d.first_edge[nb + r], ne = d.n_edges[nb + r];
+  const MctsEdge* ce = nullptr;  // the edge of the played action, if its child exists
+  if (meta_flags(tr->meta) & kNodeExpanded) {
+    const int fe = tr->fe, ne = meta_edges(tr->meta);
     for (int k = 0; k < ne; ++k)
-      if (d.action[eb + fe + k] == a) child = d.child[eb + fe + k];
+      if ((int)meta_action(E[fe + k].meta) == a && (meta_flags(E[fe + k].meta) & kNodeCreated)) ce = E + fe + k;
   }
   int8_t b[kMctsBoardStride];
-  for (int i = 0; i < kMctsBoardStride; ++i) b[i] = d.board[(nb + r) * kMctsBoardStride + i];
-  const int mover = d.side[nb + r];
+  for (int i = 0; i < kMctsBoardStride; ++i) b[i] = tr->board[i];
+  const int mover = tr->side;
   const int sq = apply_action(d.game, b, a, mover);
   const int oc = sq < 0 ? 2 : outcome_after(d.game, b, sq, mover);
   if (done) done[t] = (int8_t)(oc != 0);
   if (oc != 0) {
     for (int i = 0; i < kMctsBoardStride; ++i) b[i] = 0;
-    d.root[t] = 0;
-    d.node_count[t] = 1;
-    d.edge_count[t] = 0;
-    d.move_no[t] = 0;
-    init_node(d, nb, b, 1, 0, 0.0f);
-  } else if (child >= 0 && d.node_count[t] + reserve <= d.node_cap) {
-    d.root[t] = child;
-    d.move_no[t] += 1;
+    reset_tree(tr, b, d.N, 1, 0);
+  } else if (ce && tr->node_count + reserve <= d.node_cap) {
+    for (int i = 0; i < kMctsBoardStride; ++i) tr->board[i] = b[i];
+    tr->fe = ce->child_fe;
+    tr->meta = make_meta(0, meta_edges(ce->meta), meta_flags(ce->meta));
+    tr->n = ce->Nv;
+    tr->vl = ce->VL;
+    tr->side = -mover;
+    tr->move_no += 1;
   } else {
-    d.root[t] = 0;
-    d.node_count[t] = 1;
-    d.edge_count[t] = 0;
-    d.move_no[t] += 1;
-    init_node(d, nb, b, -mover, 0, 0.0f);
+    reset_tree(tr, b, d.N, -mover, tr->move_no + 1);
   }
 }
 
 __global__ void tree_sizes_kernel(MctsDev d, int32_t* nodes, int32_t* edges) {
-  int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= d.trees) return;
-  nodes[t] = d.node_count[t];
-  edges[t] = d.edge_count[t];
+  nodes[t] = d.tree[t].node_count;
+  edges[t] = d.tree[t].edge_count;
 }
 
 inline int blocks_for(int n, int per) { return (n + per - 1) / per; }

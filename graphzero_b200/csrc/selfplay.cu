@@ -40,23 +40,23 @@ namespace {
 // one-hot on the most visited action (the first edge, i.e. the lowest
 // action, on ties).
 __device__ void root_policy(const MctsDev& d, int t, int temp_moves, float* pi) {
-  const size_t nb = (size_t)t * d.node_cap, eb = (size_t)t * d.edge_cap;
-  const int r = d.root[t];
+  const MctsTree* tr = d.tree + t;
+  const MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
   for (int a = 0; a < d.A; ++a) pi[a] = 0.0f;
-  if (!d.expanded[nb + r]) return;
-  const int fe = d.first_edge[nb + r], ne = d.n_edges[nb + r];
+  if (!(meta_flags(tr->meta) & kNodeExpanded)) return;
+  const int fe = tr->fe, ne = meta_edges(tr->meta);
   long long total = 0;
   int best = 0;
   for (int k = 0; k < ne; ++k) {
-    const int nv = d.Nv[eb + fe + k];
+    const int nv = E[fe + k].Nv;
     total += nv;
-    if (nv > d.Nv[eb + fe + best]) best = k;
+    if (nv > E[fe + best].Nv) best = k;
   }
   if (ne == 0) return;
-  if (d.move_no[t] < temp_moves && total > 0) {
-    for (int k = 0; k < ne; ++k) pi[d.action[eb + fe + k]] = (float)d.Nv[eb + fe + k] / (float)total;
+  if (tr->move_no < temp_moves && total > 0) {
+    for (int k = 0; k < ne; ++k) pi[meta_action(E[fe + k].meta)] = (float)E[fe + k].Nv / (float)total;
   } else {
-    pi[d.action[eb + fe + best]] = 1.0f;
+    pi[meta_action(E[fe + best].meta)] = 1.0f;
   }
 }
 
@@ -69,12 +69,11 @@ __global__ void record_kernel(MctsDev d, SelfPlayDev s, int temp_moves) {
     return;
   }
   const size_t slot = (size_t)t * s.max_moves + k;
-  const size_t root = (size_t)t * d.node_cap + d.root[t];
-  const int8_t side = d.side[root];
-  const int8_t* b = d.board + root * kMctsBoardStride;
-  for (int i = 0; i < d.N; ++i) s.log_board[slot * d.N + i] = (int8_t)(b[i] * side);
+  const MctsTree* tr = d.tree + t;
+  const int side = tr->side;
+  for (int i = 0; i < d.N; ++i) s.log_board[slot * d.N + i] = (int8_t)(tr->board[i] * side);
   root_policy(d, t, temp_moves, s.log_pi + slot * d.A);
-  s.log_side[slot] = side;
+  s.log_side[slot] = (int8_t)side;
   s.log_len[t] = k + 1;
 }
 
@@ -84,10 +83,10 @@ __global__ void finish_kernel(MctsDev d, SelfPlayDev s, const int32_t* __restric
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= d.trees) return;
   s.fin_len[t] = 0;
-  const size_t root = (size_t)t * d.node_cap + d.root[t];
+  const MctsTree* tr = d.tree + t;
   int8_t b[kMctsBoardStride];
-  for (int i = 0; i < kMctsBoardStride; ++i) b[i] = d.board[root * kMctsBoardStride + i];
-  const int mover = d.side[root];
+  for (int i = 0; i < kMctsBoardStride; ++i) b[i] = tr->board[i];
+  const int mover = tr->side;
   const int sq = apply_action(d.game, b, actions[t], mover);
   const int oc = sq < 0 ? 2 : outcome_after(d.game, b, sq, mover);
   if (oc == 0) return;
