@@ -14,7 +14,16 @@
 //     position's 4672 logits, staged in shared memory and written with one
 //     bulk copy per position;
 //   * value: mean-pool over the 64 squares (warp reduce-scatter), then the
-//     256 -> 64 ReLU -> 1 tanh head in fp32.
+//     256 -> 64 ReLU -> 1 tanh head in fp32;
+//   * as in the Connect4 kernel, layer l + 1's projection runs under layer
+//     l's head loop: K chunk t of X(l + 1) holds heads t and t + 4 and its
+//     MMAs are issued as soon as both groups have finished head t, into three
+//     128-column accumulator blocks that rotate from layer to layer (eight
+//     layers a tile, so the rotation follows a layer count that runs on
+//     across tiles).  Each group has one e buffer (32 columns: a row's 64
+//     squares); a head's e is stored once the group's previous gather has
+//     read the buffer.  The gathers run per position (K = 64, the other
+//     position's lanes disabled).
 //
 // Reference: networks/gat/gat.cu:836-870 (forward_gat_layer), 916-948
 // (compute_output: per-node 256 -> 73 policy for chess), 995-1038
@@ -44,10 +53,11 @@ constexpr int kP = 73;              // policy outputs per square
 constexpr int kPN = 80;             // policy MMA N (73 padded to a multiple of 16)
 constexpr int kA = kN * kP;         // 4672 actions
 constexpr int kEpiWarps = 8;
-constexpr int kThreads = (kEpiWarps + 3) * 32;
+constexpr int kThreads = (kEpiWarps + 4) * 32;
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;     // projection + policy MMAs + group 0's gathers
 constexpr int kGatherWarp = kEpiWarps + 2;  // group 1's gathers
+constexpr int kProjWarp = kEpiWarps + 3;    // projection, score and policy MMAs
 constexpr int kWRows = 256 + 32;            // projection rows + score rows
 constexpr int kWChunk = kWRows * 128;       // 36 KB: 288 rows x 64 K x 2 B
 constexpr int kWScoreOff = 256 * 128;
@@ -56,9 +66,21 @@ constexpr int kWSlots = 2;
 constexpr int kLayerChunks = 1 + (kLayers - 1) * 4;     // 29
 constexpr int kChunksPerTile = kLayerChunks + 4;        // + 4 policy chunks
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAlphaCol = 256;
-constexpr uint32_t kScoreCol = kAlphaCol + 64;          // aliases e buffer (0, 1) columns 0..31
-constexpr uint32_t kPolCol = kAlphaCol;                 // policy accumulator, after the last gathers
+// Tensor memory: three 128-column projection blocks (0-383), the two
+// groups' e buffers (384 + 32 g) and the scores (448).  Layer L (counted
+// across tiles) keeps heads 0, 4, 1, 5 (t = 0, 1 of both groups) in block
+// first_block(L) and heads 2, 6, 3, 7 in second_block(L); layer L + 1's
+// first half goes to the third block while layer L's heads run, its second
+// half to layer L's first-half block once heads t = 0, 1 are finished.  The
+// policy accumulator (80 columns) takes the block after the last layer's.
+constexpr uint32_t kECol = 384;
+constexpr uint32_t kScoreCol = 448;  // 16 high parts + 16 remainders
+__host__ __device__ constexpr int first_block(int L) { return (3 - L % 3) % 3; }
+__host__ __device__ constexpr int second_block(int L) { return (4 - L % 3) % 3; }
+// head 4g + t of layer L: block by t / 2, slot 2 (t % 2) + g inside it
+__host__ __device__ constexpr uint32_t head_col(int L, int g, int t) {
+  return (uint32_t)(128 * (t < 2 ? first_block(L) : second_block(L)) + 32 * (2 * (t & 1) + g));
+}
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -99,7 +121,8 @@ constexpr int kSmPool = kSmNbr + 64 * kMaxDeg;                    // [2 groups][
 constexpr int kSmZ = kSmPool + 2 * 4 * 32 * 4;          // [2 groups][2 halves][2 pos][64] value partial sums
 constexpr int kSmRed = kSmZ + 2 * 2 * kGPT * 64 * 4;    // [4 quarters][2] policy max / sum exchange
 constexpr int kSmBar = (kSmRed + 4 * 2 * 4 + 7) & ~7;
-constexpr int kNumBars = 2 * kWSlots + 1 + 1 + 4 + 4 + 2 + 1;  // full, empty, acc_full, x_ready, req, done2, drain[2], pol_full
+// full, empty, sc_full, acc_a, acc_b, x_ready[4], req[2][2], done2[2][2], drain[3], pol_full
+constexpr int kNumBars = 2 * kWSlots + 3 + 4 + 4 + 4 + 3 + 1;
 constexpr int kSmMisc = kSmBar + kNumBars * 8;
 constexpr int kSmemBytes = kSmMisc + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -203,23 +226,31 @@ __device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
   return v[0];  // each halving keeps the half selected by one lane bit: lane L ends with element L
 }
 
-// One group's four gathers of a layer (see gat_tc.cu): wait for head t's
-// request, issue its eight K = 16 steps, commit to done2.
-__device__ __forceinline__ bool serve_gathers(int g, uint32_t tmem, uint64_t b2desc0, uint64_t* req, uint64_t* done2,
-                                              uint32_t (&rph)[2], volatile int* abort_flag) {
+// One group's four gathers of layer L (see gat_tc.cu): wait for head t's
+// request, then per position four K = 16 steps over its 64 squares (A: the
+// group's e buffer, row i holding its position's e in half-column k; B:
+// Wh^h from the position's first node; the other position's lanes
+// disabled), commit to done2.
+__device__ __forceinline__ bool serve_gathers(int L, int g, uint32_t tmem, uint64_t b2desc0, uint64_t* req,
+                                              uint64_t* done2, uint32_t (&rph)[2], volatile int* abort_flag) {
   constexpr uint32_t idesc2 = idesc_f16(0 /* fp16 */, 128, 32, 1 /* B N-contiguous */);
+  constexpr uint32_t kMasks[kGPT][4] = {{0u, 0u, ~0u, ~0u}, {~0u, ~0u, 0u, 0u}};  // bit set = lane skipped
+  const uint32_t a_col = tmem + kECol + (uint32_t)(32 * g);
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
     const int b = t & 1, ab = 2 * g + b;
     if (!mbar_wait(&req[ab], rph[b] & 1, abort_flag, kWaitLimitNs)) return false;
     ++rph[b];
     tc_fence_after();
-    const uint32_t d = tmem + (uint32_t)(32 * (4 * g + t));
-    const uint32_t a_col = tmem + kAlphaCol + (uint32_t)(ab * 64);
+    const uint32_t d = tmem + head_col(L, g, t);
     const uint64_t bd = b2desc0 + (uint64_t)(ab * (8192 >> 4));
-    mma_f16_ts(d, a_col, bd, idesc2, 0);
 #pragma unroll
-    for (int kk = 1; kk < 8; ++kk) mma_f16_ts(d, a_col + kk * 8, bd + kk * (1024 >> 4), idesc2, 1);
+    for (int pg = 0; pg < kGPT; ++pg) {
+      const uint64_t bp = bd + (uint64_t)(pg * 8 * (512 >> 4));  // node 64 pg: 8 groups of 8 nodes, 512 B apart
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_ts_masked(d, a_col + kk * 8, bp + kk * (1024 >> 4), idesc2, kk != 0, kMasks[pg]);
+    }
     mma_commit(&done2[ab]);
   }
   return true;
@@ -262,12 +293,18 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
   uint64_t* bars = (uint64_t*)(smem + kSmBar);
   uint64_t* full = bars;
   uint64_t* empty = bars + kWSlots;
-  uint64_t* acc_full = bars + 2 * kWSlots;
-  uint64_t* x_ready = acc_full + 1;
-  uint64_t* req = acc_full + 2;     // [2 groups][2 buffers]
-  uint64_t* done2 = acc_full + 6;   // [2 groups][2 buffers]
-  uint64_t* drain = acc_full + 10;  // [issuing thread]
-  uint64_t* pol_full = acc_full + 12;
+  // sc_full: a layer's scores complete; acc_a / acc_b: its first / second
+  // projection half; x_ready[c]: K chunk c of the next X written (all eight
+  // epilogue warps); req / done2 per (group, B2 buffer): a head's gather
+  // request and its completion
+  uint64_t* sc_full = bars + 2 * kWSlots;
+  uint64_t* acc_a = sc_full + 1;
+  uint64_t* acc_b = sc_full + 2;
+  uint64_t* x_ready = sc_full + 3;  // [4 chunks]
+  uint64_t* req = sc_full + 7;      // [2 groups][2 buffers]
+  uint64_t* done2 = sc_full + 11;   // [2 groups][2 buffers]
+  uint64_t* drain = sc_full + 15;   // [issuing thread: gathers 0, gathers 1, projection]
+  uint64_t* pol_full = sc_full + 18;
   uint32_t* tmem_slot = (uint32_t*)(smem + kSmMisc);
   volatile int* abort_flag = (volatile int*)(smem + kSmMisc + 4);
   uint8_t* nbr = smem + kSmNbr;
@@ -292,14 +329,15 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(x_ready, kEpiWarps);
+    mbar_init(sc_full, 1);
+    mbar_init(acc_a, 1);
+    mbar_init(acc_b, 1);
     for (int i = 0; i < 4; ++i) {
+      mbar_init(&x_ready[i], kEpiWarps);
       mbar_init(&req[i], 4);
       mbar_init(&done2[i], 1);
     }
-    mbar_init(&drain[0], 1);
-    mbar_init(&drain[1], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&drain[i], 1);
     mbar_init(pol_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -334,65 +372,145 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
         mbar_wait(&full[k % kWSlots], (k / kWSlots) & 1, abort_flag, kWaitLimitNs);
     }
     __syncwarp();
-  } else if (warp == kMmaWarp) {
-    // ---------------- MMA issuer: projections, policy, group 0's gathers ----------------
+  } else if (warp == kMmaWarp || warp == kGatherWarp) {
+    // ---------------- gathers: one issuing thread per group ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc1 = idesc_f16(OpType<OpT>::fmt, 128, 256);
+      const int g = warp - kMmaWarp;
+      const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
+      uint32_t rph[2] = {0, 0};
+      bool ok = true;
+      int L = 0;  // layers counted across tiles: the projection blocks rotate with it
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x)
+        for (int l = 0; l < kLayers && ok; ++l, ++L) ok = serve_gathers(L, g, tmem, b2desc0, req, done2, rph, abort_flag);
+      mma_commit(&drain[g]);
+      mbar_wait(&drain[g], 0, abort_flag, kWaitLimitNs);
+    }
+    __syncwarp();
+  } else if (warp == kProjWarp) {
+    // ---------------- projection, score and policy MMAs ----------------
+    // Layer L + 1's projection is issued chunk by chunk under layer L's head
+    // loop, as the K chunks of X(L + 1) appear (the Connect4 kernel's order:
+    // gat_tc.cu).  Descriptors are advanced by adding (byte offset >> 4) to
+    // the start-address field.
+    if (lane == 0) {
+      constexpr uint32_t idescH = idesc_f16(OpType<OpT>::fmt, 128, 128);
       constexpr uint32_t idesc_s = idesc_f16(OpType<OpT>::fmt, 128, 32);
       constexpr uint32_t idesc_p = idesc_f16(OpType<OpT>::fmt, 128, kPN);
       const uint64_t xdesc = sw128_desc(smem_u32(sX));
       const uint64_t wdesc0 = sw128_desc(smem_u32(sW));
-      const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
-      uint32_t q = 0, xph = 0, rph[2] = {0, 0};
+      uint32_t q = 0, xph[4] = {0, 0, 0, 0};
       bool ok = true;
+      int L = 0;
+      auto wait_x = [&](int c) {
+        ok = ok && mbar_wait(&x_ready[c], xph[c] & 1, abort_flag, kWaitLimitNs);
+        ++xph[c];
+        tc_fence_after();
+      };
+      auto wait_w = [&](uint32_t k) {  // weight chunk k of the stream landed
+        ok = ok && mbar_wait(&full[k % kWSlots], (k / kWSlots) & 1, abort_flag, kWaitLimitNs);
+        tc_fence_after();
+      };
+      auto xd = [&](int c, int kk) { return xdesc + (uint64_t)(c * (16384 >> 4) + kk * 2); };
+      auto wd = [&](uint32_t k, int kk) { return wdesc0 + (uint64_t)((k % kWSlots) * (kWChunk >> 4) + kk * 2); };
+      // K = 16 step kk of X chunk c against weight chunk k: N = 128 into
+      // `dcol` from weight rows 128 * half .., or the 32 score columns
+      auto proj = [&](uint32_t dcol, int half, int c, uint32_t k, int kk, bool first) {
+        mma_f16_ss(tmem + dcol, xd(c, kk), wd(k, kk) + (uint64_t)(half * (16384 >> 4)), idescH, !first);
+      };
+      auto score = [&](int c, uint32_t k, int kk, bool first) {
+        mma_f16_ss(tmem + kScoreCol, xd(c, kk), wd(k, kk) + (uint64_t)(kWScoreOff >> 4), idesc_s, !first);
+      };
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        for (int l = 0; l <= kLayers && ok; ++l) {  // l == kLayers: the policy MMA
-          ok = mbar_wait(x_ready, xph & 1, abort_flag, kWaitLimitNs);
-          ++xph;
+        // layer 0: the encoded features (18 of K = 32: two K = 16 steps)
+        {
+          const uint32_t fa = 128 * first_block(L), fb = 128 * second_block(L);
+          wait_x(0);
+          wait_w(q);
           if (!ok) break;
-          tc_fence_after();
-          const bool pol = l == kLayers;
-          const int nchunk = l == 0 ? 1 : 4;
-          for (int c = 0; c < nchunk && ok; ++c, ++q) {
-            const int s = q % kWSlots;
-            ok = mbar_wait(&full[s], (q / kWSlots) & 1, abort_flag, kWaitLimitNs);
-            if (!ok) break;
-            tc_fence_after();
-            const uint64_t xd = xdesc + (uint64_t)(c * (16384 >> 4)), wd = wdesc0 + (uint64_t)(s * (kWChunk >> 4));
-            if (pol) {
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk) mma_f16_ss(tmem + kPolCol, xd + kk * 2, wd + kk * 2, idesc_p, (c | kk) != 0);
-            } else {
-              const int ksteps = l == 0 ? 2 : 4;  // layer 0: 18 features in K = 32
-              for (int kk = 0; kk < ksteps; ++kk) {
-                mma_f16_ss(tmem, xd + kk * 2, wd + kk * 2, idesc1, (c | kk) != 0);
-                mma_f16_ss(tmem + kScoreCol, xd + kk * 2, wd + (kWScoreOff >> 4) + kk * 2, idesc_s, (c | kk) != 0);
-              }
-            }
-            mma_commit(&empty[s]);
-          }
-          if (!ok) break;
-          if (pol) {
-            mma_commit(pol_full);
-          } else {
-            mma_commit(acc_full);
-            ok = serve_gathers(0, tmem, b2desc0, req, done2, rph, abort_flag);
-          }
+          for (int kk = 0; kk < 2; ++kk) score(0, q, kk, kk == 0);
+          mma_commit(sc_full);
+          for (int kk = 0; kk < 2; ++kk) proj(fa, 0, 0, q, kk, kk == 0);
+          mma_commit(acc_a);
+          for (int kk = 0; kk < 2; ++kk) proj(fb, 1, 0, q, kk, kk == 0);
+          mma_commit(acc_b);
+          mma_commit(&empty[q % kWSlots]);
+          ++q;
+          ++L;
         }
+        for (int l = 1; l < kLayers && ok; ++l, ++L) {
+          // layer L from X, weight chunks q .. q + 3
+          const uint32_t fa = 128 * first_block(L), fb = 128 * second_block(L);
+          // chunk 0: first half + scores (the third block is free)
+          wait_x(0);
+          wait_w(q);
+          if (!ok) break;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            proj(fa, 0, 0, q, kk, kk == 0);
+            score(0, q, kk, kk == 0);
+          }
+          // chunk 1: first half + scores; the second half of chunks 0 and 1
+          // (layer L - 1's first-half block is free: heads 0, 1, 4, 5 done)
+          wait_x(1);
+          wait_w(q + 1);
+          if (!ok) break;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            proj(fa, 0, 1, q + 1, kk, false);
+            score(1, q + 1, kk, false);
+          }
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fb, 1, 0, q, kk, kk == 0);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fb, 1, 1, q + 1, kk, false);
+          mma_commit(&empty[q % kWSlots]);
+          mma_commit(&empty[(q + 1) % kWSlots]);
+          // chunk 2: scores only; its halves wait until chunk 3's scores are
+          // issued, so nothing queues ahead of the scores the epilogue waits on
+          wait_x(2);
+          wait_w(q + 2);
+          if (!ok) break;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) score(2, q + 2, kk, false);
+          // chunk 3: scores first, then the first half of chunks 2 and 3, then
+          // the second, each committed on its own barrier
+          wait_x(3);
+          wait_w(q + 3);
+          if (!ok) break;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) score(3, q + 3, kk, false);
+          mma_commit(sc_full);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fa, 0, 2, q + 2, kk, false);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fa, 0, 3, q + 3, kk, false);
+          mma_commit(acc_a);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fb, 1, 2, q + 2, kk, false);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) proj(fb, 1, 3, q + 3, kk, false);
+          mma_commit(acc_b);
+          mma_commit(&empty[(q + 2) % kWSlots]);
+          mma_commit(&empty[(q + 3) % kWSlots]);
+          q += 4;
+        }
+        if (!ok) break;
+        // policy: X(8) chunk by chunk, N = 80 into the block after the last
+        // layer's (free: its last use was layer L - 2's second half)
+        const uint32_t pcol = 128 * first_block(L);
+        for (int c = 0; c < 4 && ok; ++c) {
+          wait_x(c);
+          wait_w(q + c);
+          if (!ok) break;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) mma_f16_ss(tmem + pcol, xd(c, kk), wd(q + c, kk), idesc_p, (c | kk) != 0);
+          mma_commit(&empty[(q + c) % kWSlots]);
+        }
+        mma_commit(pol_full);
+        q += 4;
       }
-      mma_commit(&drain[0]);
-      mbar_wait(&drain[0], 0, abort_flag, kWaitLimitNs);
-    }
-    __syncwarp();
-  } else if (warp == kGatherWarp) {
-    if (lane == 0) {
-      const uint64_t b2desc0 = noswizzle_desc(smem_u32(smem + kSmB2), 512, 128);
-      uint32_t rph[2] = {0, 0};
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x)
-        for (int l = 0; l < kLayers && ok; ++l) ok = serve_gathers(1, tmem, b2desc0, req, done2, rph, abort_flag);
-      mma_commit(&drain[1]);
-      mbar_wait(&drain[1], 0, abort_flag, kWaitLimitNs);
+      mma_commit(&drain[2]);
+      mbar_wait(&drain[2], 0, abort_flag, kWaitLimitNs);
     }
     __syncwarp();
   } else {
@@ -401,20 +519,13 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
     const int i = 32 * qd + lane;        // node row
     const int pg = i >> 6, sq = i & 63;  // position slot in the tile, square
     const uint32_t tlane = tmem + ((uint32_t)(32 * qd) << 16);
-    const int jw0 = 64 * pg;             // first node of this row's position: its e window
     uint8_t* srow = smem + kSmStage + (g * 128 + i) * kStageStride;
     const float* tsc = (const float*)(smem + kSmTsc) + (g * kGPT + pg) * 4 * 65;  // this row's position, head 0
     const uint8_t* my_nbr = nbr + sq * kMaxDeg;
     const int gbar = 3 + g;
     uint32_t aph = 0, pph = 0, dph[2] = {0, 0};
     bool ok = true, wok = true;
-
-    {
-      uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int b = 0; b < 2; ++b)
-        for (int c = 0; c < 64; c += 8) tmem_st_x8(tlane + kAlphaCol + (2 * g + b) * 64 + c, z);
-      tmem_st_wait();
-    }
+    int L = 0;  // layers counted across tiles (projection block rotation)
 
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       // -- encode the tile's positions into X chunk 0 (K = 0..31: 18 features, zeros) --
@@ -435,8 +546,9 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
         *(uint4*)(sX + sw128_offset(j, unit * 8)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
       }
       fence_proxy_async_smem();
+      tc_fence_before();  // the previous tile's policy reads precede this tile's layer-0 MMAs
       __syncwarp();
-      if (lane == 0) mbar_arrive(x_ready);
+      if (lane == 0) mbar_arrive(&x_ready[0]);
 
       const int gt = threadIdx.x & 127, vu = gt & 63, vhalf = gt >> 6;
       float* zacc = (float*)(smem + kSmZ) + (g * 2 + vhalf) * kGPT * 64 + vu;  // [pg * 64]
@@ -445,9 +557,9 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
         constexpr bool last = decltype(last_tag)::value;
         float* vec = (float*)(smem + kSmVec) + (l & 1) * kVecFloats;
         vec[threadIdx.x] = __ldg(p.w + ChOff::b(l) + threadIdx.x) * kLog2e;
-        wok = mbar_wait(acc_full, aph & 1, abort_flag, kWaitLimitNs) && wok;
+        const uint32_t lph = aph++ & 1;  // phase of this layer's sc_full / acc_a / acc_b
+        wok = mbar_wait(sc_full, lph, abort_flag, kWaitLimitNs) && wok;
         ok = epilogue_all(wok);
-        ++aph;
         if (!ok) return false;
         tc_fence_after();
 
@@ -464,23 +576,25 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
           for (int t = 0; t < 4; ++t) tw[t * 65] = hi[2 * t + 1] + lo[2 * t + 1];
         }
         tc_fence_before();
-        named_bar_sync(1, kEpiWarps * 32);
+        named_bar_sync(1, kEpiWarps * 32);  // t scores visible; score columns read by everyone
         tc_fence_after();
-        if (g == 0) {
-          uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-          for (int c = 0; c < 32; c += 8) tmem_st_x8(tlane + kScoreCol + c, z);
-          tmem_st_wait();
-        }
         float inv[4] = {0.f, 0.f, 0.f, 0.f};
 
-        auto finish_head = [&](int t) {
-          const int h = 4 * g + t, b = t & 1;
+        // head t's gather complete: its result may be read, and the group's
+        // e buffer rewritten
+        auto wait_gather = [&](int t) {
+          const int b = t & 1;
           wok = mbar_wait(&done2[2 * g + b], dph[b] & 1, abort_flag, kWaitLimitNs) && wok;
           ++dph[b];
           tc_fence_after();
+        };
+
+        // result of head t (after wait_gather(t)) -> / z, + bias, ELU -> K
+        // chunk t of the next X (heads t and t + 4)
+        auto finish_head = [&](int t) {
+          const int h = 4 * g + t;
           float o[32];
-          tmem_ld_x32(tlane + (uint32_t)(32 * h), o);
+          tmem_ld_x32(tlane + head_col(L, g, t), o);
           tmem_ld_wait();
           const float4* bias4 = (const float4*)(vec + 32 * h);
           const float2 iv = make_float2(inv[t], inv[t]);
@@ -496,10 +610,10 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
           {
             constexpr bool kSr = std::is_same<OpT, __nv_bfloat16>::value;
             const uint32_t seed = kSr ? round_seed(sq, l, h) : 0u;
-            uint8_t* xrow = sX + (h >> 1) * 16384 + (i >> 3) * 1024 + (i & 7) * 128;
+            uint8_t* xrow = sX + t * 16384 + (i >> 3) * 1024 + (i & 7) * 128;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-              const int unit = (4 * (h & 1) + u) ^ (i & 7);
+              const int unit = (4 * g + u) ^ (i & 7);
               uint32_t qv[4];
 #pragma unroll
               for (int m = 0; m < 4; ++m)
@@ -508,6 +622,10 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
               *(uint4*)(xrow + unit * 16) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
             }
           }
+          fence_proxy_async_smem();  // X writes -> the next projection's (or the policy MMA's) async proxy
+          tc_fence_before();         // this head's tensor-memory reads precede the block's reuse
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&x_ready[t]);
           if constexpr (last) {
             // value head: node sums of this head (fp32), per position
             float v32[32];
@@ -538,10 +656,17 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
 
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          const int h = 4 * g + t, b = t & 1;
+          const int b = t & 1;
           {  // P1: Wh^h (fp32) -> fp16 B operand of the gather
+            if (t == 0 || t == 2) {  // the block of heads t, t + 1 is complete
+              wok = mbar_wait(t == 0 ? acc_a : acc_b, lph, abort_flag, kWaitLimitNs) && wok;
+              // layer 0's MMAs all read X chunk 0, which head 0's result
+              // overwrites: the second half must be complete as well
+              if (t == 0 && l == 0) wok = mbar_wait(acc_b, lph, abort_flag, kWaitLimitNs) && wok;
+              tc_fence_after();
+            }
             float wh[32];
-            tmem_ld_x32(tlane + (uint32_t)(32 * h), wh);
+            tmem_ld_x32(tlane + head_col(L, g, t), wh);
             tmem_ld_wait();
             uint8_t* b2 = smem + kSmB2 + (2 * g + b) * 8192 + (i >> 3) * 512 + (i & 7) * 16;
 #pragma unroll
@@ -591,7 +716,9 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
               a[4 * k + 2] = v.z;
               a[4 * k + 3] = v.w;
             }
-            const uint32_t acol = tlane + kAlphaCol + (uint32_t)((2 * g + b) * 64 + (jw0 >> 1));
+            // the group's e buffer is free once its previous gather completed
+            if (t >= 1) wait_gather(t - 1);
+            const uint32_t acol = tlane + kECol + (uint32_t)(32 * g);
 #pragma unroll
             for (int k = 0; k < 4; ++k) tmem_st_x8(acol + 8 * k, *(const uint32_t(*)[8])(a + 8 * k));
             tmem_st_wait();
@@ -602,14 +729,11 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
           if (lane == 0) mbar_arrive(&req[2 * g + b]);
           if (t >= 1) finish_head(t - 1);
         }
+        wait_gather(3);
         finish_head(3);
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(x_ready);  // next layer's X (after the last: the policy MMA's A)
         return true;
       };
-      for (int l = 0; l < kLayers && ok; ++l) {
+      for (int l = 0; l < kLayers && ok; ++l, ++L) {
         const bool cont = l < kLayers - 1 ? layer(l, std::false_type{}) : layer(l, std::true_type{});
         if (!cont) break;
       }
@@ -626,10 +750,11 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
       if (g == 0) {
         // policy: this square's 73 logits, softmax over the position's 4672
         float lgt[kPN];
-        tmem_ld_x32(tlane + kPolCol, *(float(*)[32])(lgt));
-        tmem_ld_x32(tlane + kPolCol + 32, *(float(*)[32])(lgt + 32));
-        tmem_ld_x8(tlane + kPolCol + 64, *(float(*)[8])(lgt + 64));
-        tmem_ld_x8(tlane + kPolCol + 72, *(float(*)[8])(lgt + 72));
+        const uint32_t pcol = tlane + 128 * first_block(L);  // the block after the last layer's
+        tmem_ld_x32(pcol, *(float(*)[32])(lgt));
+        tmem_ld_x32(pcol + 32, *(float(*)[32])(lgt + 32));
+        tmem_ld_x8(pcol + 64, *(float(*)[8])(lgt + 64));
+        tmem_ld_x8(pcol + 72, *(float(*)[8])(lgt + 72));
         tmem_ld_wait();
         float mx = -INFINITY;
 #pragma unroll
@@ -656,13 +781,6 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
         float* out = stage + pg * kA + sq * kP;
 #pragma unroll
         for (int k = 0; k < kP; ++k) out[k] = lgt[k] * iz;
-        // the policy accumulator overlaid e buffers (0, 0) and (0, 1): restore
-        // their zero background (columns outside each lane's window are read
-        // by every gather)
-        uint32_t zz[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-        for (int c = 0; c < kPN; c += 8) tmem_st_x8(tlane + kPolCol + c, zz);
-        tmem_st_wait();
       } else if (warp - 4 < kGPT) {
         // value head of position (warp - 4): 64 hidden units, two per lane
         const int q2 = warp - 4, pos = tile * kGPT + q2;
@@ -707,6 +825,15 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
 // Chunks 0..28: per layer W_l^T (256 rows) + attention-score rows W_l a (16
 // high parts, 16 remainders), [288 rows][64 K] swizzled; layer 0 has K = 18.
 // Chunks 29..32: W_pi^T [80 rows (73 used)][64 K].
+// Input feature of K index kk of X chunk c after layer 0: chunk c holds heads
+// c (K 0-31) and c + 4 (K 32-63).
+__host__ __device__ constexpr int x_feature(int c, int kk) { return kk < 32 ? 32 * c + kk : 32 * (c + 4) + kk - 32; }
+// Output feature of projection row n: the first 128 rows are heads 0, 4, 1, 5
+// and the second 128 heads 2, 6, 3, 7 (head_col's order inside a block).
+__host__ __device__ constexpr int proj_feature(int n) {
+  return 32 * (4 * ((n >> 5) & 1) + 2 * (n >> 7) + ((n >> 6) & 1)) + (n & 31);
+}
+
 template <typename OpT>
 __global__ void pack_chess_kernel(const float* __restrict__ w, uint8_t* __restrict__ out) {
   const int chunk = blockIdx.x;
@@ -714,7 +841,7 @@ __global__ void pack_chess_kernel(const float* __restrict__ w, uint8_t* __restri
     const int c = chunk - kLayerChunks;
     uint8_t* dst = out + (size_t)kLayerChunks * kWChunk + (size_t)c * kPolChunk;
     for (int t = threadIdx.x; t < kPN * 64; t += blockDim.x) {
-      const int n = t / 64, kk = t % 64, k = c * 64 + kk;
+      const int n = t / 64, kk = t % 64, k = x_feature(c, kk);
       const float x = n < kP ? w[ChOff::w_pi + (size_t)k * kP + n] : 0.f;
       *(uint16_t*)(dst + sw128_offset(n, kk)) = OpType<OpT>::bits(x);
     }
@@ -727,12 +854,12 @@ __global__ void pack_chess_kernel(const float* __restrict__ w, uint8_t* __restri
   const float* A = w + ChOff::a(layer);
   uint8_t* dst = out + (size_t)chunk * kWChunk;
   for (int t = threadIdx.x; t < 256 * 64; t += blockDim.x) {
-    const int f = t / 64, kk = t % 64, k = c * 64 + kk;
-    const float x = k < fin ? W[(size_t)k * 256 + f] : 0.f;
-    *(uint16_t*)(dst + sw128_offset(f, kk)) = OpType<OpT>::bits(x);
+    const int n = t / 64, kk = t % 64, k = layer == 0 ? kk : x_feature(c, kk);
+    const float x = k < fin ? W[(size_t)k * 256 + proj_feature(n)] : 0.f;
+    *(uint16_t*)(dst + sw128_offset(n, kk)) = OpType<OpT>::bits(x);
   }
   for (int t = threadIdx.x; t < 16 * 64; t += blockDim.x) {
-    const int j = t / 64, kk = t % 64, k = c * 64 + kk, h = j >> 1, v = j & 1;
+    const int j = t / 64, kk = t % 64, k = layer == 0 ? kk : x_feature(c, kk), h = j >> 1, v = j & 1;
     float acc = 0.f;
     if (k < fin)
       for (int f = 0; f < 32; ++f) acc = fmaf(W[(size_t)k * 256 + 32 * h + f], A[(2 * h + v) * 32 + f], acc);
