@@ -459,12 +459,14 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
         wait_x(0);
         wait_w(q);
         if (!ok) break;
+        // the second half goes first: acc_a then covers both halves, and both
+        // have read X chunk 0 before head 0's result overwrites it
         score(0, q, 0, true);
         mma_commit(sc_full);
-        proj(128 * first_block(0), 0, 0, q, 0, true);
-        mma_commit(acc_a);
         proj(128 * second_block(0), 1, 0, q, 0, true);
         mma_commit(acc_b);
+        proj(128 * first_block(0), 0, 0, q, 0, true);
+        mma_commit(acc_a);
         mma_commit(&empty[q % kWSlots]);
         ++q;
         for (int l = 1; l < kLayers && ok; ++l) {

@@ -427,12 +427,14 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
           wait_x(0);
           wait_w(q);
           if (!ok) break;
+          // the second half goes first: acc_a then covers both halves, and
+          // both have read X chunk 0 before head 0's result overwrites it
           for (int kk = 0; kk < 2; ++kk) score(0, q, kk, kk == 0);
           mma_commit(sc_full);
-          for (int kk = 0; kk < 2; ++kk) proj(fa, 0, 0, q, kk, kk == 0);
-          mma_commit(acc_a);
           for (int kk = 0; kk < 2; ++kk) proj(fb, 1, 0, q, kk, kk == 0);
           mma_commit(acc_b);
+          for (int kk = 0; kk < 2; ++kk) proj(fa, 0, 0, q, kk, kk == 0);
+          mma_commit(acc_a);
           mma_commit(&empty[q % kWSlots]);
           ++q;
           ++L;
@@ -660,9 +662,6 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
           {  // P1: Wh^h (fp32) -> fp16 B operand of the gather
             if (t == 0 || t == 2) {  // the block of heads t, t + 1 is complete
               wok = mbar_wait(t == 0 ? acc_a : acc_b, lph, abort_flag, kWaitLimitNs) && wok;
-              // layer 0's MMAs all read X chunk 0, which head 0's result
-              // overwrites: the second half must be complete as well
-              if (t == 0 && l == 0) wok = mbar_wait(acc_b, lph, abort_flag, kWaitLimitNs) && wok;
               tc_fence_after();
             }
             float wh[32];
