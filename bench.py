@@ -341,7 +341,9 @@ def mcts_bench(net, device, game: int, trees: int, sims: int, leaves: int, moves
            "positions_per_s": trees * moves * world / el,
            "config": f"{trees} games/GPU x {sims} sims/move, leaf batch {trees * leaves}, c_puct 1.5, "
                      f"virtual loss 3, Dirichlet(1.0, 0.25), {moves} timed moves",
-           "gpu_launches_per_move": 3 * waves + 2}
+           # per move: a selection, per wave a network pass and a backup fused
+           # with the next wave's selection (the last backup alone), choose, play
+           "gpu_launches_per_move": 2 * waves + 3}
 
     # Whole games through the self-play driver: every tree starts from the
     # empty board and plays until `trees` games have ended; examples are the

@@ -1106,10 +1106,19 @@ gz_status gz_mcts_step(gz_mcts* m, gz_net* net, void* stream) {
 
 gz_status gz_mcts_run(gz_mcts* m, gz_net* net, int sims, void* stream) {
   if (!m || !net || sims < 0) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
-  int waves = (sims + m->d.leaves - 1) / m->d.leaves;
+  if (net->game != m->d.game) return fail(GZ_ERR_INVALID_ARG, "net and search play different games");
+  if (net->device != m->device) return fail(GZ_ERR_INVALID_ARG, "net and search live on different devices");
+  const int waves = (sims + m->d.leaves - 1) / m->d.leaves;
+  if (waves == 0) return GZ_OK;
+  GZ_DEVICE(m->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  // the gz_mcts_step sequence, with each backup and the next selections in one launch
+  GZ_CUDA(mcts_launch_select(m->d, s));
   for (int w = 0; w < waves; ++w) {
-    gz_status st = gz_mcts_step(m, net, stream);
+    gz_status st = run_forward(net, m->d.leaf_board, m->d.leaf_side, m->d.trees * m->d.leaves, m->d_pi, m->d_v, s);
     if (st != GZ_OK) return st;
+    if (w + 1 < waves) GZ_CUDA(mcts_launch_backup_select(m->d, m->d_pi, m->d_v, s));
+    else GZ_CUDA(mcts_launch_backup(m->d, m->d_pi, m->d_v, s));
   }
   return GZ_OK;
 }
@@ -1323,12 +1332,13 @@ gz_status gz_arena_play(gz_mcts* m, gz_net* net_a, gz_net* net_b, int n_games, i
     int live = n;
     for (int mv = 0; live > 0 && mv <= N && st == GZ_OK; ++mv) {
       cuda(mcts_launch_reset(d, boards, side, s), "reset");
+      if (waves > 0) cuda(mcts_launch_select(d, s), "select");
       for (int w = 0; w < waves && st == GZ_OK; ++w) {
-        cuda(mcts_launch_select(d, s), "select");
         if (st == GZ_OK) st = run_forward(net_a, d.leaf_board, d.leaf_side, (int)L, pi_a, v_a, s);
         if (st == GZ_OK) st = run_forward(net_b, d.leaf_board, d.leaf_side, (int)L, pi_b, v_b, s);
         cuda(arena_launch_merge((int)L, d.leaves, A, a_moves, pi_a, v_a, pi_b, v_b, m->d_pi, m->d_v, s), "merge");
-        cuda(mcts_launch_backup(d, m->d_pi, m->d_v, s), "backup");
+        if (w + 1 < waves) cuda(mcts_launch_backup_select(d, m->d_pi, m->d_v, s), "backup+select");
+        else cuda(mcts_launch_backup(d, m->d_pi, m->d_v, s), "backup");
       }
       cuda(mcts_launch_choose(d, 0, actions, s), "choose");
       cuda(cudaMemsetAsync(n_active, 0, 4, s), "memset");

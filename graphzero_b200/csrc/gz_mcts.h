@@ -80,6 +80,8 @@ enum MctsErr : int { kMctsOk = 0, kMctsNodeCap = 1, kMctsEdgeCap = 2, kMctsDepth
 cudaError_t mcts_launch_reset(const MctsDev& d, const int8_t* boards, const int8_t* side, cudaStream_t s);
 cudaError_t mcts_launch_select(const MctsDev& d, cudaStream_t s);
 cudaError_t mcts_launch_backup(const MctsDev& d, const float* pi, const float* v, cudaStream_t s);
+// backup of the current wave, then the next wave's selections (one launch)
+cudaError_t mcts_launch_backup_select(const MctsDev& d, const float* pi, const float* v, cudaStream_t s);
 cudaError_t mcts_launch_root_visits(const MctsDev& d, int32_t* visits, float* wsum, cudaStream_t s);
 cudaError_t mcts_launch_choose(const MctsDev& d, int temp_moves, int32_t* actions, cudaStream_t s);
 cudaError_t mcts_launch_play(const MctsDev& d, const int32_t* actions, int reserve, int8_t* done, cudaStream_t s);

@@ -161,10 +161,8 @@ __global__ void reset_kernel(MctsDev d, const int8_t* __restrict__ boards, const
   reset_tree(d.tree + t, boards + (size_t)t * d.N, d.N, side[t], 0);
 }
 
-__global__ void select_kernel(MctsDev d) {
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (t >= d.trees) return;
+// One wave's selections on tree t (all 32 lanes of a warp).
+__device__ __forceinline__ void select_tree(const MctsDev& d, int t, int lane) {
   MctsTree* tr = d.tree + t;
   MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
   const int N = d.N;
@@ -257,10 +255,9 @@ __global__ void select_kernel(MctsDev d) {
   }
 }
 
-__global__ void backup_kernel(MctsDev d, const float* __restrict__ pi, const float* __restrict__ value) {
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (t >= d.trees) return;
+// Expansion and backup of the wave's leaves of tree t (all 32 lanes of a warp).
+__device__ __forceinline__ void backup_tree(const MctsDev& d, const float* __restrict__ pi,
+                                            const float* __restrict__ value, int t, int lane) {
   MctsTree* tr = d.tree + t;
   MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
   int r_fe = tr->fe;
@@ -366,6 +363,27 @@ __global__ void backup_kernel(MctsDev d, const float* __restrict__ pi, const flo
     tr->vl = r_vl;
     tr->edge_count = edge_count;
   }
+}
+
+__global__ void select_kernel(MctsDev d) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t < d.trees) select_tree(d, t, threadIdx.x & 31);
+}
+
+__global__ void backup_kernel(MctsDev d, const float* __restrict__ pi, const float* __restrict__ value) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t < d.trees) backup_tree(d, pi, value, t, threadIdx.x & 31);
+}
+
+// A wave's backup followed by the next wave's selections in the same warp:
+// one launch instead of two between network passes (the warp's own writes
+// are visible to its lanes after the barrier).
+__global__ void backup_select_kernel(MctsDev d, const float* __restrict__ pi, const float* __restrict__ value) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t >= d.trees) return;
+  backup_tree(d, pi, value, t, threadIdx.x & 31);
+  __syncwarp();
+  select_tree(d, t, threadIdx.x & 31);
 }
 
 __global__ void root_visits_kernel(MctsDev d, int32_t* __restrict__ visits, float* __restrict__ wsum) {
@@ -486,6 +504,11 @@ cudaError_t mcts_launch_select(const MctsDev& d, cudaStream_t s) {
 
 cudaError_t mcts_launch_backup(const MctsDev& d, const float* pi, const float* v, cudaStream_t s) {
   backup_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
+  return cudaGetLastError();
+}
+
+cudaError_t mcts_launch_backup_select(const MctsDev& d, const float* pi, const float* v, cudaStream_t s) {
+  backup_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
   return cudaGetLastError();
 }
 
