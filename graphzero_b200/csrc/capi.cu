@@ -127,7 +127,7 @@ struct gz_net {
   // host calls: a copy stream beside `stream`, and per half of a split call
   // the events "inputs copied", "forward done", "outputs copied"
   cudaStream_t copy_stream = nullptr;
-  cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_fwd[2] = {nullptr, nullptr}, ev_out[2] = {nullptr, nullptr};
+  cudaEvent_t ev_in[4] = {}, ev_fwd[4] = {}, ev_out[4] = {};  // per piece of a host call
   gz::train::State* tr = nullptr;  // training state, created by the first training call
 };
 
@@ -378,7 +378,7 @@ gz_status gz_net_create(const gz_net_config* cfg, int device, gz_net** out) {
   chk(cudaMalloc(&n->d_out, out_floats * sizeof(float)), "cudaMalloc out");
   chk(cudaStreamCreateWithFlags(&n->stream, cudaStreamNonBlocking), "stream");
   chk(cudaStreamCreateWithFlags(&n->copy_stream, cudaStreamNonBlocking), "copy stream");
-  for (int h = 0; h < 2; ++h) {
+  for (int h = 0; h < 4; ++h) {
     chk(cudaEventCreateWithFlags(&n->ev_in[h], cudaEventDisableTiming), "event");
     chk(cudaEventCreateWithFlags(&n->ev_fwd[h], cudaEventDisableTiming), "event");
     chk(cudaEventCreateWithFlags(&n->ev_out[h], cudaEventDisableTiming), "event");
@@ -415,7 +415,7 @@ gz_status gz_net_destroy(gz_net* n) {
   cudaFree(n->d_out);
   if (n->stream) cudaStreamDestroy(n->stream);
   if (n->copy_stream) cudaStreamDestroy(n->copy_stream);
-  for (int h = 0; h < 2; ++h) {
+  for (int h = 0; h < 4; ++h) {
     if (n->ev_in[h]) cudaEventDestroy(n->ev_in[h]);
     if (n->ev_fwd[h]) cudaEventDestroy(n->ev_fwd[h]);
     if (n->ev_out[h]) cudaEventDestroy(n->ev_out[h]);
@@ -548,7 +548,8 @@ bool page_locked(const void* p) {
   }
   return a.type == cudaMemoryTypeHost;
 }
-constexpr int kSplitMin = 1024;  // host calls at least this large run as two overlapped halves
+constexpr int kSplitMin = 1024;  // chess host calls at least this large run as overlapped pieces
+constexpr int kPieces = 4;       // pieces of such a call (at most 4, the events per net)
 }  // namespace
 
 gz_status gz_net_predict_host(gz_net* n, const int8_t* boards, const int8_t* side, int count, float* pi, float* v) {
@@ -566,15 +567,23 @@ gz_status gz_net_predict_host(gz_net* n, const int8_t* boards, const int8_t* sid
   // the error word rides in the same stream as the outputs (no second round trip)
   int* h_err = (int*)(n->h_out + (size_t)n->max_batch * (s.actions + 1));
 
-  // A large call runs as two halves: inputs on the copy stream, forward
+  // A large chess call runs in pieces: inputs on the copy stream, forward
   // passes on the compute stream, outputs back on the copy stream once each
-  // half's forward pass is done, so that one half's transfers (and, for
-  // pageable caller buffers, host copies) overlap the other half's forward
-  // pass.  The split point is a multiple of 6, so every position keeps its
+  // piece's forward pass is done, so that one piece's transfers (and, for
+  // pageable caller buffers, host copies) overlap the next piece's forward
+  // pass.  The split points are multiples of 6, so every position keeps its
   // slot in the kernels' tiles (2 or 3 positions each) and the results are
-  // the unsplit call's bit for bit.
-  const int halves = count >= kSplitMin ? 2 : 1;
-  const int first[3] = {0, halves == 2 ? count / 2 / 6 * 6 : count, count};
+  // the unsplit call's bit for bit.  Measured on B200 from page-locked
+  // buffers, chess 8192 positions (153 MB of policy back to the host): 5.06
+  // ms per call unsplit, 3.90 in two pieces, 3.35 in four.  Connect4 runs
+  // unsplit: its outputs are small (GAT 4096: 381 µs per call unsplit, 383
+  // in two pieces), and the ResNet kernel runs its tiles in pairs per CTA,
+  // which a smaller launch leaves unpaired (1.03 ms unsplit, 1.24 in two).
+  static_assert(kPieces >= 1 && kPieces <= 4, "events per net");
+  const int halves = count >= kSplitMin && n->game == GZ_GAME_CHESS ? kPieces : 1;
+  int first[5];
+  for (int h = 0; h < halves; ++h) first[h] = count * h / halves / 6 * 6;
+  first[halves] = count;
   auto issue = [&](const int8_t* src_b, const int8_t* src_s, int h) -> gz_status {
     const size_t lo = first[h], m = first[h + 1] - first[h];
     GZ_CUDA(cudaMemcpyAsync(d_boards + lo * s.board_bytes, src_b + lo * s.board_bytes, m * s.board_bytes,

@@ -152,8 +152,9 @@ gz_status gz_net_check(gz_net* net);
 /* Same with host buffers: copies in, evaluates, copies out, synchronises.
  * n <= max_batch.  Page-locked caller buffers (cudaHostAlloc /
  * cudaHostRegister) are transferred directly, pageable ones through the
- * net's page-locked staging; n >= 1024 runs as two halves whose transfers
- * and host copies overlap the other half's forward pass (same results). */
+ * net's page-locked staging; a chess call of n >= 1024 runs as four pieces
+ * whose transfers and host copies overlap the next piece's forward pass
+ * (same results). */
 gz_status gz_net_predict_host(gz_net* net, const int8_t* h_boards, const int8_t* h_side, int n, float* h_pi,
                               float* h_v);
 /* INeuralNet::predict (neural_network.h:22): one position given as the
