@@ -692,17 +692,28 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
             }
             const float xm = s[t] + tmax;
             const float c = -fmaxf(xm, kLeakySlope * xm);  // scores are in base 2
+            // LeakyReLU(s + t_j) + c = max(t_j + (s + c), 0.2 t_j + (0.2 s + c)):
+            // an add, a fused multiply-add and a max per neighbour
+            const float sc = s[t] + c, s2c = fmaf(kLeakySlope, s[t], c);
             float z = 0.f;
             const uint32_t sbase = smem_u32(srow);
 #pragma unroll
-            for (int k = 0; k < kMaxDeg; ++k) {
-              const float x = s[t] + tj[k];
-              const __half e = __float2half_rn(ex2_approx(fmaxf(x, kLeakySlope * x) + c));
-              z += __half2float(e);  // absent neighbours: e = 0
+            for (int k = 0; k < kMaxDeg; k += 2) {
+              const float a0 = ex2_approx(fmaxf(tj[k] + sc, fmaf(tj[k], kLeakySlope, s2c)));
+              const float a1 = ex2_approx(fmaxf(tj[k + 1] + sc, fmaf(tj[k + 1], kLeakySlope, s2c)));
+              const __half2 e2 = __floats2half2_rn(a0, a1);  // one conversion for the pair
+              const float2 ef = __half22float2(e2);
+              z += ef.x;  // absent neighbours: e = 0
+              z += ef.y;
               // only real neighbours store (all absent ones would hit the same
               // bank group of their rows: up to 12 four-way conflicted stores)
               if (nbr_k(k) != 64u)
-                asm volatile("st.shared.b16 [%0], %1;" ::"r"(sbase + 2 * nbr_k(k)), "h"(__half_as_ushort(e)) : "memory");
+                asm volatile("st.shared.b16 [%0], %1;" ::"r"(sbase + 2 * nbr_k(k)), "h"(__half_as_ushort(__low2half(e2)))
+                             : "memory");
+              if (nbr_k(k + 1) != 64u)
+                asm volatile("st.shared.b16 [%0], %1;" ::"r"(sbase + 2 * nbr_k(k + 1)),
+                             "h"(__half_as_ushort(__high2half(e2)))
+                             : "memory");
             }
             // layer 0 reads the raw features: its Wh carries no log2(e) yet
             inv[t] = rcp_approx(z) * (l == 0 ? kLog2e : 1.f);
