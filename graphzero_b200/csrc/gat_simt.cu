@@ -276,7 +276,7 @@ cudaError_t launch_gat_simt(int game, const float* w, const int* csr, const int8
                             float* pi, float* v, cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
   switch (game) {
-    case kTicTacToe: return launch<kTicTacToe>(w, csr, boards, side, n, pi, v, stream);
+    case kTicTacToe: return launch_gat_simt_ttt(w, boards, side, n, pi, v, stream);
     case kConnect4: return launch<kConnect4>(w, csr, boards, side, n, pi, v, stream);
     case kChess: return launch<kChess>(w, csr, boards, side, n, pi, v, stream);
   }

@@ -37,6 +37,9 @@ gz_status nccl_broadcast_floats(void* comm, float* d_buf, size_t count, int root
 //   pi [n][A] fp32, v [n] fp32.
 cudaError_t launch_gat_simt(int game, const float* d_weights, const int* d_csr, const int8_t* d_boards,
                             const int8_t* d_side, int n, float* d_pi, float* d_v, cudaStream_t stream);
+// The same for TicTacToe, laid out for its 9-node stencil graph (gat_simt_ttt.cu).
+cudaError_t launch_gat_simt_ttt(const float* d_weights, const int8_t* d_boards, const int8_t* d_side, int n,
+                                float* d_pi, float* d_v, cudaStream_t stream);
 
 // Tensor-core (tcgen05) GAT forward for Connect4 and chess, bf16 or fp16 operands.
 // gat_tc_packed_bytes(game) is 0 when the game has no tensor-core kernel.
