@@ -548,6 +548,17 @@ bool page_locked(const void* p) {
   }
   return a.type == cudaMemoryTypeHost;
 }
+// The device-side address of page-locked host memory that is mapped into the
+// device's address space (cudaHostAlloc'd memory is, with unified
+// addressing), or null.
+void* mapped_address(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
 constexpr int kSplitMin = 1024;  // chess host calls at least this large run as overlapped pieces
 constexpr int kPieces = 4;       // pieces of such a call (at most 4, the events per net)
 }  // namespace
@@ -611,6 +622,26 @@ gz_status gz_net_predict_host(gz_net* n, const int8_t* boards, const int8_t* sid
     return GZ_OK;
   };
 
+  if (halves == 1) {
+    // Connect4 (small inputs and outputs) from mapped page-locked buffers:
+    // the forward kernel reads the boards and writes the results through the
+    // mapped addresses itself (one launch instead of five copies and a
+    // launch; the same bytes cross the bus)
+    void* mb = mapped_address(boards);
+    void* ms = mb ? mapped_address(side) : nullptr;
+    void* mp = ms ? mapped_address(pi) : nullptr;
+    void* mv = mp ? mapped_address(v) : nullptr;
+    if (mv) {
+      if (gz_status st = run_forward(n, (const int8_t*)mb, (const int8_t*)ms, count, (float*)mp, (float*)mv, n->stream);
+          st != GZ_OK) {
+        cudaStreamSynchronize(n->stream);
+        return st;
+      }
+      GZ_CUDA(cudaMemcpyAsync(h_err, n->d_err, sizeof(int), cudaMemcpyDeviceToHost, n->stream));
+      GZ_CUDA(cudaStreamSynchronize(n->stream));
+      return forward_error(n, *h_err);
+    }
+  }
   if (page_locked(boards) && page_locked(side) && page_locked(pi) && page_locked(v)) {
     // caller buffers are page-locked: the copy engines read and write them directly
     for (int h = 0; h < halves; ++h)

@@ -154,7 +154,9 @@ gz_status gz_net_check(gz_net* net);
  * cudaHostRegister) are transferred directly, pageable ones through the
  * net's page-locked staging; a chess call of n >= 1024 runs as four pieces
  * whose transfers and host copies overlap the next piece's forward pass
- * (same results). */
+ * (same results).  Other games read page-locked buffers that are mapped
+ * into the device's address space (cudaHostAlloc'd memory is) straight
+ * from the forward kernel, which also writes the outputs there. */
 gz_status gz_net_predict_host(gz_net* net, const int8_t* h_boards, const int8_t* h_side, int n, float* h_pi,
                               float* h_v);
 /* INeuralNet::predict (neural_network.h:22): one position given as the
