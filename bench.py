@@ -512,7 +512,9 @@ def ours(args, cfg: dict) -> None:
     e2e = {"value": B * e2e_steps * info.world / e2e_el, "unit": "leaf evals/s",
            "h2d_bytes_per_step": B * (s.board_bytes + 1), "d2h_bytes_per_step": B * (s.actions + 1) * 4,
            "steps": e2e_steps,
-           "call": "gz_net_predict_host (page-locked host buffers: H2D, forward, D2H, synchronise per step)"}
+           "call": ("gz_net_predict_host (page-locked host buffers, synchronise per step; Connect4: the forward "
+                    "kernel reads the boards and writes pi and v through the buffers' mapped addresses; chess: "
+                    "H2D, forward and D2H in four overlapped pieces)")}
 
     # ---- batched search throughput (secondary metric) ----
     mcts = None
