@@ -44,6 +44,21 @@ template <int G> struct SimtSmem {
   static constexpr size_t bytes = side + 16;
 };
 
+// Offsets (floats) into the fp32 weight blob (gat_layout order) as
+// compile-time arithmetic: a GatLayout indexed by the layer lives in local
+// memory.
+template <int G> struct SimtOff {
+  using T = Traits<G>;
+  static constexpr int kLayer0 = T::F * kHidden + kHidden + 2 * kHeads * kHeadDim;
+  static constexpr int kLayerN = kHidden * kHidden + kHidden + 2 * kHeads * kHeadDim;
+  __host__ __device__ static constexpr int W(int l) { return l == 0 ? 0 : kLayer0 + (l - 1) * kLayerN; }
+  __host__ __device__ static constexpr int b(int l) { return W(l) + (l == 0 ? T::F : kHidden) * kHidden; }
+  __host__ __device__ static constexpr int a(int l) { return b(l) + kHidden; }
+  static constexpr int w_pi = kLayer0 + (T::L - 1) * kLayerN, b_pi = w_pi + kHidden * T::P;
+  static constexpr int W_v1 = b_pi + T::P, b_v1 = W_v1 + kHidden * kValueHidden;
+  static constexpr int w_v2 = b_v1 + kValueHidden, b_v2 = w_v2 + kValueHidden;
+};
+
 __device__ __forceinline__ float lrelu(float x) { return x > 0.f ? x : kLeakySlope * x; }
 __device__ __forceinline__ float elu(float x) { return x > 0.f ? x : expm1f(x); }
 
@@ -66,7 +81,7 @@ __global__ void __launch_bounds__(kThreads) gat_simt_kernel(const float* __restr
   int* side = (int*)(smem + S::side);
   const int tid = threadIdx.x;
   const int g0 = blockIdx.x * GPC;
-  const GatLayout L = gat_layout(G);
+  using L = SimtOff<G>;
 
   for (int i = tid; i < N + 1 + NNZ; i += kThreads) rp[i] = csr_g[i];
   if (tid < GPC) side[tid] = g0 + tid < n ? (int)side_g[g0 + tid] : 1;
@@ -84,9 +99,9 @@ __global__ void __launch_bounds__(kThreads) gat_simt_kernel(const float* __restr
 
   int fin = T::F;
   for (int l = 0; l < T::L; ++l) {
-    const float* W = w + L.W[l];
-    const float* bias = w + L.b[l];
-    const float* a = w + L.a[l];
+    const float* W = w + L::W(l);
+    const float* bias = w + L::b(l);
+    const float* a = w + L::a(l);
     // Wh[:, c] = X W[:, c]
     {
       const int c = tid;
@@ -205,15 +220,15 @@ __global__ void __launch_bounds__(kThreads) gat_simt_kernel(const float* __restr
   __syncthreads();
   for (int t = tid; t < GPC * kValueHidden; t += kThreads) {
     int g = t / kValueHidden, u = t % kValueHidden;
-    float acc = __ldg(w + L.b_v1 + u);
-    for (int c = 0; c < kHidden; ++c) acc = fmaf(pooled[g * kHidden + c], __ldg(w + L.W_v1 + (size_t)c * kValueHidden + u), acc);
+    float acc = __ldg(w + L::b_v1 + u);
+    for (int c = 0; c < kHidden; ++c) acc = fmaf(pooled[g * kHidden + c], __ldg(w + L::W_v1 + (size_t)c * kValueHidden + u), acc);
     hid[t] = fmaxf(acc, 0.f);
   }
   // policy logits
   if (G == kTicTacToe) {
     for (int t = tid; t < GPC * N; t += kThreads) {
-      float acc = __ldg(w + L.b_pi);
-      for (int c = 0; c < kHidden; ++c) acc = fmaf(X[t * kHidden + c], __ldg(w + L.w_pi + c), acc);
+      float acc = __ldg(w + L::b_pi);
+      for (int c = 0; c < kHidden; ++c) acc = fmaf(X[t * kHidden + c], __ldg(w + L::w_pi + c), acc);
       logits[t] = acc;  // A == N
     }
   } else if (G == kConnect4) {
@@ -223,15 +238,15 @@ __global__ void __launch_bounds__(kThreads) gat_simt_kernel(const float* __restr
       for (int c = 0; c < kHidden; ++c) {
         float m = 0.f;
         for (int r = 0; r < 6; ++r) m += X[(g * N + r * 7 + cc) * kHidden + c];
-        acc = fmaf(m * (1.0f / 6.0f), __ldg(w + L.w_pi + c), acc);
+        acc = fmaf(m * (1.0f / 6.0f), __ldg(w + L::w_pi + c), acc);
       }
-      logits[t] = acc + __ldg(w + L.b_pi);
+      logits[t] = acc + __ldg(w + L::b_pi);
     }
   } else {
     for (int t = tid; t < GPC * T::A; t += kThreads) {
       int g = t / T::A, a = t % T::A, i = a / 73, k = a % 73;
-      float acc = __ldg(w + L.b_pi + k);
-      for (int c = 0; c < kHidden; ++c) acc = fmaf(X[(g * N + i) * kHidden + c], __ldg(w + L.w_pi + (size_t)c * 73 + k), acc);
+      float acc = __ldg(w + L::b_pi + k);
+      for (int c = 0; c < kHidden; ++c) acc = fmaf(X[(g * N + i) * kHidden + c], __ldg(w + L::w_pi + (size_t)c * 73 + k), acc);
       logits[t] = acc;
     }
   }
@@ -249,11 +264,11 @@ __global__ void __launch_bounds__(kThreads) gat_simt_kernel(const float* __restr
     for (int o = 16; o; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
     float inv = 1.f / z;
     float vv = 0.f;
-    for (int u = lane; u < kValueHidden; u += 32) vv = fmaf(hid[g * kValueHidden + u], __ldg(w + L.w_v2 + u), vv);
+    for (int u = lane; u < kValueHidden; u += 32) vv = fmaf(hid[g * kValueHidden + u], __ldg(w + L::w_v2 + u), vv);
     for (int o = 16; o; o >>= 1) vv += __shfl_xor_sync(0xffffffffu, vv, o);
     if (gi < n) {
       for (int a = lane; a < T::A; a += 32) pi[(size_t)gi * T::A + a] = expf(lg[a] - m) * inv;
-      if (lane == 0) v[gi] = tanhf(vv + __ldg(w + L.b_v2));
+      if (lane == 0) v[gi] = tanhf(vv + __ldg(w + L::b_v2));
     }
   }
 }
