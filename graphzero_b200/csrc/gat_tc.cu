@@ -809,13 +809,13 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
               }
               mean[pg * 256 + f] = tot * (kLn2 / kN);
             }
+            // the warp's 21 policy partials, summed over its lanes and
+            // scattered (lane k holds partial k)
+            float v32[32];
 #pragma unroll
-            for (int k = 0; k < kGPT * 7; ++k) {
-              float x = lp[k];
-#pragma unroll
-              for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-              if (lane == 0) lgw[warp * (kGPT * 7) + k] = x;
-            }
+            for (int k = 0; k < 32; ++k) v32[k] = k < kGPT * 7 ? lp[k < kGPT * 7 ? k : 0] : 0.f;
+            const float ps = reduce_scatter32(v32, lane);
+            if (lane < kGPT * 7) lgw[warp * (kGPT * 7) + lane] = ps;
           }
           named_bar_sync(1, kEpiWarps * 32);  // means and policy partials visible; X tile read
           // value head, first layer: warp w sums features 32 w .. 32 w + 31,

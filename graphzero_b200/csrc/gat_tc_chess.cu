@@ -209,23 +209,6 @@ __device__ __forceinline__ float2 elu2_log2e(float2 u) {
   return make_float2(fmaxf(m.x, u.x), fmaxf(m.y, u.y));
 }
 
-// Sum of v[0..31] over the 32 lanes, scattered: lane d returns the sum of
-// element d (recursive halving: 16 + 8 + 4 + 2 + 1 shuffles).
-__device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
-#pragma unroll
-  for (int w = 16; w >= 1; w >>= 1) {
-    const bool upper = (lane & w) != 0;
-#pragma unroll
-    for (int k = 0; k < w; ++k) {
-      // keep the half this lane owns, send the other half
-      const float send = upper ? v[k] : v[k + w];
-      const float keep = upper ? v[k + w] : v[k];
-      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, w);
-    }
-  }
-  return v[0];  // each halving keeps the half selected by one lane bit: lane L ends with element L
-}
-
 // One group's four gathers of layer L (see gat_tc.cu): wait for head t's
 // request, then per position four K = 16 steps over its 64 squares (A: the
 // group's e buffer, row i holding its position's e in half-column k; B:
