@@ -154,13 +154,17 @@ def test_host_call_matches_device_call(cuda):
         net.predict_host(np.zeros((301, 42), np.int8), np.ones(301, np.int8))
 
 
-@pytest.mark.parametrize("game,n", [(gz.CONNECT4, 4096), (gz.CONNECT4, 1023), (gz.CHESS, 1500)])
-def test_host_call_routes_agree(cuda, game, n):
-    """The three routes of the host call give the device call's results:
-    pageable buffers in one piece (n < 1024) or as two overlapped halves,
-    and page-locked buffers copied directly (outputs reused via out=)."""
-    net = gz.Net(game, max_batch=n)
-    net.load_weights(gz.synth_weights(game, seed=5))
+@pytest.mark.parametrize("game,kind,n", [(gz.CONNECT4, gz.GAT, 4096), (gz.CONNECT4, gz.GAT, 1023),
+                                         (gz.CONNECT4, gz.RESNET, 2000), (gz.TICTACTOE, gz.GAT, 300),
+                                         (gz.CHESS, gz.GAT, 1500)])
+def test_host_call_routes_agree(cuda, game, kind, n):
+    """The routes of the host call give the device call's results: pageable
+    buffers through the net's staging (chess from 1024 positions in four
+    overlapped pieces), page-locked buffers read and written by the forward
+    kernel through their mapped addresses (Connect4, TicTacToe) or copied
+    directly in pieces (chess); outputs reused via out=."""
+    net = gz.Net(game, kind, max_batch=n)
+    net.load_weights(gz.synth_weights(game, kind, seed=5))
     boards, side = gz.synth_positions(game, n, seed=6)
     p_dev, v_dev = run(net, boards, side)
     p1, v1 = net.predict_host(boards, side)
