@@ -758,10 +758,10 @@ extern "C" {
 namespace {
 
 gz_status ensure_train(gz_net* n, int batch) {
-  if (n->kind != GZ_NET_GAT) return fail(GZ_ERR_UNSUPPORTED, "training is built for the GAT nets");
   if (batch <= 0) return fail(GZ_ERR_INVALID_ARG, "batch of %d positions", batch);
   if (!n->tr) n->tr = new gz::train::State();
-  const cudaError_t e = gz::train::ensure_state(*n->tr, n->game, batch);
+  const cudaError_t e = n->kind == GZ_NET_RESNET ? gz::train::res_ensure_state(*n->tr, batch)
+                                                 : gz::train::ensure_state(*n->tr, n->game, batch);
   if (e != cudaSuccess)
     return fail(GZ_ERR_CUDA, "training buffers for %d positions: %s", batch, cudaGetErrorString(e));
   return GZ_OK;
@@ -792,12 +792,18 @@ gz_status train_batch(gz_net* n, const int8_t* boards, const int8_t* side, const
     if (e == cudaSuccess) e = cudaStreamWaitEvent(st.comm_stream, st.ev_bucket[k], 0);
     if (e != cudaSuccess) return e;
     size_t off = 0, count = 0;
-    gz::train::bucket_range(n->game, k, &off, &count);
+    if (n->kind == GZ_NET_RESNET)
+      gz::train::res_bucket_range(k, &off, &count);
+    else
+      gz::train::bucket_range(n->game, k, &off, &count);
     if (nr == ncclSuccess)
       nr = c->allReduce(st.grad + off, st.grad + off, count, ncclFloat32, ncclSum, (ncclComm_t)comm, st.comm_stream);
     return cudaSuccess;
   };
-  const cudaError_t e = gz::train::loss_and_grad(st, n->d_weights, boards, side, pi, v, cnt, s, bucket_done);
+  const cudaError_t e =
+      n->kind == GZ_NET_RESNET
+          ? gz::train::res_loss_and_grad(st, n->d_weights, boards, side, pi, v, cnt, s, bucket_done)
+          : gz::train::loss_and_grad(st, n->d_weights, boards, side, pi, v, cnt, s, bucket_done);
   if (e != cudaSuccess) return fail(GZ_ERR_CUDA, "training step: %s", cudaGetErrorString(e));
   if (nr != ncclSuccess) return fail(GZ_ERR_NCCL, "ncclAllReduce: %s", c->errorString ? c->errorString(nr) : "?");
   if (c) {
@@ -807,7 +813,8 @@ gz_status train_batch(gz_net* n, const int8_t* boards, const int8_t* side, const
   if (update) {
     const gz::train::AdamParams p{cfg->learning_rate, cfg->beta1, cfg->beta2, cfg->eps, cfg->weight_decay,
                                   c ? 1.f / (float)world : 1.f};
-    GZ_CUDA(gz::train::adam_step(st, n->d_weights, p, s));
+    GZ_CUDA(n->kind == GZ_NET_RESNET ? gz::train::res_adam_step(st, n->d_weights, p, s)
+                                     : gz::train::adam_step(st, n->d_weights, p, s));
     const gz_status ps = prepare_weights(n, s);
     if (ps != GZ_OK) return ps;
   }
@@ -899,7 +906,6 @@ gz_status gz_net_train(gz_net* n, const gz_train_example* ex, int64_t count, con
   if (world < 1 || rank < 0 || rank >= world) return fail(GZ_ERR_INVALID_ARG, "rank %d of %d", rank, world);
   if (n->game != kTicTacToe && n->game != kConnect4)
     return fail(GZ_ERR_UNSUPPORTED, "training examples hold TicTacToe or Connect4 boards");
-  if (n->kind != GZ_NET_GAT) return fail(GZ_ERR_UNSUPPORTED, "training is built for the GAT nets");
   GZ_DEVICE(n->device);
   const GameShape sh = game_shape(n->game);
   const int B = cfg->batch_size, A = sh.actions, N = sh.nodes;

@@ -1,6 +1,7 @@
-// GAT training step (train.cu): buffers, kernels' host launchers, and the
-// per-net training state (Adam moments, activations kept for the backward
-// pass).  Internal to the library; the C ABI is in graphzero_b200.h.
+// Training steps of the GAT (train.cu) and the Connect4 ResNet
+// (train_resnet.cu): buffers, kernels' host launchers, and the per-net
+// training state (Adam moments, activations kept for the backward pass).
+// Internal to the library; the C ABI is in graphzero_b200.h.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -19,6 +20,7 @@ struct Workspace {
 
 // Everything the training step of one net keeps on its device.
 struct State {
+  int kind = 0;                 // 0 = GAT, 1 = ResNet (the net kinds of graphzero_b200.h)
   int game = -1;
   int capacity = 0;             // positions the activation buffers hold
   size_t weight_count = 0;
@@ -32,7 +34,7 @@ struct State {
   float* arena = nullptr;       // activation and gradient buffers (see train.cu: layout())
   size_t arena_floats = 0;
   cudaStream_t comm_stream = nullptr;  // gradient all-reduce, beside the compute stream
-  cudaEvent_t ev_bucket[9] = {};       // per bucket: its gradients are complete
+  cudaEvent_t ev_bucket[16] = {};      // per bucket: its gradients are complete
   cudaEvent_t ev_comm = nullptr;       // all buckets reduced
 };
 
@@ -67,6 +69,17 @@ cudaError_t adam_step(State& st, float* w, const AdamParams& p, cudaStream_t s);
 // Offset and length (floats) of gradient bucket k of `game`'s weight layout.
 void bucket_range(int game, int k, size_t* offset, size_t* count);
 int bucket_count(int game);
+
+// The same for the Connect4 ResNet (res_layout weights).  Buckets: 0 the
+// heads, 1 .. 10 the residual blocks from the last down, 11 the stem; BN
+// means and variances are fixed (zero gradient, not updated by Adam).
+cudaError_t res_ensure_state(State& st, int capacity);
+cudaError_t res_loss_and_grad(State& st, const float* w, const int8_t* boards, const int8_t* side, const float* pi,
+                              const float* v, int B, cudaStream_t s,
+                              const std::function<cudaError_t(int)>& bucket_done);
+cudaError_t res_adam_step(State& st, float* w, const AdamParams& p, cudaStream_t s);
+void res_bucket_range(int k, size_t* offset, size_t* count);
+constexpr int kResBuckets = 12;
 
 }  // namespace train
 }  // namespace gz

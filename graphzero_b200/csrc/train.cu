@@ -561,7 +561,7 @@ void free_state(State& st) {
 cudaError_t ensure_state(State& st, int game, int capacity) {
   cudaError_t e = cudaSuccess;
   const GameShape sh = game_shape(game);
-  if (st.game != game) {
+  if (st.game != game || st.kind != 0) {
     free_state(st);
     st.game = game;
     st.weight_count = gat_layout(game).total;

@@ -280,14 +280,18 @@ gz_status gz_train_examples_save(const char* path, int n_iters, const gz_train_e
 gz_status gz_train_examples_load(const char* path, gz_train_example* out, int64_t capacity, int32_t* counts,
                                  int max_iters, int* n_iters, int64_t* total);
 
-/* ---- training (GAT nets) ---------------------------------------------------
+/* ---- training (GAT nets and the Connect4 ResNet) ---------------------------
  * Loss per position: -sum_a pi_a log p_a + (z - v)^2, averaged over the
  * batch (the reference's loss gradients, networks/gat/gat.cu:1040-1109:
- * softmax cross-entropy p - pi, value MSE 2 (v - z)).  fp32 forward and
- * backward on CUDA cores, every reduction in a fixed order (a step is
- * reproducible bit for bit), then Adam as torch::optim::Adam with weight
- * decay added to the gradient (gat.cu:71).  After every step the net's
- * tensor-core weights are repacked, so predictions use the new weights. */
+ * softmax cross-entropy p - pi, value MSE 2 (v - z); the ResNet's losses
+ * at networks/resnet/resnet.cu:669-699 are the same two terms).  fp32
+ * forward and backward on CUDA cores, every reduction in a fixed order (a
+ * step is reproducible bit for bit), then Adam as torch::optim::Adam with
+ * weight decay added to the gradient (gat.cu:71).  The ResNet trains with
+ * its BN in inference form, as gz_net_predict evaluates it: BN scales and
+ * shifts are trained, the stored means and variances get a zero gradient
+ * and are not updated.  After every step the net's tensor-core weights are
+ * repacked, so predictions use the new weights. */
 typedef struct {
   float learning_rate; /* 1e-3 (gat.cu:712) */
   float weight_decay;  /* 1e-4 (gat.cu:713) */
@@ -308,8 +312,8 @@ void gz_train_config_default(gz_train_config* cfg);
  * side [n], target policies pi [n][actions], target values v [n].  The
  * gradient (gz_net_weight_count floats, the weight blob's layout) goes to
  * d_grad when it is not NULL, the two loss terms to h_loss (policy, value)
- * when it is not NULL.  GAT nets of every game; GZ_ERR_UNSUPPORTED for the
- * ResNet.  Synchronises. */
+ * when it is not NULL.  GAT nets of every game and the Connect4 ResNet.
+ * Synchronises. */
 gz_status gz_net_loss_grad(gz_net* net, const int8_t* d_boards, const int8_t* d_side, const float* d_pi,
                            const float* d_v, int n, float* d_grad, float h_loss[2], void* stream);
 /* One optimizer step on one batch (device buffers as above).  With a
@@ -340,7 +344,8 @@ gz_status gz_train_batch_indices(int64_t n, const gz_train_config* cfg, int epoc
  * k == layers: the policy and value heads), as an offset and a length in
  * floats of the weight layout; gz_net_train_step all-reduces the buckets
  * from the heads down to layer 0, each as soon as the backward pass has
- * produced it.  Host only. */
+ * produced it.  (The ResNet's 12 buckets, in the order they complete: the
+ * heads, blocks 9 down to 0, the stem.)  Host only. */
 gz_status gz_train_bucket_range(int game, int k, size_t* offset, size_t* count);
 
 /* ---- allocation-free leaf evaluation --------------------------------------

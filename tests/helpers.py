@@ -200,3 +200,56 @@ def torch_gat_loss(game: int, w: np.ndarray, boards: np.ndarray, side: np.ndarra
     lv = ((torch.tensor(v, dtype=dtype) - val) ** 2).mean()
     (lp + lv).backward()
     return float(lp.detach()), float(lv.detach()), flat.grad.numpy()
+
+
+def resnet_frozen_mask() -> np.ndarray:
+    """True at the ResNet's BN means and variances (fixed statistics)."""
+    o = res_blob_views()
+    mask = np.zeros(gz.weight_count(gz.CONNECT4, gz.RESNET), bool)
+    for k, (p, sh) in o.items():
+        if k.endswith("bn") or k.startswith("bn"):
+            c = sh[1]
+            mask[p + 2 * c:p + 4 * c] = True
+    return mask
+
+
+def torch_resnet_loss(w: np.ndarray, boards: np.ndarray, side: np.ndarray, pi: np.ndarray, v: np.ndarray,
+                      dtype=torch.float64) -> tuple[float, float, np.ndarray]:
+    """Training loss of the Connect4 ResNet (BN in inference form with its
+    stored statistics held fixed) and its gradient with respect to the flat
+    weight blob, by torch autograd on an independent restatement."""
+    o = res_blob_views()
+    flat = torch.tensor(w.astype(np.float64), dtype=dtype, requires_grad=True)
+    frozen = torch.tensor(resnet_frozen_mask())
+    src = torch.where(frozen, flat.detach(), flat)
+
+    def t(k):
+        p, sh = o[k]
+        return src[p:p + int(np.prod(sh))].view(sh)
+
+    b = torch.tensor(boards.astype(np.int64)).view(-1, 6, 7)
+    sd = torch.tensor(side.astype(np.int64)).view(-1, 1, 1)
+    x = torch.stack([(b == sd), (b == -sd), (sd == 1).expand_as(b)], 1).to(dtype)
+
+    def conv(x, k):
+        return torch.nn.functional.conv2d(x, t(k).permute(0, 3, 1, 2), padding=1)
+
+    def bn(x, k):
+        g, be, mu, var = t(k)
+        sh = (1, -1, 1, 1)
+        return (x - mu.view(sh)) / torch.sqrt(var.view(sh) + 1e-5) * g.view(sh) + be.view(sh)
+
+    a = torch.relu(bn(conv(x, "stem_w"), "stem_bn"))
+    for k in range(10):
+        h = torch.relu(bn(conv(a, f"c1_{k}"), f"bn1_{k}"))
+        a = torch.relu(bn(conv(h, f"c2_{k}"), f"bn2_{k}") + a)
+    pf = bn(torch.einsum("oc,bchw->bohw", t("pol_w"), a), "pol_bn").reshape(-1, 84)
+    lg = pf @ t("pol_fc") + t("pol_fc_b")
+    vf = bn(torch.einsum("oc,bchw->bohw", t("val_w"), a), "val_bn").reshape(-1, 42)
+    hv = torch.relu(vf @ t("val_fc1") + t("val_fc1_b"))
+    val = torch.tanh(hv @ t("val_fc2") + t("val_fc2_b"))
+    tp = torch.tensor(pi, dtype=dtype)
+    lp = -(tp * torch.log_softmax(lg, -1)).sum(-1).mean()
+    lv = ((torch.tensor(v, dtype=dtype) - val) ** 2).mean()
+    (lp + lv).backward()
+    return float(lp.detach()), float(lv.detach()), flat.grad.numpy()

@@ -163,7 +163,13 @@ def _free_port():
     return p
 
 
-def _dp_worker(rank, world, port, out):
+def _dp_weights(G, kind):
+    if kind == G.RESNET:
+        return G.synth_weights(G.CONNECT4, G.RESNET, seed=70, bias_scale=0.3)
+    return sharpen(G.CONNECT4, G.synth_weights(G.CONNECT4, seed=70, bias_scale=0.3))
+
+
+def _dp_worker(rank, world, port, out, kind):
     sys.path[:0] = [str(ROOT), str(ROOT / "oracle"), str(ROOT / "tests")]
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
                       MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -176,8 +182,8 @@ def _dp_worker(rank, world, port, out):
     info = D.rank_info()
     D.init_process_group("gloo", info, timeout_s=60.0)
     game, n = G.CONNECT4, 16
-    net = G.Net(game, device=rank, max_batch=n)
-    net.load_weights(sharpen(game, G.synth_weights(game, seed=70, bias_scale=0.3)))
+    net = G.Net(game, kind, device=rank, max_batch=n)
+    net.load_weights(_dp_weights(G, kind))
     uid = D.share_bytes(G.nccl_unique_id() if rank == 0 else None)
     comm = G.nccl_comm_init(uid, world, rank, rank)
     b, s, pi, v = batch(game, n * world, seed=71)
@@ -194,7 +200,8 @@ def _dp_worker(rank, world, port, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_data_parallel_step_matches_one_gpu(cuda):
+@pytest.mark.parametrize("kind", [gz.GAT, gz.RESNET])
+def test_data_parallel_step_matches_one_gpu(cuda, kind):
     """Two ranks on two GPUs, each with half of the batch, gradients
     all-reduced bucket by bucket over NCCL and averaged: both end with the
     same weights as one GPU stepping on the whole batch."""
@@ -204,7 +211,7 @@ def test_data_parallel_step_matches_one_gpu(cuda):
     mgr = ctx.Manager()
     out = mgr.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_dp_worker, args=(r, 2, port, out)) for r in range(2)]
+    procs = [ctx.Process(target=_dp_worker, args=(r, 2, port, out, kind)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -214,8 +221,8 @@ def test_data_parallel_step_matches_one_gpu(cuda):
             pytest.fail("rank did not finish")
     assert [p.exitcode for p in procs] == [0, 0]
     game, n = gz.CONNECT4, 16
-    net = gz.Net(game, max_batch=2 * n)
-    net.load_weights(sharpen(game, gz.synth_weights(game, seed=70, bias_scale=0.3)))
+    net = gz.Net(game, kind, max_batch=2 * n)
+    net.load_weights(_dp_weights(gz, kind))
     d = dev(*batch(game, 2 * n, seed=71))
     cfg = gz.train_config(learning_rate=1e-3)
     for _ in range(2):
