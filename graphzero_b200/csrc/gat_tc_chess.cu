@@ -84,40 +84,31 @@ __host__ __device__ constexpr uint32_t head_col(int L, int g, int t) {
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
-constexpr int kMaxDeg = 36;                             // queen lines (27 max) + knights (8) + self
+// Rows whose neighbour maximum lies more than this many (base-2) score units
+// below the maximum of a half board take the direct exponentials: the
+// product form's factors would leave the fp32 range.
+constexpr float kMaxFactorGap = 64.f;
 
-// chess graph degree of a square (queen lines + knight + self), host/device
-__host__ __device__ constexpr int chess_degree(int s) {
-  int d = 0;
-  for (int j = 0; j < 64; ++j) {
-    const int dr = (j >> 3) - (s >> 3), dc = (j & 7) - (s & 7);
-    const int ar = dr < 0 ? -dr : dr, ac = dc < 0 ? -dc : dc;
-    if (j == s || dr == 0 || dc == 0 || ar == ac || (ar == 1 && ac == 2) || (ar == 2 && ac == 1)) ++d;
-  }
-  return d;
-}
-__host__ __device__ constexpr int chess_max_degree() {
-  int m = 0;
-  for (int s = 0; s < 64; ++s) m = chess_degree(s) > m ? chess_degree(s) : m;
-  return m;
-}
-static_assert(chess_max_degree() <= kMaxDeg, "neighbour table width");
-static_assert(kMaxDeg % 4 == 0, "neighbour rows are read as words");
+// Knight move k of 8 as (row, column) steps.
+__host__ __device__ constexpr int knight_dr(int k) { return k < 4 ? (k == 0 || k == 3 ? 1 : 2) : (k == 4 || k == 7 ? -1 : -2); }
+__host__ __device__ constexpr int knight_dc(int k) { return (k == 0 || k == 7) ? 2 : (k == 1 || k == 6) ? 1 : (k == 2 || k == 5) ? -1 : -2; }
 
 // Shared memory map (bytes).
-constexpr int kStageStride = 144;                       // 32 used words + pad (conflict-free 16 B reads)
 constexpr int kSmX = 0;                                 // X tile 64 KB; after the policy MMA: pi staging
 constexpr int kSmW = kSmX + 4 * 16384;
 constexpr int kSmB2 = kSmW + kWSlots * kWChunk;
-constexpr int kSmStage = kSmB2 + 4 * 8192;
-constexpr int kSmTsc = kSmStage + 2 * 128 * kStageStride;
-// t scores: [group][position][head][64 squares + pad], head-major so that a
-// head's loads of 32 lanes' neighbours are single words (random squares spread
-// over the 32 banks instead of 16-byte groups of 8)
-constexpr int kSmVec = kSmTsc + 2 * 130 * 16;
+// board graph adjacency as 0/1 factors: row s, 16-byte unit u (squares
+// 4u .. 4u + 3) at unit u ^ (s & 15), so that 8 consecutive squares' reads
+// of one unit fall in 8 different bank groups
+constexpr int kSmMask = kSmB2 + 4 * 8192;
+constexpr int kSmT = kSmMask + 64 * 64 * 4;                  // t scores [group][position][head][64]
+constexpr int kSmBD = kSmT + 2 * kGPT * 4 * 64 * 4;          // [group][position][head][B: 64 | D: 64]
+constexpr int kSmLines = kSmBD + 2 * kGPT * 4 * 128 * 4;     // diagonal maxima [group][position][head][2][16]
+constexpr int kSmCol = kSmLines + 2 * kGPT * 4 * 2 * 16 * 4; // column maxima of a warp's 4 rows [group][quarter][head][8]
+constexpr int kSmRef = kSmCol + 2 * 4 * 4 * 8 * 4;          // maxima of a warp's 32 squares [group][quarter][head]
+constexpr int kSmVec = kSmRef + 2 * 4 * 4 * 4;
 constexpr int kVecFloats = 256;
-constexpr int kSmNbr = kSmVec + 2 * kVecFloats * 4;     // [64 squares][kMaxDeg] neighbour squares, 64 = none (pad)
-constexpr int kSmPool = kSmNbr + 64 * kMaxDeg;                    // [2 groups][4 quarters][32] node sums of one head
+constexpr int kSmPool = kSmVec + 2 * kVecFloats * 4;    // [2 groups][4 quarters][32] node sums of one head
 constexpr int kSmZ = kSmPool + 2 * 4 * 32 * 4;          // [2 groups][2 halves][2 pos][64] value partial sums
 constexpr int kSmRed = kSmZ + 2 * 2 * kGPT * 64 * 4;    // [4 quarters][2] policy max / sum exchange
 constexpr int kSmBar = (kSmRed + 4 * 2 * 4 + 7) & ~7;
@@ -290,22 +281,14 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
   uint64_t* pol_full = sc_full + 18;
   uint32_t* tmem_slot = (uint32_t*)(smem + kSmMisc);
   volatile int* abort_flag = (volatile int*)(smem + kSmMisc + 4);
-  uint8_t* nbr = smem + kSmNbr;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  for (int i = threadIdx.x; i < 2 * 128 * kStageStride / 4; i += blockDim.x) ((uint32_t*)(smem + kSmStage))[i] = 0u;
-  // the pad row (square 64) of every (group, position) t-score table is -inf:
-  // absent neighbours point at it and get weight 0
-  if (threadIdx.x < 16)  // (group, position, head) = threadIdx.x
-    ((float*)(smem + kSmTsc))[threadIdx.x * 65 + 64] = -INFINITY;
-  if (threadIdx.x < 64) {  // neighbour table of square s (the chess board graph, build_graph_csr order)
-    const int s = threadIdx.x;
-    int d = 0;
-    for (int j = 0; j < 64; ++j)
-      if (graph_adjacent(kChess, 8, 8, s, j)) nbr[s * kMaxDeg + d++] = (uint8_t)j;
-    for (int k = d; k < kMaxDeg; ++k) nbr[s * kMaxDeg + k] = 64;  // the pad square
+  for (int k = threadIdx.x; k < 64 * 64; k += blockDim.x) {
+    const int s = k >> 6, j = k & 63;
+    ((float*)(smem + kSmMask))[s * 64 + (((j >> 2) ^ (s & 15)) << 2) + (j & 3)] =
+        graph_adjacent(kChess, 8, 8, s, j) ? 1.f : 0.f;
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kWSlots; ++s) {
@@ -504,9 +487,19 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
     const int i = 32 * qd + lane;        // node row
     const int pg = i >> 6, sq = i & 63;  // position slot in the tile, square
     const uint32_t tlane = tmem + ((uint32_t)(32 * qd) << 16);
-    uint8_t* srow = smem + kSmStage + (g * 128 + i) * kStageStride;
-    const float* tsc = (const float*)(smem + kSmTsc) + (g * kGPT + pg) * 4 * 65;  // this row's position, head 0
-    const uint8_t* my_nbr = nbr + sq * kMaxDeg;
+    const int br = sq >> 3, bc = sq & 7;  // board row and column
+    // this row's position: t scores, B / D factors and diagonal maxima (head 0)
+    float* sT = (float*)(smem + kSmT) + (g * kGPT + pg) * 4 * 64;
+    float* sBD = (float*)(smem + kSmBD) + (g * kGPT + pg) * 4 * 128;
+    const float* sLn = (const float*)(smem + kSmLines) + (g * kGPT + pg) * 4 * 32;
+    float* sCol = (float*)(smem + kSmCol) + g * 4 * 4 * 8;
+    float* sRef = (float*)(smem + kSmRef) + g * 4 * 4;
+    const float* mrow = (const float*)(smem + kSmMask) + sq * 64;
+    // knight moves that stay on the board (bit k)
+    uint32_t kvalid = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      kvalid |= ((unsigned)(br + knight_dr(k)) < 8u && (unsigned)(bc + knight_dc(k)) < 8u ? 1u : 0u) << k;
     const int gbar = 3 + g;
     uint32_t aph = 0, pph = 0, dph[2] = {0, 0};
     bool ok = true, wok = true;
@@ -548,21 +541,83 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
         if (!ok) return false;
         tc_fence_after();
 
-        float s[4];
+        // ---- scores: s (this row attending), t (this square as a neighbour) ----
+        // e_ij = 2^(LeakyReLU(s_i + t_j) + c_i) over the neighbours j of i,
+        // with c_i = -LeakyReLU(s_i + max_j t_j) (LeakyReLU is monotonic).
+        // With r_h the maximum of t over half board h (one warp's 32 squares),
+        // per square B_j = 2^(t_j - r_h), D_j = 2^(0.2 (t_j - r_h)) and per
+        // row A_i = 2^(s_i + r_h + c_i), C_i = 2^(0.2 (s_i + r_h) + c_i):
+        // e_ij = max(A_i B_j, C_i D_j) -- two exponentials per square and
+        // head, four per row, instead of one per edge.  The neighbours'
+        // maximum is that of the square's row, column, diagonal, anti-diagonal
+        // (the queen lines of the graph) and knight squares.
+        float s[4], cs[4];
+        uint32_t fb = 0;  // bit t: this row takes head t's direct exponentials
         {
           float hi[8], lo[8];
           tmem_ld_x8(tlane + kScoreCol + 8 * g, hi);
           tmem_ld_x8(tlane + kScoreCol + 16 + 8 * g, lo);
           tmem_ld_wait();
+          float rmax[4], cmax[4];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) s[t] = hi[2 * t] + lo[2 * t];
-          float* tw = (float*)(smem + kSmTsc) + (g * kGPT + pg) * 4 * 65 + sq;
+          for (int t = 0; t < 4; ++t) {
+            s[t] = hi[2 * t] + lo[2 * t];
+            const float tv = hi[2 * t + 1] + lo[2 * t + 1];
+            sT[t * 64 + sq] = tv;
+            // board row (8 lanes), the column over the warp's 4 rows, the warp
+            float m = fmaxf(tv, __shfl_xor_sync(~0u, tv, 1));
+            m = fmaxf(m, __shfl_xor_sync(~0u, m, 2));
+            m = fmaxf(m, __shfl_xor_sync(~0u, m, 4));
+            rmax[t] = m;
+            float cm = fmaxf(tv, __shfl_xor_sync(~0u, tv, 8));
+            cm = fmaxf(cm, __shfl_xor_sync(~0u, cm, 16));
+            cmax[t] = cm;
+            float wm = fmaxf(m, __shfl_xor_sync(~0u, m, 8));
+            wm = fmaxf(wm, __shfl_xor_sync(~0u, wm, 16));
+            if (lane < 8) sCol[(qd * 4 + t) * 8 + lane] = cm;
+            if (lane == 0) sRef[qd * 4 + t] = wm;
+            const float d = tv - wm;
+            sBD[t * 128 + sq] = ex2_approx(d);
+            sBD[t * 128 + 64 + sq] = ex2_approx(kLeakySlope * d);
+          }
+          tc_fence_before();
+          named_bar_sync(1, kEpiWarps * 32);  // tables written; score columns read by everyone
+          tc_fence_after();
+          // the other half board's part of the column, and the knight squares
+          float nmax[4];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) tw[t * 65] = hi[2 * t + 1] + lo[2 * t + 1];
+          for (int t = 0; t < 4; ++t) {
+            float m = fmaxf(fmaxf(rmax[t], cmax[t]), sCol[((qd ^ 1) * 4 + t) * 8 + bc]);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int j = (kvalid >> k) & 1u ? sq + 8 * knight_dr(k) + knight_dc(k) : sq;
+              m = fmaxf(m, sT[t * 64 + j]);
+            }
+            nmax[t] = m;
+          }
+          // diagonal and anti-diagonal maxima of the group's two positions
+          // and four heads: 240 lines over the group's 128 threads
+          for (int task = threadIdx.x & 127; task < kGPT * 4 * 30; task += 128) {
+            const int tp = task / 120, rem = task % 120, t = rem / 30, kind = (rem % 30) / 15, d = rem % 15;
+            const float* tt = (const float*)(smem + kSmT) + ((g * kGPT + tp) * 4 + t) * 64;
+            float m = -INFINITY;
+#pragma unroll
+            for (int rr = 0; rr < 8; ++rr) {
+              const int cc = kind == 0 ? rr + 7 - d : d - rr;  // r - c = d - 7, or r + c = d
+              if ((unsigned)cc < 8u) m = fmaxf(m, tt[rr * 8 + cc]);
+            }
+            ((float*)(smem + kSmLines))[((g * kGPT + tp) * 4 + t) * 32 + kind * 16 + d] = m;
+          }
+          named_bar_sync(gbar, 128);
+          const int qlo = qd & ~1;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float m = fmaxf(nmax[t], fmaxf(sLn[t * 32 + br - bc + 7], sLn[t * 32 + 16 + br + bc]));
+            const float x = s[t] + m;
+            cs[t] = -fmaxf(x, kLeakySlope * x);
+            if (fmaxf(sRef[qlo * 4 + t], sRef[(qlo + 1) * 4 + t]) - m > kMaxFactorGap) fb |= 1u << t;
+          }
         }
-        tc_fence_before();
-        named_bar_sync(1, kEpiWarps * 32);  // t scores visible; score columns read by everyone
-        tc_fence_after();
         float inv[4] = {0.f, 0.f, 0.f, 0.f};
 
         // head t's gather complete: its result may be read, and the group's
@@ -657,63 +712,56 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
                   make_uint4(OpType<__half>::pack(wh[8 * ng + 0], wh[8 * ng + 1]), OpType<__half>::pack(wh[8 * ng + 2], wh[8 * ng + 3]),
                              OpType<__half>::pack(wh[8 * ng + 4], wh[8 * ng + 5]), OpType<__half>::pack(wh[8 * ng + 6], wh[8 * ng + 7]));
           }
-          {  // P2: softmax numerators over the square's neighbours -> e row (fp16)
-            // LeakyReLU is monotonic: the largest logit is lrelu(s + max_j t_j).
-            // The square's neighbour list (36 bytes) is read as nine words
-            // into registers once per head: the stores below clobber memory,
-            // so byte loads would be repeated in the second loop.
-            uint32_t nb4[kMaxDeg / 4];
+          {  // P2: softmax numerators over the position's 64 squares -> e row (fp16)
+            const float st = s[t], ct = cs[t];
+            uint32_t e2[32];
+            float2 z2 = make_float2(0.f, 0.f);
+            // squares 4q .. 4q + 3 -> e row words 2q, 2q + 1; z sums the fp32 values
+            auto put = [&](int q, float2 e01, float2 e23) {
+              z2 = __fadd2_rn(z2, __fadd2_rn(e01, e23));
+              e2[2 * q] = OpType<__half>::pack(e01.x, e01.y);
+              e2[2 * q + 1] = OpType<__half>::pack(e23.x, e23.y);
+            };
+            if (__any_sync(~0u, (fb >> t) & 1u)) {
+              // one exponential per square, off-graph squares at -inf
+              const float* tt = sT + t * 64;
 #pragma unroll
-            for (int w = 0; w < kMaxDeg / 4; ++w) nb4[w] = ((const uint32_t*)my_nbr)[w];
-            auto nbr_k = [&](int k) { return (nb4[k >> 2] >> (8 * (k & 3))) & 0xffu; };
-            float tj[kMaxDeg];
-            float tmax = -INFINITY;
+              for (int q = 0; q < 16; ++q) {
+                const float4 tq = *(const float4*)(tt + 4 * q);
+                const float4 mq = *(const float4*)(mrow + ((q ^ (sq & 15)) << 2));
+                float a[4] = {st + tq.x, st + tq.y, st + tq.z, st + tq.w};
+                const float mk[4] = {mq.x, mq.y, mq.z, mq.w};
 #pragma unroll
-            for (int k = 0; k < kMaxDeg; ++k) {
-              tj[k] = tsc[t * 65 + nbr_k(k)];  // absent neighbours: the pad entry, -inf
-              tmax = fmaxf(tmax, tj[k]);
-            }
-            const float xm = s[t] + tmax;
-            const float c = -fmaxf(xm, kLeakySlope * xm);  // scores are in base 2
-            // LeakyReLU(s + t_j) + c = max(t_j + (s + c), 0.2 t_j + (0.2 s + c)):
-            // an add, a fused multiply-add and a max per neighbour
-            const float sc = s[t] + c, s2c = fmaf(kLeakySlope, s[t], c);
-            float z = 0.f;
-            const uint32_t sbase = smem_u32(srow);
+                for (int k = 0; k < 4; ++k) a[k] = ex2_approx(mk[k] > 0.f ? fmaxf(a[k], kLeakySlope * a[k]) + ct : -INFINITY);
+                put(q, make_float2(a[0], a[1]), make_float2(a[2], a[3]));
+              }
+            } else {
+              const int qlo = qd & ~1;
+              const float h0 = st + sRef[qlo * 4 + t], h1 = st + sRef[(qlo + 1) * 4 + t];
+              const float2 A0 = make_float2(ex2_approx(h0 + ct), ex2_approx(h0 + ct));
+              const float2 C0 = make_float2(ex2_approx(fmaf(kLeakySlope, h0, ct)), ex2_approx(fmaf(kLeakySlope, h0, ct)));
+              const float2 A1 = make_float2(ex2_approx(h1 + ct), ex2_approx(h1 + ct));
+              const float2 C1 = make_float2(ex2_approx(fmaf(kLeakySlope, h1, ct)), ex2_approx(fmaf(kLeakySlope, h1, ct)));
+              const float* bd = sBD + t * 128;
 #pragma unroll
-            for (int k = 0; k < kMaxDeg; k += 2) {
-              const float a0 = ex2_approx(fmaxf(tj[k] + sc, fmaf(tj[k], kLeakySlope, s2c)));
-              const float a1 = ex2_approx(fmaxf(tj[k + 1] + sc, fmaf(tj[k + 1], kLeakySlope, s2c)));
-              const __half2 e2 = __floats2half2_rn(a0, a1);  // one conversion for the pair
-              const float2 ef = __half22float2(e2);
-              z += ef.x;  // absent neighbours: e = 0
-              z += ef.y;
-              // only real neighbours store (all absent ones would hit the same
-              // bank group of their rows: up to 12 four-way conflicted stores)
-              if (nbr_k(k) != 64u)
-                asm volatile("st.shared.b16 [%0], %1;" ::"r"(sbase + 2 * nbr_k(k)), "h"(__half_as_ushort(__low2half(e2)))
-                             : "memory");
-              if (nbr_k(k + 1) != 64u)
-                asm volatile("st.shared.b16 [%0], %1;" ::"r"(sbase + 2 * nbr_k(k + 1)),
-                             "h"(__half_as_ushort(__high2half(e2)))
-                             : "memory");
+              for (int q = 0; q < 16; ++q) {
+                const float2 A = q < 8 ? A0 : A1, C = q < 8 ? C0 : C1;
+                const float4 bq = *(const float4*)(bd + 4 * q), dq = *(const float4*)(bd + 64 + 4 * q);
+                const float4 mq = *(const float4*)(mrow + ((q ^ (sq & 15)) << 2));
+                const float2 ab01 = __fmul2_rn(A, make_float2(bq.x, bq.y)), ab23 = __fmul2_rn(A, make_float2(bq.z, bq.w));
+                const float2 cd01 = __fmul2_rn(C, make_float2(dq.x, dq.y)), cd23 = __fmul2_rn(C, make_float2(dq.z, dq.w));
+                const float2 e01 = __fmul2_rn(make_float2(fmaxf(ab01.x, cd01.x), fmaxf(ab01.y, cd01.y)), make_float2(mq.x, mq.y));
+                const float2 e23 = __fmul2_rn(make_float2(fmaxf(ab23.x, cd23.x), fmaxf(ab23.y, cd23.y)), make_float2(mq.z, mq.w));
+                put(q, e01, e23);
+              }
             }
             // layer 0 reads the raw features: its Wh carries no log2(e) yet
-            inv[t] = rcp_approx(z) * (l == 0 ? kLog2e : 1.f);
-            uint32_t a[32];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint4 v = *(const uint4*)(srow + 16 * k);
-              a[4 * k] = v.x;
-              a[4 * k + 1] = v.y;
-              a[4 * k + 2] = v.z;
-              a[4 * k + 3] = v.w;
-            }
+            inv[t] = rcp_approx(z2.x + z2.y) * (l == 0 ? kLog2e : 1.f);
             // the group's e buffer is free once its previous gather completed
             if (t >= 1) wait_gather(t - 1);
             const uint32_t acol = tlane + kECol + (uint32_t)(32 * g);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) tmem_st_x8(acol + 8 * k, *(const uint32_t(*)[8])(a + 8 * k));
+            for (int k = 0; k < 4; ++k) tmem_st_x8(acol + 8 * k, *(const uint32_t(*)[8])(e2 + 8 * k));
             tmem_st_wait();
           }
           fence_proxy_async_smem();
