@@ -32,6 +32,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include <type_traits>
 
@@ -86,7 +87,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 // Rows whose neighbour maximum lies more than this many (base-2) score units
 // below the maximum of a half board take the direct exponentials: the
-// product form's factors would leave the fp32 range.
+// product form's factors would leave the fp32 range.  The environment
+// variable GZ_CHESS_FACTOR_GAP overrides it at launch (a negative value
+// sends every row through the direct path; both paths compute the same
+// numerators).
 constexpr float kMaxFactorGap = 64.f;
 
 // Knight move k of 8 as (row, column) steps.
@@ -253,6 +257,7 @@ struct TcParams {
   int* err;
   int n;
   int num_tiles;
+  float max_gap;  // kMaxFactorGap or its override
 };
 
 template <typename OpT>
@@ -615,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_chess_kernel(TcParams p) {
             const float m = fmaxf(nmax[t], fmaxf(sLn[t * 32 + br - bc + 7], sLn[t * 32 + 16 + br + bc]));
             const float x = s[t] + m;
             cs[t] = -fmaxf(x, kLeakySlope * x);
-            if (fmaxf(sRef[qlo * 4 + t], sRef[(qlo + 1) * 4 + t]) - m > kMaxFactorGap) fb |= 1u << t;
+            if (fmaxf(sRef[qlo * 4 + t], sRef[(qlo + 1) * 4 + t]) - m > p.max_gap) fb |= 1u << t;
           }
         }
         float inv[4] = {0.f, 0.f, 0.f, 0.f};
@@ -935,6 +940,9 @@ cudaError_t launch_chess_tc(int fp16, const void* d_packed, const float* d_weigh
   p.err = d_err;
   p.n = n;
   p.num_tiles = (n + kGPT - 1) / kGPT;
+  const char* gap = getenv("GZ_CHESS_FACTOR_GAP");
+  p.max_gap = gap && *gap ? (float)atof(gap) : kMaxFactorGap;
+  if (!(p.max_gap <= kMaxFactorGap)) p.max_gap = kMaxFactorGap;  // larger gaps would leave the fp32 range
   auto kern = fp16 ? gat_tc_chess_kernel<__half> : gat_tc_chess_kernel<__nv_bfloat16>;
   static int cached_grid[64][2];
   int dev = 0;

@@ -244,6 +244,30 @@ def test_chess_tensor_core_matches_oracle(cuda, prec, sharp, tol):
     net.check()
 
 
+def test_chess_direct_softmax_path(cuda, monkeypatch):
+    """The chess kernel's direct numerators (one exponential per square,
+    taken by rows whose score spread would push the factor products out of
+    the fp32 range), forced for every row: against the oracle, and against
+    the factor path (the same numerators up to fp32 rounding)."""
+    game = gz.CHESS
+    w = sharpen(game, gz.synth_weights(game, seed=23, bias_scale=0.4))
+    net = gz.Net(game, max_batch=128)
+    net.load_weights(w)
+    boards, side = inputs(game, 65, seed=365)
+    pi_f, v_f = run(net, boards, side)
+    monkeypatch.setenv("GZ_CHESS_FACTOR_GAP", "-1")
+    pi_d, v_d = run(net, boards, side)
+    opi, ov = oracle.gat_forward(game, w, boards, side)
+    assert np.isfinite(pi_d).all() and np.isfinite(v_d).all()
+    assert np.abs(pi_d - opi).max() < SPEC_TOL and np.abs(v_d - ov).max() < SPEC_TOL
+    # numerators equal up to fp32 rounding can still round to neighbouring
+    # fp16 values; eight layers and the sharpened policy turn that into
+    # about 1.2e-4 (measured on B200), the same size as each path's distance
+    # from the oracle
+    assert np.abs(pi_d - pi_f).max() < 5e-4 and np.abs(v_d - v_f).max() < 5e-4
+    net.check()
+
+
 def test_chess_tensor_core_full_batch(cuda):
     """The c3 shape: 8192 legal positions in one launch; determinism, batch
     invariance, and a sample of rows against the oracle."""
