@@ -169,6 +169,19 @@ def _dp_weights(G, kind):
     return sharpen(G.CONNECT4, G.synth_weights(G.CONNECT4, seed=70, bias_scale=0.3))
 
 
+def _dp_config(G, kind):
+    # The ResNet has many weights whose gradient is a sum that cancels to
+    # almost nothing; Adam's first steps move each weight by about lr
+    # whatever its gradient's size, so a different summation order (two half
+    # batches against one whole batch) can move such a weight by a different
+    # fraction of lr.  With eps = 1 the update is lr * m, proportional to the
+    # averaged gradient, and the comparison checks the all-reduce and the
+    # averaging themselves.
+    if kind == G.RESNET:
+        return G.train_config(learning_rate=1e-3, eps=1.0)
+    return G.train_config(learning_rate=1e-3)
+
+
 def _dp_worker(rank, world, port, out, kind):
     sys.path[:0] = [str(ROOT), str(ROOT / "oracle"), str(ROOT / "tests")]
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
@@ -189,7 +202,7 @@ def _dp_worker(rank, world, port, out, kind):
     b, s, pi, v = batch(game, n * world, seed=71)
     sl = slice(rank * n, (rank + 1) * n)
     d = [T.from_numpy(np.ascontiguousarray(a[sl])).cuda(rank) for a in (b, s, pi, v)]
-    cfg = G.train_config(learning_rate=1e-3)
+    cfg = _dp_config(G, kind)
     for _ in range(2):
         net.train_step(*d, n, cfg, comm=comm, world=world)
     out[rank] = net.save_weights()
@@ -224,11 +237,17 @@ def test_data_parallel_step_matches_one_gpu(cuda, kind):
     net = gz.Net(game, kind, max_batch=2 * n)
     net.load_weights(_dp_weights(gz, kind))
     d = dev(*batch(game, 2 * n, seed=71))
-    cfg = gz.train_config(learning_rate=1e-3)
+    cfg = _dp_config(gz, kind)
+    w0 = net.save_weights()
     for _ in range(2):
         net.train_step(*d, 2 * n, cfg)
     w = net.save_weights()
     assert np.array_equal(out[0], out[1])
+    if kind == gz.RESNET:
+        upd, upd_dp = w - w0, out[0] - w0
+        assert np.abs(upd).max() > 0
+        assert np.abs(upd_dp - upd).max() <= 1e-3 * np.abs(upd).max(), (np.abs(upd_dp - upd).max(), np.abs(upd).max())
+        return
     # the averaged gradient differs from the whole-batch one in the last bits
     # of its sums; Adam divides by sqrt(v), so an entry with a near-zero
     # gradient can move by a different fraction of the learning rate:
