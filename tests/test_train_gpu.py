@@ -125,15 +125,16 @@ def test_training_reduces_the_loss_and_predictions_follow(cuda, game):
     net.check()
 
 
-def test_ineuralnet_train_through_the_shim(cuda):
+@pytest.mark.parametrize("kind", ["gat", "resnet"])
+def test_ineuralnet_train_through_the_shim(cuda, kind):
     """INeuralNet::train from the reference's vtable (TrainingExample with
-    float board and policy arrays)."""
+    float board and policy arrays), for both factories' nets."""
     import ctypes as C
 
     game = gz.CONNECT4
-    nn = gz.create_ineuralnet("gat", gz.create_igame("connect4"))
+    nn = gz.create_ineuralnet(kind, gz.create_igame("connect4"))
     net_h = gz._lib.gz_shim_net(nn)
-    w0 = np.empty(gz.weight_count(game), np.float32)
+    w0 = np.empty(gz.weight_count(game, gz.RESNET if kind == "resnet" else gz.GAT), np.float32)
     gz._check(gz._lib.gz_net_save_weights(net_h, gz._ptr(w0, C.c_float), w0.size))
     ex = teacher_examples(game, 128, seed=60)
 
@@ -153,6 +154,10 @@ def test_ineuralnet_train_through_the_shim(cuda):
     w1 = np.empty_like(w0)
     gz._check(gz._lib.gz_net_save_weights(net_h, gz._ptr(w1, C.c_float), w1.size))
     assert np.isfinite(w1).all() and not np.array_equal(w0, w1)
+    if kind == "resnet":  # BN statistics stay fixed
+        from helpers import resnet_frozen_mask
+        frozen = resnet_frozen_mask()
+        assert np.array_equal(w1[frozen], w0[frozen])
 
 
 def _free_port():
