@@ -114,15 +114,32 @@ __global__ void gemm_reduce_kernel(int M, int N, int splits, const float* __rest
   *c = accumulate ? *c + s : s;
 }
 
+// Streaming multiprocessors of the current device (queried once per device).
+static int device_sms() {
+  static int sms[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (sms[dev] == 0 && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    sms[dev] = 148;
+  }
+  return sms[dev];
+}
+
 cudaError_t gemm(Workspace& ws, int M, int N, int K, const float* A, int lda, bool ta, const float* B, int ldb,
                  bool tb, float* C, int ldc, bool accumulate, cudaStream_t s) {
   if (M <= 0 || N <= 0) return cudaSuccess;
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-  // split K when the output has few tiles and K is long (dW = X^T dWh)
+  // Split K when the output has fewer tiles than about two waves of CTAs
+  // (four of these CTAs fit on an SM) and K is long (the weight gradients
+  // dW = X^T dY, whose K is the batch's rows): at least 128 K per split.
+  // The split depends on the shape only, and the partials are summed in
+  // split order, so a step is reproducible.
   int splits = 1;
-  if (tiles < 256 && K > 4096) {
-    splits = (512 + tiles - 1) / tiles;
-    const int max_splits = (K + 2047) / 2048;
+  const int target = 8 * device_sms();
+  if (tiles < target && K >= 512) {
+    splits = (target + tiles - 1) / tiles;
+    const int max_splits = K / 128;
     splits = splits > max_splits ? max_splits : splits;
     if ((size_t)splits * M * N > ws.split_floats) splits = (int)(ws.split_floats / ((size_t)M * N));
     if (splits < 1) splits = 1;
