@@ -104,6 +104,87 @@ __global__ void __launch_bounds__(256) gemm_kernel(int M, int N, int K, const fl
     }
 }
 
+// The same product for large outputs: a 128 x 128 tile per CTA of 256
+// threads, 8 x 8 outputs per thread (rows 4 ty .. 4 ty + 3 and 64 + 4 ty ..,
+// columns likewise with tx), K in steps of 8 through two shared-memory
+// buffers (the next step's operands are loaded into registers while the
+// current one is multiplied; one barrier per step).  Each output still sums
+// its products in ascending k, one fused multiply-add at a time.
+constexpr int kBM2 = 128, kBN2 = 128, kBK2 = 8, kPad2 = 4;
+
+__global__ void __launch_bounds__(256) gemm128_kernel(int M, int N, int K, const float* __restrict__ A, int lda,
+                                                      int ta, const float* __restrict__ B, int ldb, int tb, float* C,
+                                                      int ldc, int accumulate, int k_chunk, float* part) {
+  __shared__ __align__(16) float As[2][kBK2][kBM2 + kPad2];
+  __shared__ __align__(16) float Bs[2][kBK2][kBN2 + kPad2];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * kBM2, n0 = blockIdx.x * kBN2;
+  const int k_lo = blockIdx.z * k_chunk, k_hi = min(K, k_lo + k_chunk);
+  float ra[4], rb[4];
+  // element r of this thread's share of the A (B) tile at K step k0: (m, k)
+  // with consecutive threads along A's (B's) contiguous dimension
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int e = threadIdx.x + 256 * r;
+      int m, k;
+      if (ta) { m = e % kBM2; k = e / kBM2; } else { k = e % kBK2; m = e / kBK2; }
+      const int gm = m0 + m, gk = k0 + k;
+      ra[r] = (gm < M && gk < k_hi) ? (ta ? A[(size_t)gk * lda + gm] : A[(size_t)gm * lda + gk]) : 0.f;
+      int n, kb;
+      if (tb) { kb = e % kBK2; n = e / kBK2; } else { n = e % kBN2; kb = e / kBN2; }
+      const int gn = n0 + n, gkb = k0 + kb;
+      rb[r] = (gn < N && gkb < k_hi) ? (tb ? B[(size_t)gn * ldb + gkb] : B[(size_t)gkb * ldb + gn]) : 0.f;
+    }
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int e = threadIdx.x + 256 * r;
+      if (ta) As[buf][e / kBM2][e % kBM2] = ra[r]; else As[buf][e % kBK2][e / kBK2] = ra[r];
+      if (tb) Bs[buf][e % kBK2][e / kBK2] = rb[r]; else Bs[buf][e / kBN2][e % kBN2] = rb[r];
+    }
+  };
+  float acc[8][8] = {};
+  int buf = 0;
+  if (k_lo < k_hi) {
+    load(k_lo);
+    store(0);
+  }
+  __syncthreads();
+  for (int k0 = k_lo; k0 < k_hi; k0 += kBK2) {
+    const bool more = k0 + kBK2 < k_hi;
+    if (more) load(k0 + kBK2);
+#pragma unroll
+    for (int k = 0; k < kBK2; ++k) {
+      const float4 a0 = *(const float4*)&As[buf][k][4 * ty], a1 = *(const float4*)&As[buf][k][64 + 4 * ty];
+      const float4 b0 = *(const float4*)&Bs[buf][k][4 * tx], b1 = *(const float4*)&Bs[buf][k][64 + 4 * tx];
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    if (more) store(buf ^ 1);
+    __syncthreads();
+    buf ^= 1;
+  }
+  float* out = part ? part + (size_t)blockIdx.z * M * N : C;
+  const int ld = part ? N : ldc;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int gm = m0 + (i < 4 ? 4 * ty + i : 64 + 4 * ty + i - 4);
+      const int gn = n0 + (j < 4 ? 4 * tx + j : 64 + 4 * tx + j - 4);
+      if (gm < M && gn < N) {
+        float* c = out + (size_t)gm * ld + gn;
+        *c = (!part && accumulate) ? *c + acc[i][j] : acc[i][j];
+      }
+    }
+}
+
 __global__ void gemm_reduce_kernel(int M, int N, int splits, const float* __restrict__ part, float* C, int ldc,
                                    int accumulate) {
   const size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -129,14 +210,17 @@ static int device_sms() {
 cudaError_t gemm(Workspace& ws, int M, int N, int K, const float* A, int lda, bool ta, const float* B, int ldb,
                  bool tb, float* C, int ldc, bool accumulate, cudaStream_t s) {
   if (M <= 0 || N <= 0) return cudaSuccess;
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  // large outputs take the 128 x 128 tile kernel
+  const bool big = M >= kBM2 && N >= kBN2;
+  const int bm = big ? kBM2 : kBM, bn = big ? kBN2 : kBN, bk = big ? kBK2 : kBK;
+  const int tiles = ((M + bm - 1) / bm) * ((N + bn - 1) / bn);
   // Split K when the output has fewer tiles than about two waves of CTAs
-  // (four of these CTAs fit on an SM) and K is long (the weight gradients
+  // (four 64 x 64 or two 128 x 128 CTAs fit on an SM) and K is long (the weight gradients
   // dW = X^T dY, whose K is the batch's rows): at least 128 K per split.
   // The split depends on the shape only, and the partials are summed in
   // split order, so a step is reproducible.
   int splits = 1;
-  const int target = 8 * device_sms();
+  const int target = (big ? 4 : 8) * device_sms();
   if (tiles < target && K >= 512) {
     splits = (target + tiles - 1) / tiles;
     const int max_splits = K / 128;
@@ -145,12 +229,16 @@ cudaError_t gemm(Workspace& ws, int M, int N, int K, const float* A, int lda, bo
     if (splits < 1) splits = 1;
   }
   int k_chunk = (K + splits - 1) / splits;
-  k_chunk = (k_chunk + kBK - 1) / kBK * kBK;
+  k_chunk = (k_chunk + bk - 1) / bk * bk;
   splits = (K + k_chunk - 1) / k_chunk;
   if (splits < 1) splits = 1;
-  dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM, splits);
-  gemm_kernel<<<grid, 256, 0, s>>>(M, N, K, A, lda, ta, B, ldb, tb, C, ldc, accumulate, k_chunk,
-                                   splits > 1 ? ws.split : nullptr);
+  dim3 grid((N + bn - 1) / bn, (M + bm - 1) / bm, splits);
+  if (big)
+    gemm128_kernel<<<grid, 256, 0, s>>>(M, N, K, A, lda, ta, B, ldb, tb, C, ldc, accumulate, k_chunk,
+                                        splits > 1 ? ws.split : nullptr);
+  else
+    gemm_kernel<<<grid, 256, 0, s>>>(M, N, K, A, lda, ta, B, ldb, tb, C, ldc, accumulate, k_chunk,
+                                     splits > 1 ? ws.split : nullptr);
   if (splits > 1) {
     const size_t total = (size_t)M * N;
     gemm_reduce_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(M, N, splits, ws.split, C, ldc, accumulate);
