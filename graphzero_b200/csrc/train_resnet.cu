@@ -1,8 +1,10 @@
 // Connect4 ResNet training step: loss, backward pass and Adam, fp32 on CUDA
-// cores (the reference's backward_resnet and its losses,
-// networks/resnet/resnet.cu:669-699 and the cudnn*Backward* calls after it;
-// here the same network as the forward kernels: stem, 10 residual blocks
-// with a real residual add, policy and value heads, BN in inference form).
+// cores, for the network the forward kernels evaluate (stem, 10 residual
+// blocks with a real residual add, policy and value heads, BN in inference
+// form).  The reference's losses are networks/resnet/resnet.cu:669-699; its
+// backward_resnet (701-837) passes the input boards to every layer's filter
+// gradient (796, 807), so it is not a gradient to reproduce: this computes
+// the true one (checked against autograd in the tests).
 //
 // Convolutions are GEMMs over an im2col buffer: Z[rows][128] = col[rows][9 Cin]
 // . W^T with W stored [Cout][ky][kx][Cin]; their backward passes are
