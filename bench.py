@@ -12,7 +12,8 @@ weights reach every GPU through one NCCL broadcast before timing, and the
 reported time is the maximum over ranks.  Prints ONE JSON line on rank 0.
 The c1 line also carries, under "configs", the other leaf-evaluation
 workloads (c0 TicTacToe fp32, c2 Connect4 ResNet, c3 chess GAT) measured on
-the same GPU, each with its roofline and CPU baseline.
+the same GPU, each with its roofline and CPU baseline, and under "train" the
+training step time of the Connect4 GAT and ResNet at batch 64.
 
 --impl reference times the CPU restatement of the same math (the reference's
 own network code does not build) on the host cores with all threads; that
@@ -455,6 +456,39 @@ def other_config(name: str, dev: int, stream, with_cpu: bool) -> dict:
     return out
 
 
+def train_bench(dev: int, stream, steps: int = 20, warmup: int = 3) -> dict:
+    """Training steps (gz_net_train_step: loss, backward, Adam, repack) at the
+    reference's batch of 64 (gat.cu:716) on device-resident synthetic
+    batches, for the Connect4 GAT and ResNet, timed with CUDA events."""
+    import torch
+
+    out = {}
+    for name, kind in (("connect4_gat", GAT), ("connect4_resnet", RESNET)):
+        B = 64
+        net = gz.Net(CONNECT4, kind, device=dev, max_batch=B)
+        net.load_weights(gz.synth_weights(CONNECT4, kind, seed=0x7A1))
+        boards, side = gz.synth_positions(CONNECT4, B, seed=0x7A2)
+        rng = np.random.default_rng(0x7A3)
+        pi = rng.dirichlet(np.full(7, 0.5), size=B).astype(np.float32)
+        v = rng.uniform(-1, 1, B).astype(np.float32)
+        d = [torch.from_numpy(np.ascontiguousarray(x)).cuda(dev) for x in (boards, side, pi, v)]
+        cfg = gz.train_config()
+        for _ in range(warmup):
+            net.train_step(*d, B, cfg, stream=stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            net.train_step(*d, B, cfg, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        out[name] = {"batch": B, "steps": steps, "ms_per_step": ms, "positions_per_s": B / ms * 1e3,
+                     "dtype": "f32", "optimizer": "Adam (lr 1e-3, weight decay 1e-4)"}
+        net.close()
+    return out
+
+
 def ours(args, cfg: dict) -> None:
     import torch
 
@@ -546,6 +580,7 @@ def ours(args, cfg: dict) -> None:
         if info.world == 1 and args.config == "c1" and not args.no_other_configs:
             line["configs"] = {name: other_config(name, dev, stream, not args.no_cpu_baseline)
                                for name in ("c0", "c2", "c3")}
+            line["train"] = train_bench(dev, stream)
         print(json.dumps(line), flush=True)
     gzd.barrier()
     if multi:
