@@ -340,6 +340,8 @@ def mcts_bench(net, device, game: int, trees: int, sims: int, leaves: int, moves
     world = gzd.rank_info().world
     out = {"sims_per_s": trees * waves * leaves * moves * world / el,
            "positions_per_s": trees * moves * world / el,
+           "sims_per_s_per_gpu": trees * waves * leaves * moves / el,
+           "positions_per_s_per_gpu": trees * moves / el,
            "config": f"{trees} games/GPU x {sims} sims/move, leaf batch {trees * leaves}, c_puct 1.5, "
                      f"virtual loss 3, Dirichlet(1.0, 0.25), {moves} timed moves",
            # per move: a selection, per wave a network pass and a backup fused
