@@ -4,10 +4,11 @@
 //
 //   * a tile is 128 node rows = 2 positions x 64 squares;
 //   * the graph is the static queen-line + knight + self geometry (up to 36
-//     neighbours per square, 1856 edges per position), held as a neighbour
-//     table in shared memory; each row's attention weights span its
-//     position's 64 squares, i.e. 32 tensor-memory columns of the e buffer
-//     (lane quarters 0-1: columns 0-31, quarters 2-3: 32-63);
+//     neighbours per square, 1856 edges per position), held as a 0/1
+//     adjacency table in shared memory; each row's attention weights span
+//     its position's 64 squares, i.e. 32 tensor-memory columns of the e
+//     buffer, computed from per-square exponential factors (no exponential
+//     per edge; see the layer's score phase) and stored from registers;
 //   * layer 0 has 18 input features (K padded to 32);
 //   * policy: logits[square][73] = X_8[square] . W_pi + b_pi as one more MMA
 //     (N = 80, K = 256) on the last layer's activations, softmax over the
