@@ -292,10 +292,9 @@ __global__ void encode_kernel(int game, const int8_t* __restrict__ boards, const
 }
 
 // ------------------------------------------------------ graph attention ----
-// One CTA of 256 threads per position.  Per-node 256-vectors sit in shared
-// memory with an odd row stride, so threads that walk nodes hit distinct
-// banks.
-constexpr int kRS = 257;
+// One CTA per position and group of heads.  Per-node feature vectors sit in
+// shared memory with an odd row stride, so threads that walk nodes hit
+// distinct banks.
 
 struct GraphArgs {
   const int* g;  // row_ptr[N + 1] | col[nnz] | rev[nnz]; rev[e] = index of the edge j -> i for e = i -> j
@@ -310,33 +309,47 @@ __device__ __forceinline__ void load_graph(const GraphArgs& ga, int* rp, int* co
   }
 }
 
-size_t attn_fwd_smem(int N, int nnz) { return (size_t)(N * kRS + N * 16 + nnz * 8) * 4 + (size_t)(N + 1 + nnz) * 4; }
+// The attention kernels take one position and HS of its 8 heads per CTA
+// (32 threads a head): 8 at large batches, 2 when a batch has too few
+// positions to fill the device.  Heads are independent here, and each
+// head's sums run in the same order whatever HS is.
+template <int HS>
+__host__ __device__ constexpr int wh_stride() { return 32 * HS + 1; }  // odd: node walks hit distinct banks
+
+template <int HS>
+size_t attn_fwd_smem(int N, int nnz) {
+  return (size_t)(N * wh_stride<HS>() + N * 16 + nnz * 8) * 4 + (size_t)(N + 1 + nnz) * 4;
+}
+template <int HS>
 size_t attn_bwd_smem(int N, int nnz) {
-  return (size_t)(2 * N * kRS + N * 16 + nnz * 8 + N * 16) * 4 + (size_t)(N + 1 + 2 * nnz) * 4;
+  return (size_t)(2 * N * wh_stride<HS>() + N * 16 + nnz * 8 + N * 16) * 4 + (size_t)(N + 1 + 2 * nnz) * 4;
 }
 
 // Scores S [N][16] (s_i of heads 0-7, then t_i), attention weights alpha
-// [nnz][8], pre-activation Y = sum_j alpha_ij Wh_j + b and X' = ELU(Y).
-__global__ void __launch_bounds__(256) attn_fwd_kernel(GraphArgs ga, const float* __restrict__ Wh,
-                                                       const float* __restrict__ a, const float* __restrict__ bias,
-                                                       float* __restrict__ S, float* __restrict__ alpha,
-                                                       float* __restrict__ Y, float* __restrict__ Xn) {
+// [nnz][8], pre-activation Y = sum_j alpha_ij Wh_j + b and X' = ELU(Y), for
+// heads h0 .. h0 + HS - 1 (h0 = HS blockIdx.y) of position blockIdx.x.
+template <int HS>
+__global__ void __launch_bounds__(32 * HS) attn_fwd_kernel(GraphArgs ga, const float* __restrict__ Wh,
+                                                           const float* __restrict__ a, const float* __restrict__ bias,
+                                                           float* __restrict__ S, float* __restrict__ alpha,
+                                                           float* __restrict__ Y, float* __restrict__ Xn) {
+  constexpr int kF = 32 * HS, kW = wh_stride<HS>();
   extern __shared__ float sm[];
-  const int N = ga.N, nnz = ga.nnz, b = blockIdx.x;
-  float* wh = sm;            // [N][kRS]
-  float* ss = wh + N * kRS;  // [N][16]
-  float* al = ss + N * 16;   // [nnz][8]
+  const int N = ga.N, nnz = ga.nnz, b = blockIdx.x, h0 = HS * blockIdx.y;
+  float* wh = sm;           // [N][kW]: this CTA's heads' features
+  float* ss = wh + N * kW;  // [N][16]
+  float* al = ss + N * 16;  // [nnz][8]
   int* rp = (int*)(al + nnz * 8);
   int* col = rp + N + 1;
   load_graph(ga, rp, col, nullptr);
-  const float* whg = Wh + (size_t)b * N * 256;
-  for (int e = threadIdx.x; e < N * 256; e += 256) wh[(e >> 8) * kRS + (e & 255)] = whg[e];
+  const float* whg = Wh + (size_t)b * N * 256 + 32 * h0;
+  for (int e = threadIdx.x; e < N * kF; e += kF) wh[(e / kF) * kW + e % kF] = whg[(size_t)(e / kF) * 256 + e % kF];
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, hw = h0 + warp;
   {
-    const float as = a[warp * 64 + lane], an = a[warp * 64 + 32 + lane];  // a[h][0 self / 1 neighbour][d]
+    const float as = a[hw * 64 + lane], an = a[hw * 64 + 32 + lane];  // a[h][0 self / 1 neighbour][d]
     for (int i = 0; i < N; ++i) {
-      const float x = wh[i * kRS + 32 * warp + lane];
+      const float x = wh[i * kW + 32 * warp + lane];
       float p = x * as, q = x * an;
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) {
@@ -344,15 +357,18 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(GraphArgs ga, const float
         q += __shfl_xor_sync(0xffffffffu, q, o);
       }
       if (lane == 0) {
-        ss[i * 16 + warp] = p;
-        ss[i * 16 + 8 + warp] = q;
+        ss[i * 16 + hw] = p;
+        ss[i * 16 + 8 + hw] = q;
       }
     }
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < N * 16; e += 256) S[(size_t)b * N * 16 + e] = ss[e];
-  for (int t = threadIdx.x; t < N * 8; t += 256) {
-    const int i = t % N, h = t / N;
+  for (int e = threadIdx.x; e < N * 2 * HS; e += kF) {  // this CTA's score columns
+    const int i = e / (2 * HS), c = e % (2 * HS), k = (c < HS ? 0 : 8) + h0 + c % HS;
+    S[(size_t)b * N * 16 + i * 16 + k] = ss[i * 16 + k];
+  }
+  for (int t = threadIdx.x; t < N * HS; t += kF) {
+    const int i = t % N, h = h0 + t / N;
     const float si = ss[i * 16 + h];
     float mx = -INFINITY;
     for (int e = rp[i]; e < rp[i + 1]; ++e) {
@@ -373,55 +389,58 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(GraphArgs ga, const float
     }
   }
   __syncthreads();
-  const int f = threadIdx.x, h = f >> 5;
-  const float bf = bias[f];
+  const int f = threadIdx.x, h = h0 + (f >> 5), gf = 32 * h0 + f;
+  const float bf = bias[gf];
   for (int i = 0; i < N; ++i) {
     float acc = 0.f;
-    for (int e = rp[i]; e < rp[i + 1]; ++e) acc = fmaf(al[e * 8 + h], wh[col[e] * kRS + f], acc);
+    for (int e = rp[i]; e < rp[i + 1]; ++e) acc = fmaf(al[e * 8 + h], wh[col[e] * kW + f], acc);
     const float y = acc + bf;
-    const size_t o = ((size_t)b * N + i) * 256 + f;
+    const size_t o = ((size_t)b * N + i) * 256 + gf;
     Y[o] = y;
     Xn[o] = y > 0.f ? y : expm1f(y);
   }
 }
 
-// Backward of attn_fwd_kernel for one position: from dX' (gradient of the
-// layer output) to dWh, dY (for the bias gradient) and this position's
-// share of the attention-weight gradient, da_part [8][2][32].
-__global__ void __launch_bounds__(256) attn_bwd_kernel(GraphArgs ga, const float* __restrict__ dXn,
-                                                       const float* __restrict__ Y, const float* __restrict__ Wh,
-                                                       const float* __restrict__ S, const float* __restrict__ alpha,
-                                                       const float* __restrict__ a, float* __restrict__ dWh,
-                                                       float* __restrict__ dY, float* __restrict__ da_part) {
+// Backward of attn_fwd_kernel for one position and HS heads: from dX'
+// (gradient of the layer output) to dWh, dY (for the bias gradient) and
+// this position's share of the attention-weight gradient, da_part [8][2][32].
+template <int HS>
+__global__ void __launch_bounds__(32 * HS) attn_bwd_kernel(GraphArgs ga, const float* __restrict__ dXn,
+                                                           const float* __restrict__ Y, const float* __restrict__ Wh,
+                                                           const float* __restrict__ S, const float* __restrict__ alpha,
+                                                           const float* __restrict__ a, float* __restrict__ dWh,
+                                                           float* __restrict__ dY, float* __restrict__ da_part) {
+  constexpr int kF = 32 * HS, kW = wh_stride<HS>();
   extern __shared__ float sm[];
-  const int N = ga.N, nnz = ga.nnz, b = blockIdx.x;
-  float* dy = sm;             // [N][kRS]
-  float* wh = dy + N * kRS;   // [N][kRS]
-  float* ss = wh + N * kRS;   // [N][16]
+  const int N = ga.N, nnz = ga.nnz, b = blockIdx.x, h0 = HS * blockIdx.y;
+  float* dy = sm;             // [N][kW]
+  float* wh = dy + N * kW;    // [N][kW]
+  float* ss = wh + N * kW;    // [N][16]
   float* dx = ss + N * 16;    // [nnz][8]: dalpha, then d(s_i + t_j)
   float* dst = dx + nnz * 8;  // [N][16]: ds (heads 0-7), dt (8-15)
   int* rp = (int*)(dst + N * 16);
   int* col = rp + N + 1;
   int* rev = col + nnz;
   load_graph(ga, rp, col, rev);
-  const size_t base = (size_t)b * N * 256;
-  for (int e = threadIdx.x; e < N * 256; e += 256) {
-    const float y = Y[base + e];
-    const float g = dXn[base + e] * (y > 0.f ? 1.f : expf(y));
-    dy[(e >> 8) * kRS + (e & 255)] = g;
-    dY[base + e] = g;
-    wh[(e >> 8) * kRS + (e & 255)] = Wh[base + e];
+  const size_t base = (size_t)b * N * 256 + 32 * h0;
+  for (int e = threadIdx.x; e < N * kF; e += kF) {
+    const size_t ge = base + (size_t)(e / kF) * 256 + e % kF;
+    const float y = Y[ge];
+    const float g = dXn[ge] * (y > 0.f ? 1.f : expf(y));
+    dy[(e / kF) * kW + e % kF] = g;
+    dY[ge] = g;
+    wh[(e / kF) * kW + e % kF] = Wh[ge];
   }
-  for (int e = threadIdx.x; e < N * 16; e += 256) ss[e] = S[(size_t)b * N * 16 + e];
+  for (int e = threadIdx.x; e < N * 16; e += kF) ss[e] = S[(size_t)b * N * 16 + e];
   __syncthreads();
   const float* alb = alpha + (size_t)b * nnz * 8;
   // node i, head h: dalpha over i's edges, softmax and LeakyReLU backward
-  for (int t = threadIdx.x; t < N * 8; t += 256) {
-    const int i = t % N, h = t / N;
-    const float* dyi = dy + i * kRS + 32 * h;
+  for (int t = threadIdx.x; t < N * HS; t += kF) {
+    const int i = t % N, hl = t / N, h = h0 + hl;
+    const float* dyi = dy + i * kW + 32 * hl;
     float sbar = 0.f;
     for (int e = rp[i]; e < rp[i + 1]; ++e) {
-      const float* whj = wh + col[e] * kRS + 32 * h;
+      const float* whj = wh + col[e] * kW + 32 * hl;
       float d = 0.f;
 #pragma unroll 8
       for (int k = 0; k < 32; ++k) d = fmaf(dyi[k], whj[k], d);
@@ -441,22 +460,22 @@ __global__ void __launch_bounds__(256) attn_bwd_kernel(GraphArgs ga, const float
   }
   __syncthreads();
   // node j, head h: dt_j = sum over the edges i -> j
-  for (int t = threadIdx.x; t < N * 8; t += 256) {
-    const int j = t % N, h = t / N;
+  for (int t = threadIdx.x; t < N * HS; t += kF) {
+    const int j = t % N, h = h0 + t / N;
     float dt = 0.f;
     for (int e = rp[j]; e < rp[j + 1]; ++e) dt += dx[rev[e] * 8 + h];
     dst[j * 16 + 8 + h] = dt;
   }
   __syncthreads();
-  const int f = threadIdx.x, h = f >> 5, d = f & 31;
+  const int f = threadIdx.x, h = h0 + (f >> 5), d = f & 31;
   const float as = a[h * 64 + d], an = a[h * 64 + 32 + d];
   float pa = 0.f, pn = 0.f;
   for (int j = 0; j < N; ++j) {
     float acc = 0.f;
-    for (int e = rp[j]; e < rp[j + 1]; ++e) acc = fmaf(alb[rev[e] * 8 + h], dy[col[e] * kRS + f], acc);
+    for (int e = rp[j]; e < rp[j + 1]; ++e) acc = fmaf(alb[rev[e] * 8 + h], dy[col[e] * kW + f], acc);
     const float ds = dst[j * 16 + h], dt = dst[j * 16 + 8 + h];
     dWh[base + (size_t)j * 256 + f] = acc + ds * as + dt * an;
-    const float w = wh[j * kRS + f];
+    const float w = wh[j * kW + f];
     pa = fmaf(ds, w, pa);
     pn = fmaf(dt, w, pn);
   }
@@ -702,9 +721,14 @@ cudaError_t ensure_state(State& st, int game, int capacity) {
     if ((e = cudaEventCreateWithFlags(&st.ev_comm, cudaEventDisableTiming))) return e;
     // the kernels serve every game: allow the largest (chess) shared memory
     const GameShape big = game_shape(kChess);
-    const size_t fwd = attn_fwd_smem(big.nodes, big.nnz), bwd = attn_bwd_smem(big.nodes, big.nnz);
-    if ((e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd)) ||
-        (e = cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd)))
+    if ((e = cudaFuncSetAttribute(attn_fwd_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)attn_fwd_smem<8>(big.nodes, big.nnz))) ||
+        (e = cudaFuncSetAttribute(attn_bwd_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)attn_bwd_smem<8>(big.nodes, big.nnz))) ||
+        (e = cudaFuncSetAttribute(attn_fwd_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)attn_fwd_smem<2>(big.nodes, big.nnz))) ||
+        (e = cudaFuncSetAttribute(attn_bwd_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)attn_bwd_smem<2>(big.nodes, big.nnz))))
       return e;
   }
   if (capacity > st.capacity) {
@@ -737,7 +761,27 @@ cudaError_t loss_and_grad(State& st, const float* w, const int8_t* boards, const
   float* g = st.grad;
   Workspace& ws = st.ws;
   const GraphArgs ga{st.graph, N, sh.nnz};
-  const size_t fwd_smem = attn_fwd_smem(N, sh.nnz), bwd_smem = attn_bwd_smem(N, sh.nnz);
+  // all 8 heads of a position per CTA, or 2 when the batch has fewer
+  // positions than the device has SMs
+  const bool split_heads = B < device_sms();
+  auto attn_fwd = [&](int l) {
+    if (split_heads)
+      attn_fwd_kernel<2><<<dim3(B, 4), 64, attn_fwd_smem<2>(N, sh.nnz), s>>>(
+          ga, ar + o.Wh[l], w + t.a[l], w + t.b[l], ar + o.S[l], ar + o.alpha[l], ar + o.Y[l], ar + o.X[l + 1]);
+    else
+      attn_fwd_kernel<8><<<dim3(B, 1), 256, attn_fwd_smem<8>(N, sh.nnz), s>>>(
+          ga, ar + o.Wh[l], w + t.a[l], w + t.b[l], ar + o.S[l], ar + o.alpha[l], ar + o.Y[l], ar + o.X[l + 1]);
+  };
+  auto attn_bwd = [&](int l, const float* dX) {
+    if (split_heads)
+      attn_bwd_kernel<2><<<dim3(B, 4), 64, attn_bwd_smem<2>(N, sh.nnz), s>>>(
+          ga, dX, ar + o.Y[l], ar + o.Wh[l], ar + o.S[l], ar + o.alpha[l], w + t.a[l], ar + o.dWh, ar + o.dY,
+          ar + o.dapart);
+    else
+      attn_bwd_kernel<8><<<dim3(B, 1), 256, attn_bwd_smem<8>(N, sh.nnz), s>>>(
+          ga, dX, ar + o.Y[l], ar + o.Wh[l], ar + o.S[l], ar + o.alpha[l], w + t.a[l], ar + o.dWh, ar + o.dY,
+          ar + o.dapart);
+  };
 
   // ---- forward ----
   encode_kernel<<<(rowsN + 255) / 256, 256, 0, s>>>(game, boards, side, B, ar + o.X[0]);
@@ -745,8 +789,7 @@ cudaError_t loss_and_grad(State& st, const float* w, const int8_t* boards, const
     const int Fl = l ? kHidden : sh.features;
     GZ_TRY(gemm(ws, rowsN, kHidden, Fl, ar + o.X[l], Fl, false, w + t.W[l], kHidden, false, ar + o.Wh[l], kHidden,
                 false, s));
-    attn_fwd_kernel<<<B, 256, fwd_smem, s>>>(ga, ar + o.Wh[l], w + t.a[l], w + t.b[l], ar + o.S[l], ar + o.alpha[l],
-                                             ar + o.Y[l], ar + o.X[l + 1]);
+    attn_fwd(l);
   }
   float* XL = ar + o.X[L];
   pool_fwd_kernel<<<B, 256, 0, s>>>(game, XL, ar + o.gmean, ar + o.colmean);
@@ -779,8 +822,7 @@ cudaError_t loss_and_grad(State& st, const float* w, const int8_t* boards, const
   pool_bwd_kernel<<<B, 256, 0, s>>>(game, ar + o.dgmean, ar + o.dpol, dX);
   for (int l = L - 1; l >= 0; --l) {
     const int Fl = l ? kHidden : sh.features;
-    attn_bwd_kernel<<<B, 256, bwd_smem, s>>>(ga, dX, ar + o.Y[l], ar + o.Wh[l], ar + o.S[l], ar + o.alpha[l],
-                                             w + t.a[l], ar + o.dWh, ar + o.dY, ar + o.dapart);
+    attn_bwd(l, dX);
     GZ_TRY(colsum(ws, ar + o.dY, rowsN, kHidden, kHidden, g + t.b[l], false, s));
     GZ_TRY(colsum(ws, ar + o.dapart, B, 512, 512, g + t.a[l], false, s));
     GZ_TRY(gemm(ws, Fl, kHidden, rowsN, ar + o.X[l], Fl, true, ar + o.dWh, kHidden, false, g + t.W[l], kHidden, false,
