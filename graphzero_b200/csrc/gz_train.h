@@ -43,8 +43,12 @@ struct AdamParams {
   float lr, beta1, beta2, eps, weight_decay, grad_scale;
 };
 
+// im2col 1 (2): A (B) is the 3 x 3 im2col matrix, [rows][9 * 128], of the
+// [rows][128] Connect4 activation it points at, read in place (lda / ldb
+// unused); needs gemm_big(M, N) and that operand untransposed.
 cudaError_t gemm(Workspace& ws, int M, int N, int K, const float* A, int lda, bool ta, const float* B, int ldb,
-                 bool tb, float* C, int ldc, bool accumulate, cudaStream_t s);
+                 bool tb, float* C, int ldc, bool accumulate, cudaStream_t s, int im2col = 0);
+bool gemm_big(int M, int N);  // outputs that take the 128 x 128 tile kernel
 cudaError_t colsum(Workspace& ws, const float* in, int R, int C, int ld, float* out, bool accumulate,
                    cudaStream_t s, float scale = 1.f);
 

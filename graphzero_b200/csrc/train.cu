@@ -112,6 +112,18 @@ __global__ void __launch_bounds__(256) gemm_kernel(int M, int N, int K, const fl
 // its products in ascending k, one fused multiply-add at a time.
 constexpr int kBM2 = 128, kBN2 = 128, kBK2 = 8, kPad2 = 4;
 
+// Element (row, j) of the im2col matrix of a [rows][128] activation on the
+// 6 x 7 board: j = tap * 128 + channel with taps (ky, kx) row-major, 0 where
+// the tap leaves the board (the Connect4 ResNet's 3 x 3 convolutions).
+__device__ __forceinline__ float im2col_at(const float* __restrict__ in, int row, int j) {
+  const int tap = j >> 7, ci = j & 127;
+  const int p = row % 42, r = p / 7 + tap / 3 - 1, c = p % 7 + tap % 3 - 1;
+  return (r >= 0 && r < 6 && c >= 0 && c < 7) ? __ldg(in + (size_t)(row - p + r * 7 + c) * 128 + ci) : 0.f;
+}
+
+// kIm: 0 plain operands; 1 A is the im2col matrix of the activation A
+// points at (ta false); 2 likewise for B (tb false).
+template <int kIm>
 __global__ void __launch_bounds__(256) gemm128_kernel(int M, int N, int K, const float* __restrict__ A, int lda,
                                                       int ta, const float* __restrict__ B, int ldb, int tb, float* C,
                                                       int ldc, int accumulate, int k_chunk, float* part) {
@@ -130,11 +142,17 @@ __global__ void __launch_bounds__(256) gemm128_kernel(int M, int N, int K, const
       int m, k;
       if (ta) { m = e % kBM2; k = e / kBM2; } else { k = e % kBK2; m = e / kBK2; }
       const int gm = m0 + m, gk = k0 + k;
-      ra[r] = (gm < M && gk < k_hi) ? (ta ? A[(size_t)gk * lda + gm] : A[(size_t)gm * lda + gk]) : 0.f;
+      if constexpr (kIm == 1)
+        ra[r] = (gm < M && gk < k_hi) ? im2col_at(A, gm, gk) : 0.f;
+      else
+        ra[r] = (gm < M && gk < k_hi) ? (ta ? A[(size_t)gk * lda + gm] : A[(size_t)gm * lda + gk]) : 0.f;
       int n, kb;
       if (tb) { kb = e % kBK2; n = e / kBK2; } else { n = e % kBN2; kb = e / kBN2; }
       const int gn = n0 + n, gkb = k0 + kb;
-      rb[r] = (gn < N && gkb < k_hi) ? (tb ? B[(size_t)gn * ldb + gkb] : B[(size_t)gkb * ldb + gn]) : 0.f;
+      if constexpr (kIm == 2)
+        rb[r] = (gn < N && gkb < k_hi) ? im2col_at(B, gkb, gn) : 0.f;
+      else
+        rb[r] = (gn < N && gkb < k_hi) ? (tb ? B[(size_t)gn * ldb + gkb] : B[(size_t)gkb * ldb + gn]) : 0.f;
     }
   };
   auto store = [&](int buf) {
@@ -207,9 +225,12 @@ static int device_sms() {
   return sms[dev];
 }
 
+bool gemm_big(int M, int N) { return M >= kBM2 && N >= kBN2; }
+
 cudaError_t gemm(Workspace& ws, int M, int N, int K, const float* A, int lda, bool ta, const float* B, int ldb,
-                 bool tb, float* C, int ldc, bool accumulate, cudaStream_t s) {
+                 bool tb, float* C, int ldc, bool accumulate, cudaStream_t s, int im2col) {
   if (M <= 0 || N <= 0) return cudaSuccess;
+  if (im2col && (!gemm_big(M, N) || (im2col == 1 && ta) || (im2col == 2 && tb))) return cudaErrorInvalidValue;
   // large outputs take the 128 x 128 tile kernel
   const bool big = M >= kBM2 && N >= kBN2;
   const int bm = big ? kBM2 : kBM, bn = big ? kBN2 : kBN, bk = big ? kBK2 : kBK;
@@ -233,9 +254,13 @@ cudaError_t gemm(Workspace& ws, int M, int N, int K, const float* A, int lda, bo
   splits = (K + k_chunk - 1) / k_chunk;
   if (splits < 1) splits = 1;
   dim3 grid((N + bn - 1) / bn, (M + bm - 1) / bm, splits);
-  if (big)
-    gemm128_kernel<<<grid, 256, 0, s>>>(M, N, K, A, lda, ta, B, ldb, tb, C, ldc, accumulate, k_chunk,
-                                        splits > 1 ? ws.split : nullptr);
+  float* part = splits > 1 ? ws.split : nullptr;
+  if (big && im2col == 1)
+    gemm128_kernel<1><<<grid, 256, 0, s>>>(M, N, K, A, lda, ta, B, ldb, tb, C, ldc, accumulate, k_chunk, part);
+  else if (big && im2col == 2)
+    gemm128_kernel<2><<<grid, 256, 0, s>>>(M, N, K, A, lda, ta, B, ldb, tb, C, ldc, accumulate, k_chunk, part);
+  else if (big)
+    gemm128_kernel<0><<<grid, 256, 0, s>>>(M, N, K, A, lda, ta, B, ldb, tb, C, ldc, accumulate, k_chunk, part);
   else
     gemm_kernel<<<grid, 256, 0, s>>>(M, N, K, A, lda, ta, B, ldb, tb, C, ldc, accumulate, k_chunk,
                                      splits > 1 ? ws.split : nullptr);

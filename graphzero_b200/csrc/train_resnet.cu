@@ -358,12 +358,17 @@ cudaError_t bn_grads(Workspace& ws, const ResLayout& t, int k, const float* dpre
 }
 
 // conv k's weight gradient dW[Cout][9 Cin] = dz^T . im2col(in); with
-// `din`, also din = col2im(dz . W) (+ `add` when given).
+// `din`, also din = col2im(dz . W) (+ `add` when given).  The 128-channel
+// convolutions read im2col(in) in place; the 3-channel stem materialises it.
 cudaError_t conv_bwd(Workspace& ws, const ResLayout& t, int k, const float* w, const float* in, const float* dz,
                      float* col, float* dcol, int rows, float* g, float* din, const float* add, cudaStream_t s) {
   const int cin = conv_cin(k), K = 9 * cin;
-  im2col_kernel<<<blocks_for((size_t)rows * K, 256), 256, 0, s>>>(in, cin, rows, col);
-  GZ_TRY(gemm(ws, kC, K, rows, dz, kC, true, col, K, false, g + conv_w(t, k), K, false, s));
+  if (cin == kC && gemm_big(kC, K)) {
+    GZ_TRY(gemm(ws, kC, K, rows, dz, kC, true, in, 0, false, g + conv_w(t, k), K, false, s, 2));
+  } else {
+    im2col_kernel<<<blocks_for((size_t)rows * K, 256), 256, 0, s>>>(in, cin, rows, col);
+    GZ_TRY(gemm(ws, kC, K, rows, dz, kC, true, col, K, false, g + conv_w(t, k), K, false, s));
+  }
   if (!din) return cudaGetLastError();
   GZ_TRY(gemm(ws, rows, K, kC, dz, kC, false, w + conv_w(t, k), K, false, dcol, K, false, s));
   col2im_kernel<<<blocks_for((size_t)rows * cin, 256), 256, 0, s>>>(dcol, cin, rows, din);
@@ -371,10 +376,11 @@ cudaError_t conv_bwd(Workspace& ws, const ResLayout& t, int k, const float* w, c
   return cudaGetLastError();
 }
 
-// Z = im2col(in) . W^T for conv k
+// Z = im2col(in) . W^T for conv k (in place for 128 channels, as conv_bwd)
 cudaError_t conv_fwd(Workspace& ws, const ResLayout& t, int k, const float* w, const float* in, float* col,
                      float* z, int rows, cudaStream_t s) {
   const int cin = conv_cin(k), K = 9 * cin;
+  if (cin == kC && gemm_big(rows, kC)) return gemm(ws, rows, kC, K, in, 0, false, w + conv_w(t, k), K, true, z, kC, false, s, 1);
   im2col_kernel<<<blocks_for((size_t)rows * K, 256), 256, 0, s>>>(in, cin, rows, col);
   return gemm(ws, rows, kC, K, col, K, false, w + conv_w(t, k), K, true, z, kC, false, s);
 }
