@@ -128,22 +128,40 @@ __global__ void bn_relu_fwd_kernel(const float* __restrict__ z, const float* __r
   out[i] = fmaxf(y, 0.f);
 }
 
-// Backward of out = ReLU(BN(z) [+ res]): dpre = dout * (out > 0);
-// dz = dpre * gamma * inv; prod = dpre * xhat (for dgamma); dres = dpre
-// (the residual's gradient, and BN's beta gradient before the row sum).
-// dz may alias z and dres may alias dout (same element, read first).
-__global__ void bn_relu_bwd_kernel(const float* dout, const float* __restrict__ out, const float* z,
-                                   const float* __restrict__ bn, int rows, float* dz, float* __restrict__ prod,
-                                   float* dres) {
-  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (size_t)rows * kC) return;
-  const int c = (int)(i % kC);
-  const float inv = bn_inv(bn, kC, c);
-  const float dpre = out[i] > 0.f ? dout[i] : 0.f;
-  const float zi = z[i];
-  dz[i] = dpre * bn[c] * inv;
-  prod[i] = dpre * (zi - bn[2 * kC + c]) * inv;
-  if (dres) dres[i] = dpre;
+// Backward of out = ReLU(BN(z) [+ res]) with BN's gradient sums: dpre =
+// dout * (out > 0); dz = dpre * gamma * inv (dz may alias z); dres = dpre
+// when given (the residual's gradient; may alias dout).  Block `slice` of
+// kBnSlices takes a contiguous run of rows, thread c channel c, and writes
+// the run's sums of dpre * xhat (gamma's gradient) and of dpre (beta's) to
+// part[0][slice][c] and part[1][slice][c]; bn_sum_final_kernel adds the
+// runs in order.
+constexpr int kBnSlices = 256;
+__global__ void __launch_bounds__(128) bn_relu_bwd_sum_kernel(const float* dout, const float* __restrict__ out,
+                                                              const float* z, const float* __restrict__ bn, int rows,
+                                                              float* dz, float* dres, float* __restrict__ part) {
+  const int c = threadIdx.x, slice = blockIdx.x;
+  const int per = (rows + kBnSlices - 1) / kBnSlices, r0 = slice * per, r1 = min(rows, r0 + per);
+  const float inv = bn_inv(bn, kC, c), gamma = bn[c], mu = bn[2 * kC + c];
+  float sg = 0.f, sb = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const size_t i = (size_t)r * kC + c;
+    const float dpre = out[i] > 0.f ? dout[i] : 0.f;
+    const float zi = z[i];
+    dz[i] = dpre * gamma * inv;
+    if (dres) dres[i] = dpre;
+    sg = fmaf(dpre, (zi - mu) * inv, sg);
+    sb += dpre;
+  }
+  part[slice * kC + c] = sg;
+  part[(kBnSlices + slice) * kC + c] = sb;
+}
+
+// g_bn[0 .. 127] = gamma gradients, g_bn[128 .. 255] = beta gradients
+__global__ void __launch_bounds__(256) bn_sum_final_kernel(const float* __restrict__ part, float* __restrict__ g_bn) {
+  const int which = threadIdx.x >> 7, c = threadIdx.x & 127;
+  float s = 0.f;
+  for (int k = 0; k < kBnSlices; ++k) s += part[(which * kBnSlices + k) * kC + c];
+  g_bn[which * kC + c] = s;
 }
 
 // The two 1x1 head convolutions and their BN, one warp per square:
@@ -350,11 +368,14 @@ cudaError_t res_ensure_state(State& st, int capacity) {
 
 namespace {
 
-// BN gradients of conv k from dpre (dbeta) and prod (dgamma), summed over rows
-cudaError_t bn_grads(Workspace& ws, const ResLayout& t, int k, const float* dpre, const float* prod, int rows,
-                     float* g, cudaStream_t s) {
-  GZ_TRY(colsum(ws, prod, rows, kC, kC, g + conv_bn(t, k), false, s));
-  return colsum(ws, dpre, rows, kC, kC, g + conv_bn(t, k) + kC, false, s);
+// Backward of conv k's out = ReLU(BN(z) [+ res]) from dout: dz into `dz`
+// (may be z), the residual's gradient into `dres` when given (may be dout),
+// and the BN gamma and beta gradients into g.
+cudaError_t bn_bwd(Workspace& ws, const ResLayout& t, int k, const float* w, const float* dout, const float* out,
+                   const float* z, int rows, float* dz, float* dres, float* g, cudaStream_t s) {
+  bn_relu_bwd_sum_kernel<<<kBnSlices, 128, 0, s>>>(dout, out, z, w + conv_bn(t, k), rows, dz, dres, ws.colsum);
+  bn_sum_final_kernel<<<1, 256, 0, s>>>(ws.colsum, g + conv_bn(t, k));
+  return cudaGetLastError();
 }
 
 // conv k's weight gradient dW[Cout][9 Cin] = dz^T . im2col(in); with
@@ -452,27 +473,20 @@ cudaError_t res_loss_and_grad(State& st, const float* w, const int8_t* boards, c
   // which the backward pass no longer needs once BN's backward has read it.
   float* dR = ar + o.dR;  // gradient of the block input through the residual add
   float* dT = ar + o.dT;
-  float* prod = ar + o.prod;
   for (int i = kResBlocks - 1; i >= 0; --i) {
     const int k1 = 1 + 2 * i, k2 = 2 + 2 * i;
     // a_{i+1} = ReLU(BN2(z2) + a_i)
-    bn_relu_bwd_kernel<<<blocks_for(act, 256), 256, 0, s>>>(dA, ar + o.A[i + 1], ar + o.Z[k2], w + t.bn2[i], rows,
-                                                           ar + o.Z[k2], prod, dR);
-    GZ_TRY(bn_grads(ws, t, k2, dR, prod, rows, g, s));
+    GZ_TRY(bn_bwd(ws, t, k2, w, dA, ar + o.A[i + 1], ar + o.Z[k2], rows, ar + o.Z[k2], dR, g, s));
     // z2 = conv2(t_i): Z[k2] now holds dz2
     GZ_TRY(conv_bwd(ws, t, k2, w, ar + o.T[i], ar + o.Z[k2], col, dcol, rows, g, dT, nullptr, s));
     // t_i = ReLU(BN1(z1))
-    bn_relu_bwd_kernel<<<blocks_for(act, 256), 256, 0, s>>>(dT, ar + o.T[i], ar + o.Z[k1], w + t.bn1[i], rows,
-                                                           ar + o.Z[k1], prod, dT);
-    GZ_TRY(bn_grads(ws, t, k1, dT, prod, rows, g, s));
+    GZ_TRY(bn_bwd(ws, t, k1, w, dT, ar + o.T[i], ar + o.Z[k1], rows, ar + o.Z[k1], nullptr, g, s));
     // z1 = conv1(a_i); da_i = dR + col2im(dz1 . W1)
     GZ_TRY(conv_bwd(ws, t, k1, w, ar + o.A[i], ar + o.Z[k1], col, dcol, rows, g, dA, dR, s));
     GZ_TRY(bucket_done(kResBlocks - i));
   }
   // ---- stem ----
-  bn_relu_bwd_kernel<<<blocks_for(act, 256), 256, 0, s>>>(dA, ar + o.A[0], ar + o.Z[0], w + t.stem_bn, rows,
-                                                         ar + o.Z[0], prod, dR);
-  GZ_TRY(bn_grads(ws, t, 0, dR, prod, rows, g, s));
+  GZ_TRY(bn_bwd(ws, t, 0, w, dA, ar + o.A[0], ar + o.Z[0], rows, ar + o.Z[0], nullptr, g, s));
   GZ_TRY(conv_bwd(ws, t, 0, w, ar + o.x0, ar + o.Z[0], col, dcol, rows, g, nullptr, nullptr, s));
   GZ_TRY(bucket_done(kResBlocks + 1));
   return cudaSuccess;
