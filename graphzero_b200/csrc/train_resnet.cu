@@ -156,12 +156,17 @@ __global__ void __launch_bounds__(128) bn_relu_bwd_sum_kernel(const float* dout,
   part[(kBnSlices + slice) * kC + c] = sb;
 }
 
-// g_bn[0 .. 127] = gamma gradients, g_bn[128 .. 255] = beta gradients
+// g_bn[0 .. 127] = gamma gradients, g_bn[128 .. 255] = beta gradients: one
+// warp per output, lane l adding runs l, l + 32, ... in order, then a fixed
+// shuffle tree over the lanes.
 __global__ void __launch_bounds__(256) bn_sum_final_kernel(const float* __restrict__ part, float* __restrict__ g_bn) {
-  const int which = threadIdx.x >> 7, c = threadIdx.x & 127;
+  const int o = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int which = o >> 7, c = o & 127;
   float s = 0.f;
-  for (int k = 0; k < kBnSlices; ++k) s += part[(which * kBnSlices + k) * kC + c];
-  g_bn[which * kC + c] = s;
+  for (int k = lane; k < kBnSlices; k += 32) s += part[(which * kBnSlices + k) * kC + c];
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) s += __shfl_xor_sync(0xffffffffu, s, w);
+  if (lane == 0) g_bn[which * kC + c] = s;
 }
 
 // The two 1x1 head convolutions and their BN, one warp per square:
@@ -374,7 +379,7 @@ namespace {
 cudaError_t bn_bwd(Workspace& ws, const ResLayout& t, int k, const float* w, const float* dout, const float* out,
                    const float* z, int rows, float* dz, float* dres, float* g, cudaStream_t s) {
   bn_relu_bwd_sum_kernel<<<kBnSlices, 128, 0, s>>>(dout, out, z, w + conv_bn(t, k), rows, dz, dres, ws.colsum);
-  bn_sum_final_kernel<<<1, 256, 0, s>>>(ws.colsum, g + conv_bn(t, k));
+  bn_sum_final_kernel<<<2 * kC / 8, 256, 0, s>>>(ws.colsum, g + conv_bn(t, k));
   return cudaGetLastError();
 }
 
