@@ -11,6 +11,9 @@
 namespace gz {
 namespace train {
 
+// Floats of the column-sum scratch: 64 row slices of up to 4672 columns.
+constexpr size_t kColsumFloats = (size_t)64 * 4672;
+
 // Scratch shared by the GEMMs (split-K partials) and the column sums.
 struct Workspace {
   float* split = nullptr;

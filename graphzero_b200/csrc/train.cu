@@ -738,7 +738,7 @@ cudaError_t ensure_state(State& st, int game, int capacity) {
         (e = cudaMemcpy(st.graph, g.data(), g.size() * 4, cudaMemcpyHostToDevice)))
       return e;
     st.ws.split_floats = (size_t)4 << 20;
-    if ((e = cudaMalloc(&st.ws.split, st.ws.split_floats * 4)) || (e = cudaMalloc(&st.ws.colsum, (size_t)64 * 4672 * 4)))
+    if ((e = cudaMalloc(&st.ws.split, st.ws.split_floats * 4)) || (e = cudaMalloc(&st.ws.colsum, kColsumFloats * 4)))
       return e;
     if ((e = cudaStreamCreateWithFlags(&st.comm_stream, cudaStreamNonBlocking))) return e;
     for (auto& ev : st.ev_bucket)

@@ -136,6 +136,7 @@ __global__ void bn_relu_fwd_kernel(const float* __restrict__ z, const float* __r
 // part[0][slice][c] and part[1][slice][c]; bn_sum_final_kernel adds the
 // runs in order.
 constexpr int kBnSlices = 256;
+static_assert((size_t)2 * kBnSlices * kC <= kColsumFloats, "BN partial sums fit the column-sum scratch");
 __global__ void __launch_bounds__(128) bn_relu_bwd_sum_kernel(const float* dout, const float* __restrict__ out,
                                                               const float* z, const float* __restrict__ bn, int rows,
                                                               float* dz, float* dres, float* __restrict__ part) {
@@ -346,7 +347,7 @@ cudaError_t res_ensure_state(State& st, int capacity) {
     if ((e = cudaMemset(st.m, 0, wc * 4)) || (e = cudaMemset(st.v, 0, wc * 4)) || (e = cudaMemset(st.grad, 0, wc * 4)))
       return e;
     st.ws.split_floats = (size_t)4 << 20;
-    if ((e = cudaMalloc(&st.ws.split, st.ws.split_floats * 4)) || (e = cudaMalloc(&st.ws.colsum, (size_t)64 * 4672 * 4)))
+    if ((e = cudaMalloc(&st.ws.split, st.ws.split_floats * 4)) || (e = cudaMalloc(&st.ws.colsum, kColsumFloats * 4)))
       return e;
     if ((e = cudaStreamCreateWithFlags(&st.comm_stream, cudaStreamNonBlocking))) return e;
     for (auto& ev : st.ev_bucket)
