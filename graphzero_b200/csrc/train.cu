@@ -13,9 +13,9 @@
 //   Wh = X W_l                       GEMM over all B*N node rows
 //   s_i = a_self . Wh_i^h, t_j = a_nbr . Wh_j^h, x_ij = s_i + t_j
 //   alpha_ij = softmax_j lrelu(x_ij)  over the board graph's CSR neighbours
-//   Y_i = sum_j alpha_ij Wh_j + b,  X' = ELU(Y)          (one CTA per position)
-// Backward, per layer (one CTA per position for the graph part):
-//   dY = dX' * ELU'(Y); db = sum dY
+//   Y_i = sum_j alpha_ij Wh_j + b,  X' = ELU(Y)          (one CTA per position and group of heads)
+// Backward, per layer (the same CTAs for the graph part):
+//   dY = dX' * ELU'(Y); db = sum dY (per position, then over the batch)
 //   dalpha_ij = dY_i . Wh_j; de_ij = alpha_ij (dalpha_ij - sum_k alpha_ik dalpha_ik)
 //   dx_ij = de_ij lrelu'(x_ij); ds_i = sum_j dx_ij; dt_j = sum_i dx_ij
 //   dWh_j = sum_i alpha_ij dY_i + ds_j a_self + dt_j a_nbr
@@ -427,14 +427,15 @@ __global__ void __launch_bounds__(32 * HS) attn_fwd_kernel(GraphArgs ga, const f
 }
 
 // Backward of attn_fwd_kernel for one position and HS heads: from dX'
-// (gradient of the layer output) to dWh, dY (for the bias gradient) and
-// this position's share of the attention-weight gradient, da_part [8][2][32].
+// (gradient of the layer output) to dWh, this position's share of the bias
+// gradient db_part [256] (dY = dX' ELU'(Y) summed over its nodes in order)
+// and of the attention-weight gradient, da_part [8][2][32].
 template <int HS>
 __global__ void __launch_bounds__(32 * HS) attn_bwd_kernel(GraphArgs ga, const float* __restrict__ dXn,
                                                            const float* __restrict__ Y, const float* __restrict__ Wh,
                                                            const float* __restrict__ S, const float* __restrict__ alpha,
                                                            const float* __restrict__ a, float* __restrict__ dWh,
-                                                           float* __restrict__ dY, float* __restrict__ da_part) {
+                                                           float* __restrict__ db_part, float* __restrict__ da_part) {
   constexpr int kF = 32 * HS, kW = wh_stride<HS>();
   extern __shared__ float sm[];
   const int N = ga.N, nnz = ga.nnz, b = blockIdx.x, h0 = HS * blockIdx.y;
@@ -453,12 +454,16 @@ __global__ void __launch_bounds__(32 * HS) attn_bwd_kernel(GraphArgs ga, const f
     const float y = Y[ge];
     const float g = dXn[ge] * (y > 0.f ? 1.f : expf(y));
     dy[(e / kF) * kW + e % kF] = g;
-    dY[ge] = g;
     wh[(e / kF) * kW + e % kF] = Wh[ge];
   }
   for (int e = threadIdx.x; e < N * 16; e += kF) ss[e] = S[(size_t)b * N * 16 + e];
   __syncthreads();
   const float* alb = alpha + (size_t)b * nnz * 8;
+  {
+    float sb = 0.f;
+    for (int i = 0; i < N; ++i) sb += dy[i * kW + threadIdx.x];
+    db_part[(size_t)b * 256 + 32 * h0 + threadIdx.x] = sb;
+  }
   // node i, head h: dalpha over i's edges, softmax and LeakyReLU backward
   for (int t = threadIdx.x; t < N * HS; t += kF) {
     const int i = t % N, hl = t / N, h = h0 + hl;
@@ -635,7 +640,7 @@ __global__ void adam_kernel(size_t n, float* __restrict__ w, const float* __rest
 struct Layout {
   size_t X[9];                            // X[0]: features [B*N][F]; X[l]: layer l's input [B*N][256]
   size_t Wh[8], Y[8], S[8], alpha[8];     // per layer
-  size_t gmean, colmean, z1, logits, dlog, dz1, dvpre, hid, terms, dgmean, dpol, dXa, dXb, dWh, dY, dapart;
+  size_t gmean, colmean, z1, logits, dlog, dz1, dvpre, hid, terms, dgmean, dpol, dXa, dXb, dWh, dbpart, dapart;
   size_t total;
 };
 
@@ -672,7 +677,7 @@ Layout layout(int game, int B) {
   o.dXa = take(node_vec);
   o.dXb = take(node_vec);
   o.dWh = take(node_vec);
-  o.dY = take(node_vec);
+  o.dbpart = take((size_t)B * 256);
   o.dapart = take((size_t)B * 512);
   o.total = p;
   return o;
@@ -800,11 +805,11 @@ cudaError_t loss_and_grad(State& st, const float* w, const int8_t* boards, const
   auto attn_bwd = [&](int l, const float* dX) {
     if (split_heads)
       attn_bwd_kernel<2><<<dim3(B, 4), 64, attn_bwd_smem<2>(N, sh.nnz), s>>>(
-          ga, dX, ar + o.Y[l], ar + o.Wh[l], ar + o.S[l], ar + o.alpha[l], w + t.a[l], ar + o.dWh, ar + o.dY,
+          ga, dX, ar + o.Y[l], ar + o.Wh[l], ar + o.S[l], ar + o.alpha[l], w + t.a[l], ar + o.dWh, ar + o.dbpart,
           ar + o.dapart);
     else
       attn_bwd_kernel<8><<<dim3(B, 1), 256, attn_bwd_smem<8>(N, sh.nnz), s>>>(
-          ga, dX, ar + o.Y[l], ar + o.Wh[l], ar + o.S[l], ar + o.alpha[l], w + t.a[l], ar + o.dWh, ar + o.dY,
+          ga, dX, ar + o.Y[l], ar + o.Wh[l], ar + o.S[l], ar + o.alpha[l], w + t.a[l], ar + o.dWh, ar + o.dbpart,
           ar + o.dapart);
   };
 
@@ -848,7 +853,7 @@ cudaError_t loss_and_grad(State& st, const float* w, const int8_t* boards, const
   for (int l = L - 1; l >= 0; --l) {
     const int Fl = l ? kHidden : sh.features;
     attn_bwd(l, dX);
-    GZ_TRY(colsum(ws, ar + o.dY, rowsN, kHidden, kHidden, g + t.b[l], false, s));
+    GZ_TRY(colsum(ws, ar + o.dbpart, B, kHidden, kHidden, g + t.b[l], false, s));
     GZ_TRY(colsum(ws, ar + o.dapart, B, 512, 512, g + t.a[l], false, s));
     GZ_TRY(gemm(ws, Fl, kHidden, rowsN, ar + o.X[l], Fl, true, ar + o.dWh, kHidden, false, g + t.W[l], kHidden, false,
                 s));
