@@ -26,8 +26,7 @@ namespace {
 constexpr int kThreads = 256;  // one thread per hidden column
 
 template <int G> struct SimtCfg;
-template <> struct SimtCfg<kTicTacToe> { static constexpr int GPC = 1; };  // graphs per CTA
-template <> struct SimtCfg<kConnect4> { static constexpr int GPC = 1; };
+template <> struct SimtCfg<kConnect4> { static constexpr int GPC = 1; };  // graphs per CTA (TicTacToe: gat_simt_ttt.cu)
 template <> struct SimtCfg<kChess> { static constexpr int GPC = 1; };
 
 template <int G> struct SimtSmem {

@@ -700,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_tc_c4_kernel(TcParams p) {
         // stop is collective, at the next layer's start.
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          const int h = 4 * g + t, b = t & 1;
+          const int b = t & 1;
           // ---- P1: Wh^h (fp32) -> fp16 copy as the gather's B operand ----
           if (t == 0 || t == 2) {  // the block of heads t, t + 1 is complete
             wok = mbar_wait(t == 0 ? acc_a : acc_b, lph, abort_flag, kWaitLimitNs) && wok;
