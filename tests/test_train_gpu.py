@@ -258,3 +258,46 @@ def test_data_parallel_step_matches_one_gpu(cuda, kind):
     # gradient can move by a different fraction of the learning rate:
     # allow 1 % of lr per step (measured on two B200s: 4.3e-6)
     assert np.abs(out[0] - w).max() < 0.01 * cfg.learning_rate * 2
+
+
+@pytest.mark.parametrize("prec,mode", [(gz.PREC_AUTO, "fp16"), (gz.PREC_BF16, "bf16")])
+def test_tensor_core_forward_after_training_follows_its_rounding_model(cuda, prec, mode):
+    """One Adam step moves every weight coherently by about lr, and on such
+    weights the Connect4 value output is sensitive enough that the 16-bit
+    operand formats alone exceed 1e-3 (measured: fp16 2.1e-3, bf16 6.3e-3 on
+    these positions; the synthetic test weights are bf16-exact and stay near
+    1e-4).  The kernel must still match the CPU rounding simulation of its
+    formats (tests/rounding_sim.py) on exactly those weights: with fp16
+    (rounded to nearest) the outputs within 3e-4 of the simulated ones (fp32
+    accumulation and hardware exponentials against exact arithmetic); with
+    bf16 (stochastically rounded, other random bits than the simulation's)
+    the error from the oracle within 1.5 times the simulation's worst over
+    three seeds.  The fp32 kernel stays within 1e-4 of the oracle."""
+    from rounding_sim import MODES, gat_forward_rounded, simulated_error
+    from helpers import torch_features
+
+    game, n = gz.CONNECT4, 8
+    w = gz.synth_weights(game, seed=0x6A5A)
+    boards, side = gz.synth_positions(game, n, seed=0x6A5A + 1)
+    d = dev(boards, side, np.full((n, 7), 1.0 / 7, np.float32), np.zeros(n, np.float32))
+    net = gz.Net(game, precision=prec, max_batch=n)
+    net.load_weights(w)
+    net.train_step(*d, n, gz.train_config(learning_rate=1e-3))
+    w2 = net.save_weights()
+    pi, v = net.predict_host(boards, side)
+    opi, ov = oracle.gat_forward(game, w2, boards, side)
+    if mode == "fp16":
+        rp, col = gz.game_graph(game)
+        spi, sv = gat_forward_rounded(game, gz.game_shape(game), torch_features(game, boards, side).numpy(), rp, col,
+                                      w2, seed=0, **MODES["connect4"][mode])
+        assert np.abs(pi - spi).max() < 3e-4 and np.abs(v - sv).max() < 3e-4, (np.abs(pi - spi).max(),
+                                                                              np.abs(v - sv).max())
+    else:
+        sim = simulated_error(game, w2, boards, side, opi, ov, **MODES["connect4"][mode])
+        err = max(float(np.abs(pi - opi).max()), float(np.abs(v - ov).max()))
+        assert err <= 1.5 * sim, (err, sim)
+    n32 = gz.Net(game, precision=gz.PREC_FP32, max_batch=n)
+    n32.load_weights(w2)
+    f32pi, f32v = n32.predict_host(boards, side)
+    assert np.abs(f32pi - opi).max() < 1e-4 and np.abs(f32v - ov).max() < 1e-4
+    net.check()
