@@ -56,6 +56,7 @@
 
 #include "gz_games.h"
 #include "gz_internal.h"
+#include "gz_round.h"
 #include "gz_sm100.h"
 
 namespace gz {
@@ -917,8 +918,9 @@ __global__ void pack_c4_kernel(const float* __restrict__ w, uint8_t* __restrict_
     const int r = t / 64, kk = t % 64;  // packed row, K within chunk
     const int f = 32 * packed_row_head(r >> 5) + (r & 31);
     const int k = kin(kk);
-    const float x = k < fin ? W[(size_t)k * kHidden + f] : 0.f;
-    *(uint16_t*)(dst + sw128_offset(r, kk)) = OpType<OpT>::bits(x);
+    const size_t i = (size_t)k * kHidden + f;
+    const float x = k < fin ? W[i] : 0.f;
+    *(uint16_t*)(dst + sw128_offset(r, kk)) = weight_bits_sr<OpT>(x, (uint32_t)(C4Off::W(layer) + i));
   }
   for (int t = threadIdx.x; t < 16 * 64; t += blockDim.x) {
     const int j = t / 64, kk = t % 64;  // score column j = 2h + v

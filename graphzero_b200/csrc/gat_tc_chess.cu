@@ -39,6 +39,7 @@
 
 #include "gz_games.h"
 #include "gz_internal.h"
+#include "gz_round.h"
 #include "gz_sm100.h"
 
 namespace gz {
@@ -889,8 +890,9 @@ __global__ void pack_chess_kernel(const float* __restrict__ w, uint8_t* __restri
     uint8_t* dst = out + (size_t)kLayerChunks * kWChunk + (size_t)c * kPolChunk;
     for (int t = threadIdx.x; t < kPN * 64; t += blockDim.x) {
       const int n = t / 64, kk = t % 64, k = x_feature(c, kk);
-      const float x = n < kP ? w[ChOff::w_pi + (size_t)k * kP + n] : 0.f;
-      *(uint16_t*)(dst + sw128_offset(n, kk)) = OpType<OpT>::bits(x);
+      const size_t i = ChOff::w_pi + (size_t)k * kP + n;
+      const float x = n < kP ? w[i] : 0.f;
+      *(uint16_t*)(dst + sw128_offset(n, kk)) = weight_bits_sr<OpT>(x, (uint32_t)i);
     }
     return;
   }
@@ -902,8 +904,9 @@ __global__ void pack_chess_kernel(const float* __restrict__ w, uint8_t* __restri
   uint8_t* dst = out + (size_t)chunk * kWChunk;
   for (int t = threadIdx.x; t < 256 * 64; t += blockDim.x) {
     const int n = t / 64, kk = t % 64, k = layer == 0 ? kk : x_feature(c, kk);
-    const float x = k < fin ? W[(size_t)k * 256 + proj_feature(n)] : 0.f;
-    *(uint16_t*)(dst + sw128_offset(n, kk)) = OpType<OpT>::bits(x);
+    const size_t i = (size_t)k * 256 + proj_feature(n);
+    const float x = k < fin ? W[i] : 0.f;
+    *(uint16_t*)(dst + sw128_offset(n, kk)) = weight_bits_sr<OpT>(x, (uint32_t)(ChOff::W(layer) + i));
   }
   for (int t = threadIdx.x; t < 16 * 64; t += blockDim.x) {
     const int j = t / 64, kk = t % 64, k = layer == 0 ? kk : x_feature(c, kk), h = j >> 1, v = j & 1;

@@ -35,6 +35,7 @@
 
 #include "gz_games.h"
 #include "gz_internal.h"
+#include "gz_round.h"
 #include "gz_sm100.h"
 
 namespace gz {
@@ -481,13 +482,15 @@ __global__ void pack_resnet_kernel(const float* __restrict__ w, uint8_t* __restr
     c = (chunk - 9) % 2;
   }
   const int cin = cv == 0 ? kResInPlanes : kC;
-  const float* W = w + (cv == 0 ? RL.stem_w : (cv & 1) ? RL.conv1_w[(cv - 1) / 2] : RL.conv2_w[(cv - 1) / 2]);
+  const size_t wbase = cv == 0 ? RL.stem_w : (cv & 1) ? RL.conv1_w[(cv - 1) / 2] : RL.conv2_w[(cv - 1) / 2];
+  const float* W = w + wbase;
   const int ky = tap_dy(t) + 1, kx = tap_dx(t) + 1;
   uint8_t* dst = out + (size_t)chunk * kWChunk;
   for (int i = threadIdx.x; i < 128 * 64; i += blockDim.x) {
     const int co = i / 64, kk = i % 64, ci = c * 64 + kk;
-    const float x = ci < cin ? W[(((size_t)co * 3 + ky) * 3 + kx) * cin + ci] : 0.f;
-    *(uint16_t*)(dst + sw128_offset(co, kk)) = ResOp<OpT>::bits(x);
+    const size_t e = (((size_t)co * 3 + ky) * 3 + kx) * cin + ci;
+    const float x = ci < cin ? W[e] : 0.f;
+    *(uint16_t*)(dst + sw128_offset(co, kk)) = weight_bits_sr<OpT>(x, (uint32_t)(wbase + e));
   }
   if (chunk < kConvs) {  // folded BN of conv `chunk`
     const int k = chunk;

@@ -12,7 +12,10 @@ first ELU on, so the softmax works in base 2):
   X_l        the projection's A operand: bf16 or fp16, stochastically
              rounded ("sr") or rounded to nearest ("rn"); layer 0's one-hot
              features are exact
-  W_l        the B operand: rounded to nearest in the operand format
+  W_l        the B operand: stochastically rounded in the operand format
+             by a hash of each weight's index in the blob (`round_weights`,
+             the pack kernels' rule, bit for bit); `wround="rn"` models the
+             earlier kernels, which rounded weights to nearest
   W_l a      attention-score weights as a high part plus the rounding of the
              remainder (two MMA columns) -- fp32-level accurate
   Wh         the gather's B operand: fp16, rounded to nearest
@@ -66,6 +69,53 @@ def round_fp16(x: np.ndarray, mode: str, rng: np.random.Generator | None = None)
     return np.where(take & (d != 0), od, hd)
 
 
+def mix32(i: np.ndarray) -> np.ndarray:
+    """The "lowbias32" integer hash (Chris Wellons), on uint32 arrays."""
+    x = np.asarray(i, dtype=np.uint32).copy()
+    x ^= x >> np.uint32(16)
+    x *= np.uint32(0x7FEB352D)
+    x ^= x >> np.uint32(15)
+    x *= np.uint32(0x846CA68B)
+    x ^= x >> np.uint32(16)
+    return x
+
+
+def _bits16(x32: np.ndarray, fmt: str) -> np.ndarray:
+    if fmt == "fp16":
+        return x32.astype(np.float16).view(np.uint16)
+    u = x32.view(np.uint32).astype(np.uint64)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) & 0xFFFF).astype(np.uint16)
+
+
+def _value16(b: np.ndarray, fmt: str) -> np.ndarray:
+    if fmt == "fp16":
+        return b.view(np.float16).astype(np.float64)
+    return (b.astype(np.uint32) << np.uint32(16)).view(np.float32).astype(np.float64)
+
+
+def round_weights(x: np.ndarray, fmt: str, index: np.ndarray) -> np.ndarray:
+    """The pack kernels' weight rounding (graphzero_b200/csrc/gz_round.h):
+    n = x to nearest in `fmt`; where n != x the other neighbour o replaces it
+    when |x - n| 2^32 > mix32(index) |o - n|, i.e. with probability
+    |x - n| / |o - n|.  `index` is each weight's offset in the blob."""
+    if fmt == "exact":
+        return np.asarray(x, dtype=np.float64)
+    x32 = np.ascontiguousarray(x, dtype=np.float32)
+    nb = _bits16(x32, fmt)
+    n = _value16(nb, fmt)
+    xd = x32.astype(np.float64)
+    up = xd > n
+    zero = (nb & 0x7FFF) == 0
+    away = up != ((nb & 0x8000) != 0)
+    ob = np.where(zero, np.where(up, 0x0001, 0x8001),
+                  np.where(away, nb.astype(np.int32) + 1, nb.astype(np.int32) - 1)).astype(np.uint16)
+    o = _value16(ob, fmt)
+    with np.errstate(invalid="ignore"):
+        take = (np.abs(xd - n) * 4294967296.0 > mix32(np.broadcast_to(index, x32.shape)).astype(np.float64) * np.abs(o - n))
+    keep = (n == xd) | ~np.isfinite(n)
+    return np.where(keep | ~take, n, o)
+
+
 def round_op(x: np.ndarray, fmt: str, mode: str, rng=None) -> np.ndarray:
     if fmt == "exact":
         return np.asarray(x, dtype=np.float64)
@@ -74,33 +124,44 @@ def round_op(x: np.ndarray, fmt: str, mode: str, rng=None) -> np.ndarray:
     return round_fp16(x, mode, rng)
 
 
-def _views(game: int, shape, w: np.ndarray) -> dict:
+def _views(game: int, shape, w: np.ndarray, offsets: dict | None = None) -> dict:
+    """Named float64 views of a GAT weight blob; `offsets`, when given, gets
+    each tensor's blob index array (same shape)."""
     o, p = {}, 0
-    for l in range(shape.layers):
-        fin = shape.features if l == 0 else 256
-        for k, sh in ((f"W{l}", (fin, 256)), (f"b{l}", (256,)), (f"a{l}", (8, 2, 32))):
-            o[k] = w[p:p + int(np.prod(sh))].reshape(sh).astype(np.float64)
-            p += int(np.prod(sh))
     P = shape.policy_per_node
-    for k, sh in (("w_pi", (256, P)), ("b_pi", (P,)), ("W_v1", (256, 64)), ("b_v1", (64,)), ("w_v2", (64,)),
-                  ("b_v2", (1,))):
-        o[k] = w[p:p + int(np.prod(sh))].reshape(sh).astype(np.float64)
-        p += int(np.prod(sh))
+    specs = [(k, sh) for l in range(shape.layers)
+             for k, sh in ((f"W{l}", (shape.features if l == 0 else 256, 256)), (f"b{l}", (256,)), (f"a{l}", (8, 2, 32)))]
+    specs += [("w_pi", (256, P)), ("b_pi", (P,)), ("W_v1", (256, 64)), ("b_v1", (64,)), ("w_v2", (64,)), ("b_v2", (1,))]
+    for k, sh in specs:
+        m = int(np.prod(sh))
+        o[k] = w[p:p + m].reshape(sh).astype(np.float64)
+        if offsets is not None:
+            offsets[k] = (p + np.arange(m, dtype=np.int64)).reshape(sh)
+        p += m
     return o
 
 
 def gat_forward_rounded(game: int, shape, features: np.ndarray, rowptr: np.ndarray, col: np.ndarray,
                         w: np.ndarray, op: str = "bf16", act: str = "sr", gather: str = "fp16",
-                        last: str = "fp16", seed: int = 0) -> tuple[np.ndarray, np.ndarray]:
+                        last: str = "fp16", seed: int = 0, wround: str = "sr") -> tuple[np.ndarray, np.ndarray]:
     """The GAT forward with the tensor-core kernels' roundings.
 
     features: [B][N][F] one-hot node features (exact).  op: operand format of
     the projection ("bf16", "fp16" or "exact"); act: "sr" or "rn" for the
     activations written as the next projection's operand; gather: format of
     the softmax numerators and Wh in the gather ("fp16" or "exact"); last:
-    "fp16" or "fp32" pooling input.  Returns (pi [B][A], v [B])."""
+    "fp16" or "fp32" pooling input; wround: the weights' rounding, "sr" (the
+    pack kernels' hashed stochastic rounding) or "rn".  Returns (pi [B][A],
+    v [B])."""
     rng = np.random.default_rng(seed)
-    o = _views(game, shape, w)
+    idx = {}
+    o = _views(game, shape, w, idx)
+
+    def wr(k):
+        if wround == "rn" or op == "exact":
+            return round_op(o[k].astype(np.float32), op, "rn")
+        return round_weights(o[k].astype(np.float32), op, idx[k])
+
     B, N, _ = features.shape
     deg = np.diff(rowptr)
     src = np.repeat(np.arange(N), deg)
@@ -111,7 +172,7 @@ def gat_forward_rounded(game: int, shape, features: np.ndarray, rowptr: np.ndarr
     g_round = (lambda x: round_fp16(x, "rn")) if gather == "fp16" else (lambda x: np.asarray(x, np.float64))
     for l in range(shape.layers):
         Wl = o[f"W{l}"]
-        Wr = round_op(Wl.astype(np.float32), op, "rn")
+        Wr = wr(f"W{l}")
         Wa = np.einsum("khf,hvf->khv", Wl.reshape(-1, 8, 32), o[f"a{l}"])  # [K][8][2]
         if l == 0:
             Wa = Wa * LOG2E
@@ -133,10 +194,10 @@ def gat_forward_rounded(game: int, shape, features: np.ndarray, rowptr: np.ndarr
     if shape.nodes == 64:
         # chess: the policy is an MMA on the last activations as the
         # projection operand (format `op`, mode `act`, or exact with
-        # `last="fp32"`) and W_pi rounded to nearest; the value head pools
+        # `last="fp32"`) and W_pi rounded like the W_l; the value head pools
         # the fp32 activations
         Xp = X if last == "fp32" else round_op(X.astype(np.float32), op, act, rng)
-        Wp = round_op(o["w_pi"].astype(np.float32), op, "rn") if last != "fp32" else o["w_pi"]
+        Wp = wr("w_pi") if last != "fp32" else o["w_pi"]
         lgp = (Xp * LN2 @ Wp + o["b_pi"]).reshape(B, -1)
         Xv = X
     else:
@@ -157,10 +218,11 @@ def gat_forward_rounded(game: int, shape, features: np.ndarray, rowptr: np.ndarr
 
 
 def resnet_forward_rounded(w: np.ndarray, boards: np.ndarray, side: np.ndarray, op: str = "fp16",
-                           resid: str = "op") -> tuple[np.ndarray, np.ndarray]:
+                           resid: str = "op", wround: str = "sr") -> tuple[np.ndarray, np.ndarray]:
     """The Connect4 ResNet tower with the tensor-core kernel's roundings:
-    every convolution's input activations and weights rounded to nearest in
-    `op` ("bf16", "fp16", "exact"); BN folded in fp32 (exact here); the
+    every convolution's input activations rounded to nearest in `op`
+    ("bf16", "fp16", "exact") and its weights by the pack kernel's hashed
+    stochastic rounding (`wround="sr"`) or to nearest ("rn"); BN folded in fp32 (exact here); the
     residual read back from the rounded block input (`resid="op"`) or kept
     exact (`"exact"`); heads from the last convolution's exact output.
     Reference semantics: networks/resnet/resnet.cu:506-667."""
@@ -182,8 +244,15 @@ def resnet_forward_rounded(w: np.ndarray, boards: np.ndarray, side: np.ndarray, 
     sd = torch.tensor(side.astype(np.int64)).view(-1, 1, 1)
     x = torch.stack([(b == sd), (b == -sd), (sd == 1).expand_as(b)], 1).double()
 
+    def rnd_w(k):
+        if op == "exact" or wround == "rn":
+            return rnd(t(k))
+        p, sh = o[k]
+        m = int(np.prod(sh))
+        return torch.tensor(round_weights(w[p:p + m], op, p + np.arange(m, dtype=np.int64)).reshape(sh))
+
     def conv_bn(x, kw, kb):
-        wt = rnd(t(kw)).permute(0, 3, 1, 2)
+        wt = rnd_w(kw).permute(0, 3, 1, 2)
         y = torch.nn.functional.conv2d(rnd(x), wt, padding=1)
         g, be, mu, var = t(kb)
         sc = g / torch.sqrt(var + 1e-5)

@@ -37,3 +37,26 @@ def test_rounding_helpers_match_the_formats():
         r = f(y, "sr", rng)
         lo, hi = r.min(), r.max()
         assert lo == 1.0 and hi > 1.0 and abs(r.mean() - float(y[0])) < 4 * (hi - lo) / np.sqrt(y.size)
+
+
+def test_weight_rounding_is_unbiased_and_exact_on_the_grid():
+    """The pack kernels' weight rounding (hashed stochastic): values already
+    in the format stay; a value between two neighbours lands on one of them,
+    on the far one in proportion to its distance; zero stays zero."""
+    from rounding_sim import round_weights
+
+    idx = np.arange(40000, dtype=np.int64)
+    for fmt, step in (("fp16", 2.0 ** -10), ("bf16", 2.0 ** -7)):
+        y = np.full(idx.size, 1.0 + step / 4, np.float32)
+        r = round_weights(y, fmt, idx)
+        assert set(np.unique(r)) == {1.0, 1.0 + step}
+        assert abs(r.mean() - float(y[0])) < 4 * step * np.sqrt(3 / 16 / y.size)
+        neg = round_weights(-y, fmt, idx)
+        assert (neg == -r).all()  # same hash, mirrored value: the mirrored choice
+        g = round_fp16(np.random.default_rng(2).normal(size=4096).astype(np.float32), "rn")
+        g = round_bf16(g.astype(np.float32), "rn") if fmt == "bf16" else g
+        assert (round_weights(g.astype(np.float32), fmt, idx[:4096]) == g).all()
+    assert (round_weights(np.zeros(8, np.float32), "fp16", idx[:8]) == 0).all()
+    tiny = np.full(idx.size, 2.0 ** -26, np.float32)  # a quarter of fp16's smallest subnormal
+    r = round_weights(tiny, "fp16", idx)
+    assert set(np.unique(r)) == {0.0, 2.0 ** -24} and abs(r.mean() / 2.0 ** -26 - 1) < 0.05
