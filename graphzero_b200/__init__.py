@@ -78,6 +78,12 @@ _SIGS = {
     "gz_synth_positions": (C.c_int, [C.c_int, C.c_uint64, C.c_uint64, C.c_int, _i8p, _i8p]),
     "gz_chess_legal_count": (C.c_int, [_i8p, C.c_int, C.POINTER(C.c_int)]),
     "gz_chess_perft": (C.c_int, [_i8p, C.c_int, C.c_int, C.POINTER(C.c_uint64)]),
+    "gz_chess_legal_actions": (C.c_int, [_i8p, C.c_int, C.POINTER(C.c_int16), C.POINTER(C.c_int)]),
+    "gz_chess_valid_moves": (C.c_int, [_i8p, C.c_int, C.POINTER(C.c_uint8)]),
+    "gz_chess_next_state": (C.c_int, [_i8p, C.c_int, C.c_int, _i8p, C.POINTER(C.c_int)]),
+    "gz_chess_ended": (C.c_int, [_i8p, C.c_int, C.POINTER(C.c_int)]),
+    "gz_synth_positions_device": (C.c_int, [C.c_int, C.c_uint64, C.c_uint64, C.c_int, _vp, _vp, _vp]),
+    "gz_chess_legal_actions_device": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp, _vp]),
     "gz_net_create": (C.c_int, [C.POINTER(NetConfig), C.c_int, C.POINTER(_vp)]),
     "gz_net_destroy": (C.c_int, [_vp]),
     "gz_net_weight_count": (C.c_size_t, [_vp]),
@@ -272,6 +278,66 @@ def chess_perft(board: np.ndarray, side: int, depth: int) -> int:
     r = C.c_uint64()
     _check(_lib.gz_chess_perft(_ptr(b, C.c_int8), side, depth, C.byref(r)))
     return r.value
+
+
+CHESS_ACTIONS = 64 * 73
+
+
+def chess_legal_actions(board: np.ndarray, side: int) -> np.ndarray:
+    """Action indices (from * 73 + t) of the legal moves, in generation order."""
+    b = np.ascontiguousarray(board, np.int8)
+    out = np.empty(256, np.int16)
+    r = C.c_int()
+    _check(_lib.gz_chess_legal_actions(_ptr(b, C.c_int8), side, _ptr(out, C.c_int16), C.byref(r)))
+    return out[:r.value].copy()
+
+
+def chess_valid_moves(board: np.ndarray, side: int) -> np.ndarray:
+    b = np.ascontiguousarray(board, np.int8)
+    v = np.zeros(CHESS_ACTIONS, np.uint8)
+    _check(_lib.gz_chess_valid_moves(_ptr(b, C.c_int8), side, _ptr(v, C.c_uint8)))
+    return v
+
+
+def chess_next_state(board: np.ndarray, side: int, action: int) -> tuple[np.ndarray, int]:
+    b = np.ascontiguousarray(board, np.int8)
+    nb = np.empty(66, np.int8)
+    ns = C.c_int()
+    _check(_lib.gz_chess_next_state(_ptr(b, C.c_int8), side, action, _ptr(nb, C.c_int8), C.byref(ns)))
+    return nb, ns.value
+
+
+def chess_ended(board: np.ndarray, side: int) -> int:
+    """0 while the side to move has a legal move, -1 checkmated, 2 stalemate."""
+    b = np.ascontiguousarray(board, np.int8)
+    r = C.c_int()
+    _check(_lib.gz_chess_ended(_ptr(b, C.c_int8), side, C.byref(r)))
+    return r.value
+
+
+def synth_positions_device(game: int, n: int, seed: int = 0x6A5A, first: int = 0, device: int = 0, stream=None):
+    """synth_positions made on the GPU: (boards, side) as torch int8 tensors on
+    cuda:device, byte for byte what synth_positions returns."""
+    import torch
+    s = game_shape(game)
+    boards = torch.empty((n, s.board_bytes), dtype=torch.int8, device=f"cuda:{device}")
+    side = torch.empty(n, dtype=torch.int8, device=boards.device)
+    with torch.cuda.device(boards.device):
+        _check(_lib.gz_synth_positions_device(game, seed, first, n, _dev(boards), _dev(side), _stream(stream)))
+    return boards, side
+
+
+def chess_legal_actions_device(boards, side, stream=None):
+    """Legal action lists of chess positions on the GPU (torch int8 tensors
+    [n][66] and [n]): (actions int16 [n][256], -1 padded; counts int32 [n])."""
+    import torch
+    n = boards.shape[0]
+    actions = torch.empty((n, 256), dtype=torch.int16, device=boards.device)
+    counts = torch.empty(n, dtype=torch.int32, device=boards.device)
+    with torch.cuda.device(boards.device):
+        _check(_lib.gz_chess_legal_actions_device(_dev(boards.contiguous()), _dev(side.contiguous()), n, _dev(actions),
+                                                  _dev(counts), _stream(stream)))
+    return actions, counts
 
 
 def synth_positions(game: int, n: int, seed: int = 0x6A5A, first: int = 0) -> tuple[np.ndarray, np.ndarray]:

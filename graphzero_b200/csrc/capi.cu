@@ -326,6 +326,62 @@ gz_status gz_chess_perft(const int8_t* board, int side, int depth, uint64_t* nod
   return GZ_OK;
 }
 
+gz_status gz_chess_legal_actions(const int8_t* board, int side, int16_t* actions, int* count) {
+  if (!board || !actions || !count || (side != 1 && side != -1)) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  chess::Pos p;
+  chess::from_record(board, side, p);
+  chess::Move ms[256];
+  const int c = chess::legal_moves(p, ms);
+  for (int k = 0; k < c; ++k) actions[k] = (int16_t)chess::encode_action(ms[k]);
+  *count = c;
+  return GZ_OK;
+}
+
+gz_status gz_chess_valid_moves(const int8_t* board, int side, uint8_t* valid) {
+  if (!board || !valid || (side != 1 && side != -1)) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  chess::Pos p;
+  chess::from_record(board, side, p);
+  chess::Move ms[256];
+  const int c = chess::legal_moves(p, ms);
+  memset(valid, 0, 64 * 73);
+  for (int k = 0; k < c; ++k) valid[chess::encode_action(ms[k])] = 1;
+  return GZ_OK;
+}
+
+gz_status gz_chess_next_state(const int8_t* board, int side, int action, int8_t* next_board, int* next_side) {
+  if (!board || !next_board || !next_side || (side != 1 && side != -1)) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  chess::Pos p;
+  chess::from_record(board, side, p);
+  chess::Move m;
+  if (!chess::find_action(p, action, &m)) return fail(GZ_ERR_INVALID_ARG, "illegal action %d", action);
+  chess::apply(p, m);
+  chess::to_record(p, next_board);
+  *next_side = p.side;
+  return GZ_OK;
+}
+
+gz_status gz_chess_ended(const int8_t* board, int side, int* result) {
+  if (!board || !result || (side != 1 && side != -1)) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  chess::Pos p;
+  chess::from_record(board, side, p);
+  *result = chess::outcome(p);
+  return GZ_OK;
+}
+
+gz_status gz_synth_positions_device(int game, uint64_t seed, uint64_t first, int n, int8_t* d_boards, int8_t* d_side,
+                                    void* stream) {
+  if (!valid_game(game) || n < 0 || (n > 0 && (!d_boards || !d_side))) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  GZ_CUDA(launch_synth_positions(game, seed, first, n, d_boards, d_side, (cudaStream_t)stream));
+  return GZ_OK;
+}
+
+gz_status gz_chess_legal_actions_device(const int8_t* d_boards, const int8_t* d_side, int n, int16_t* d_actions,
+                                        int32_t* d_counts, void* stream) {
+  if (n < 0 || (n > 0 && (!d_boards || !d_side || !d_actions || !d_counts))) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  GZ_CUDA(launch_chess_legal(d_boards, d_side, n, d_actions, d_counts, (cudaStream_t)stream));
+  return GZ_OK;
+}
+
 gz_status gz_net_create(const gz_net_config* cfg, int device, gz_net** out) {
   if (!cfg || !out) return fail(GZ_ERR_INVALID_ARG, "null argument");
   *out = nullptr;

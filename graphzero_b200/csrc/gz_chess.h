@@ -1,5 +1,7 @@
-// Chess rules for the position generator (host code): legal move
-// generation, move application, perft, and random legal playouts.
+// Chess rules: legal move generation, move application, the reference's
+// action indices, game end, perft and random legal playouts.  Everything but
+// perft compiles for host and device alike (GZ_HDI) and behaves identically
+// on both.
 //
 // Record layout (66 bytes, the network's input): squares 0..63 = rank * 8 +
 // file (a1 = 0, h8 = 63), piece codes +1..+6 = white P N B R Q K and
@@ -37,12 +39,12 @@ struct Move {
   int8_t from, to, promo;  // promo: 0 or the promoted piece type (unsigned)
 };
 
-inline int file_of(int s) { return s & 7; }
-inline int rank_of(int s) { return s >> 3; }
-inline int sgn(int v) { return (v > 0) - (v < 0); }
+GZ_HDI int file_of(int s) { return s & 7; }
+GZ_HDI int rank_of(int s) { return s >> 3; }
+GZ_HDI int sgn(int v) { return (v > 0) - (v < 0); }
 
-inline void start_pos(Pos& p) {
-  static const int8_t back[8] = {kRook, kKnight, kBishop, kQueen, kKing, kBishop, kKnight, kRook};
+GZ_HDI void start_pos(Pos& p) {
+  const int8_t back[8] = {kRook, kKnight, kBishop, kQueen, kKing, kBishop, kKnight, kRook};
   memset(p.sq, 0, 64);
   for (int f = 0; f < 8; ++f) {
     p.sq[f] = back[f];
@@ -55,68 +57,78 @@ inline void start_pos(Pos& p) {
   p.side = 1;
 }
 
-inline void to_record(const Pos& p, int8_t* rec) {
+GZ_HDI void to_record(const Pos& p, int8_t* rec) {
   memcpy(rec, p.sq, 64);
   rec[64] = (int8_t)p.castle;
   rec[65] = p.ep;
 }
 
-inline void from_record(const int8_t* rec, int side, Pos& p) {
+GZ_HDI void from_record(const int8_t* rec, int side, Pos& p) {
   memcpy(p.sq, rec, 64);
   p.castle = (uint8_t)rec[64] & 0xF;
   p.ep = rec[65];
   p.side = (int8_t)(side >= 0 ? 1 : -1);
 }
 
-// Offsets as (file, rank) steps.
-constexpr int kKnightD[8][2] = {{1, 2}, {2, 1}, {2, -1}, {1, -2}, {-1, -2}, {-2, -1}, {-2, 1}, {-1, 2}};
-constexpr int kKingD[8][2] = {{1, 0}, {1, 1}, {0, 1}, {-1, 1}, {-1, 0}, {-1, -1}, {0, -1}, {1, -1}};
-constexpr int kDiagD[4][2] = {{1, 1}, {-1, 1}, {-1, -1}, {1, -1}};
-constexpr int kLineD[4][2] = {{1, 0}, {0, 1}, {-1, 0}, {0, -1}};
+// Step k of each piece as (file, rank) offsets: knights and kings k = 0..7,
+// diagonal rays k = 0..3, orthogonal rays k = 0..3 (functions rather than
+// tables, so device code needs no table in global memory).
+GZ_HDI int knight_df(int k) { return (int)((0x12211221u >> (4 * k)) & 0xF) * ((k & 4) ? -1 : 1); }
+GZ_HDI int knight_dr(int k) { return knight_df((k + 2) & 7); }
+GZ_HDI int king_df(int k) { return k == 2 || k == 6 ? 0 : (k == 0 || k == 1 || k == 7) ? 1 : -1; }
+GZ_HDI int king_dr(int k) { return king_df((k + 6) & 7); }
+GZ_HDI int diag_df(int k) { return k == 0 || k == 3 ? 1 : -1; }
+GZ_HDI int diag_dr(int k) { return k < 2 ? 1 : -1; }
+GZ_HDI int line_df(int k) { return k == 0 ? 1 : k == 2 ? -1 : 0; }
+GZ_HDI int line_dr(int k) { return k == 1 ? 1 : k == 3 ? -1 : 0; }
 
-inline bool on_board(int f, int r) { return (unsigned)f < 8u && (unsigned)r < 8u; }
+GZ_HDI bool on_board(int f, int r) { return (unsigned)f < 8u && (unsigned)r < 8u; }
 
 // Is square s attacked by side `by` (+1 / -1)?
-inline bool attacked(const Pos& p, int s, int by) {
+GZ_HDI bool attacked(const Pos& p, int s, int by) {
   const int f = file_of(s), r = rank_of(s);
   // pawns of `by` attack diagonally forward (rank + by)
   for (int df = -1; df <= 1; df += 2) {
     const int pf = f + df, pr = r - by;
     if (on_board(pf, pr) && p.sq[pr * 8 + pf] == by * kPawn) return true;
   }
-  for (auto& d : kKnightD) {
-    const int nf = f + d[0], nr = r + d[1];
+  for (int k = 0; k < 8; ++k) {
+    const int nf = f + knight_df(k), nr = r + knight_dr(k);
     if (on_board(nf, nr) && p.sq[nr * 8 + nf] == by * kKnight) return true;
   }
-  for (auto& d : kKingD) {
-    const int nf = f + d[0], nr = r + d[1];
+  for (int k = 0; k < 8; ++k) {
+    const int nf = f + king_df(k), nr = r + king_dr(k);
     if (on_board(nf, nr) && p.sq[nr * 8 + nf] == by * kKing) return true;
   }
-  for (auto& d : kDiagD)
-    for (int nf = f + d[0], nr = r + d[1]; on_board(nf, nr); nf += d[0], nr += d[1]) {
+  for (int k = 0; k < 8; ++k) {  // diagonal rays, then orthogonal ones
+    const bool diag = k < 4;
+    const int df = diag ? diag_df(k) : line_df(k - 4), dr = diag ? diag_dr(k) : line_dr(k - 4);
+    const int slider = diag ? kBishop : kRook;
+    for (int nf = f + df, nr = r + dr; on_board(nf, nr); nf += df, nr += dr) {
       const int v = p.sq[nr * 8 + nf];
       if (v == 0) continue;
-      if (v == by * kBishop || v == by * kQueen) return true;
+      if (v == by * slider || v == by * kQueen) return true;
       break;
     }
-  for (auto& d : kLineD)
-    for (int nf = f + d[0], nr = r + d[1]; on_board(nf, nr); nf += d[0], nr += d[1]) {
-      const int v = p.sq[nr * 8 + nf];
-      if (v == 0) continue;
-      if (v == by * kRook || v == by * kQueen) return true;
-      break;
-    }
+  }
   return false;
 }
 
-inline int king_square(const Pos& p, int side) {
+GZ_HDI int king_square(const Pos& p, int side) {
   for (int s = 0; s < 64; ++s)
     if (p.sq[s] == side * kKing) return s;
   return -1;
 }
 
+GZ_HDI void clear_corner_right(Pos& p, int s) {
+  if (s == 7) p.castle &= ~0x1u;
+  if (s == 0) p.castle &= ~0x2u;
+  if (s == 63) p.castle &= ~0x4u;
+  if (s == 56) p.castle &= ~0x8u;
+}
+
 // Apply a (pseudo-)legal move in place.
-inline void apply(Pos& p, const Move& m) {
+GZ_HDI void apply(Pos& p, const Move& m) {
   const int me = p.side, v = p.sq[m.from], type = v * me;
   const int ep_capture = (type == kPawn && m.to == p.ep && p.sq[m.to] == 0) ? m.to - 8 * me : -1;
   p.sq[m.to] = m.promo ? (int8_t)(me * m.promo) : (int8_t)v;
@@ -135,27 +147,35 @@ inline void apply(Pos& p, const Move& m) {
   // castling rights: a king move clears its side's rights; anything leaving
   // or landing on a rook corner clears that corner's right
   if (type == kKing) p.castle &= me > 0 ? ~0x3u : ~0xCu;
-  for (int s : {(int)m.from, (int)m.to}) {
-    if (s == 7) p.castle &= ~0x1u;
-    if (s == 0) p.castle &= ~0x2u;
-    if (s == 63) p.castle &= ~0x4u;
-    if (s == 56) p.castle &= ~0x8u;
-  }
+  clear_corner_right(p, m.from);
+  clear_corner_right(p, m.to);
   p.ep = (type == kPawn && (m.to - m.from == 16 || m.from - m.to == 16)) ? (int8_t)((m.from + m.to) / 2) : (int8_t)-1;
   p.side = (int8_t)-me;
 }
 
-// Pseudo-legal moves of the side to move; returns the count (<= 256).
-inline int pseudo_moves(const Pos& p, Move* out) {
+// Pseudo-legal moves of the side to move, in a fixed order (squares
+// ascending; per pawn: push, double push, captures toward the lower then the
+// higher file, promotions Q R B N; knight and king steps k = 0..7, then
+// castling king side, queen side; sliders diagonal rays then orthogonal
+// ones).  Returns the count; `out` holds 256 and the list stops there
+// (reachable chess positions have far fewer; a record with more pieces than
+// a game can reach may hit the cap, and it keeps every write in bounds).
+GZ_HDI int pseudo_moves(const Pos& p, Move* out) {
   const int me = p.side;
   int n = 0;
-  auto add = [&](int from, int to, int promo) { out[n++] = Move{(int8_t)from, (int8_t)to, (int8_t)promo}; };
+  auto add = [&](int from, int to, int promo) {
+    if (n < 256) out[n++] = Move{(int8_t)from, (int8_t)to, (int8_t)promo};
+  };
   auto add_pawn = [&](int from, int to) {
     const int last = me > 0 ? 7 : 0;
-    if (rank_of(to) == last)
-      for (int pr : {kQueen, kRook, kBishop, kKnight}) add(from, to, pr);
-    else
+    if (rank_of(to) == last) {
+      add(from, to, kQueen);
+      add(from, to, kRook);
+      add(from, to, kBishop);
+      add(from, to, kKnight);
+    } else {
       add(from, to, 0);
+    }
   };
   for (int s = 0; s < 64; ++s) {
     const int v = p.sq[s];
@@ -176,9 +196,9 @@ inline int pseudo_moves(const Pos& p, Move* out) {
         if ((tv != 0 && sgn(tv) == -me) || t == p.ep) add_pawn(s, t);
       }
     } else if (type == kKnight || type == kKing) {
-      const auto& D = type == kKnight ? kKnightD : kKingD;
-      for (auto& d : D) {
-        const int nf = f + d[0], nr = r + d[1];
+      for (int k = 0; k < 8; ++k) {
+        const int nf = f + (type == kKnight ? knight_df(k) : king_df(k));
+        const int nr = r + (type == kKnight ? knight_dr(k) : king_dr(k));
         if (!on_board(nf, nr)) continue;
         const int tv = p.sq[nr * 8 + nf];
         if (tv == 0 || sgn(tv) == -me) add(s, nr * 8 + nf, 0);
@@ -198,8 +218,8 @@ inline int pseudo_moves(const Pos& p, Move* out) {
       const bool diag = type == kBishop || type == kQueen, line = type == kRook || type == kQueen;
       for (int k = 0; k < 8; ++k) {
         if (k < 4 ? !diag : !line) continue;
-        const int* d = k < 4 ? kDiagD[k] : kLineD[k - 4];
-        for (int nf = f + d[0], nr = r + d[1]; on_board(nf, nr); nf += d[0], nr += d[1]) {
+        const int df = k < 4 ? diag_df(k) : line_df(k - 4), dr = k < 4 ? diag_dr(k) : line_dr(k - 4);
+        for (int nf = f + df, nr = r + dr; on_board(nf, nr); nf += df, nr += dr) {
           const int tv = p.sq[nr * 8 + nf];
           if (tv != 0 && sgn(tv) == me) break;
           add(s, nr * 8 + nf, 0);
@@ -211,18 +231,42 @@ inline int pseudo_moves(const Pos& p, Move* out) {
   return n;
 }
 
-// Legal moves of the side to move; returns the count (<= 256).
-inline int legal_moves(const Pos& p, Move* out) {
+// Does pseudo-legal move m leave the mover's king unattacked?
+GZ_HDI bool move_is_legal(const Pos& p, const Move& m) {
+  Pos q = p;
+  apply(q, m);
+  const int k = king_square(q, p.side);
+  return k >= 0 && !attacked(q, k, -p.side);
+}
+
+// Legal moves of the side to move, in pseudo_moves' order; returns the
+// count (<= 256).
+GZ_HDI int legal_moves(const Pos& p, Move* out) {
   Move ps[256];
   const int np = pseudo_moves(p, ps);
   int n = 0;
-  for (int i = 0; i < np; ++i) {
-    Pos q = p;
-    apply(q, ps[i]);
-    const int k = king_square(q, p.side);
-    if (k >= 0 && !attacked(q, k, -p.side)) out[n++] = ps[i];
-  }
+  for (int i = 0; i < np; ++i)
+    if (move_is_legal(p, ps[i])) out[n++] = ps[i];
   return n;
+}
+
+// Legal moves in place: the first `return` entries of ms are the legal ones
+// (ms must hold 256).  One buffer instead of two, for device threads.
+GZ_HDI int legal_moves_inplace(const Pos& p, Move* ms) {
+  const int np = pseudo_moves(p, ms);
+  int n = 0;
+  for (int i = 0; i < np; ++i)
+    if (move_is_legal(p, ms[i])) ms[n++] = ms[i];
+  return n;
+}
+
+// Has the side to move a legal move?  `scratch` holds 256 moves.
+GZ_HDI bool has_legal_move(const Pos& p, Move* scratch) {
+  Move* ms = scratch;
+  const int np = pseudo_moves(p, ms);
+  for (int i = 0; i < np; ++i)
+    if (move_is_legal(p, ms[i])) return true;
+  return false;
 }
 
 inline uint64_t perft(const Pos& p, int depth) {
@@ -244,22 +288,62 @@ inline uint64_t perft(const Pos& p, int depth) {
 // move (mate or stalemate) is not played and the playout stops there, so
 // every position has a legal move.  Writes the 66-byte record and returns
 // the side to move.
-inline int make_position(uint64_t seed, uint64_t index, int8_t* rec) {
+GZ_HDI int make_position(uint64_t seed, uint64_t index, int8_t* rec) {
   SplitMix r(mix_seed(seed, 0xC4E55 + index));
   Pos p;
   start_pos(p);
   const int k = (int)r.below(121u);
-  Move ms[256], reply[256];
+  Move ms[256];
   for (int ply = 0; ply < k; ++ply) {
-    const int n = legal_moves(p, ms);
+    const int n = legal_moves_inplace(p, ms);
     if (n == 0) break;
     Pos q = p;
     apply(q, ms[r.below((uint32_t)n)]);
-    if (legal_moves(q, reply) == 0) break;
+    if (!has_legal_move(q, ms)) break;
     p = q;
   }
   to_record(p, rec);
   return p.side;
+}
+
+// Action index of a move, in the reference's action space of 64 x 73
+// (games/chess/chess.cu:94-99, decoded at 127-133): from * 73 + t, where t
+// < 64 is the destination square (ordinary moves, castling as the king's
+// two-square step, and promotions to a queen) and t >= 64 names an
+// underpromotion: 64 + u for a straight pawn push (u = 0 knight, 1 bishop,
+// 2 rook, the reference's 64 + piece - KNIGHT), 67 + u for a capture toward
+// the lower file, 70 + u toward the higher file.  Every legal move has its
+// own index.  (The reference's generator, chess.cu:251-258, marks 64..67 for
+// every promoting pawn, queen included, whatever its destination, so it
+// cannot tell a capturing promotion from a push.)
+GZ_HDI int encode_action(const Move& m) {
+  if (m.promo == 0 || m.promo == kQueen) return m.from * 73 + m.to;
+  const int dfile = file_of(m.to) - file_of(m.from);
+  return m.from * 73 + (dfile == 0 ? 64 : dfile < 0 ? 67 : 70) + (m.promo - kKnight);
+}
+
+// The legal move with action index a, if any (returns false otherwise).
+GZ_HDI bool find_action(const Pos& p, int a, Move* out) {
+  if (a < 0 || a >= 64 * 73) return false;
+  Move ms[256];
+  const int np = pseudo_moves(p, ms);
+  for (int i = 0; i < np; ++i)
+    if (ms[i].from == a / 73 && encode_action(ms[i]) == a && move_is_legal(p, ms[i])) {
+      *out = ms[i];
+      return true;
+    }
+  return false;
+}
+
+// Game state for the side to move: 0 while it has a legal move; otherwise
+// -1 if its king is attacked (checkmate: the side to move has lost) and 2
+// for stalemate (a draw).  The 50-move rule, repetitions and insufficient
+// material are not tracked.
+GZ_HDI int outcome(const Pos& p) {
+  Move ms[256];
+  if (has_legal_move(p, ms)) return 0;
+  const int k = king_square(p, p.side);
+  return k >= 0 && attacked(p, k, -p.side) ? -1 : 2;
 }
 
 }  // namespace chess

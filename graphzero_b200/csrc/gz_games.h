@@ -22,8 +22,10 @@
 
 #if defined(__CUDACC__)
 #define GZ_HD __host__ __device__ __forceinline__
+#define GZ_HDI __host__ __device__ inline  // larger host/device functions, inlined at the compiler's choice
 #else
 #define GZ_HD static inline
+#define GZ_HDI inline
 #endif
 
 namespace gz {

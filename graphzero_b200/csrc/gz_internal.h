@@ -59,6 +59,13 @@ cudaError_t launch_chess_tc(int fp16, const void* d_packed, const float* d_weigh
                             const int8_t* d_side, int n, float* d_pi, float* d_v, int* d_err, cudaStream_t stream);
 
 // Tensor-core Connect4 ResNet forward (implicit-GEMM 3x3 convolutions), bf16 or fp16 operands.
+// rules_dev.cu: seeded positions on the device (bytes as gz_synth_positions
+// makes them) and chess legal moves as action indices ([n][256], -1 padded).
+cudaError_t launch_synth_positions(int game, uint64_t seed, uint64_t first, int n, int8_t* boards, int8_t* side,
+                                   cudaStream_t stream);
+cudaError_t launch_chess_legal(const int8_t* boards, const int8_t* side, int n, int16_t* actions, int32_t* counts,
+                               cudaStream_t stream);
+
 size_t resnet_tc_packed_bytes();
 cudaError_t launch_resnet_tc_pack(int fp16, const float* d_weights, void* d_packed, cudaStream_t stream);
 cudaError_t launch_resnet_tc(int fp16, const void* d_packed, const float* d_weights, const int8_t* d_boards,

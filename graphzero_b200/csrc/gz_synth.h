@@ -5,7 +5,9 @@
 // here every weight and position is a pure function of (seed, index), so any
 // shard of a batch can be regenerated on any rank or process.
 //
-// Host-only code.
+// The position generators (make_position, chess::make_position) compile for
+// host and device alike and give identical positions on both; the weight
+// generators are host code.
 #pragma once
 #include <math.h>
 #include <stdint.h>
@@ -18,17 +20,17 @@ namespace gz {
 // splitmix64 (Steele, Lea, Flood 2014).
 struct SplitMix {
   uint64_t s;
-  explicit SplitMix(uint64_t seed) : s(seed) {}
-  uint64_t next() {
+  GZ_HDI explicit SplitMix(uint64_t seed) : s(seed) {}
+  GZ_HDI uint64_t next() {
     uint64_t z = (s += 0x9E3779B97F4A7C15ull);
     z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
     z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
     return z ^ (z >> 31);
   }
   // Uniform in [0, 1) with 24 random bits.
-  float uniform() { return (float)(next() >> 40) * (1.0f / 16777216.0f); }
+  GZ_HDI float uniform() { return (float)(next() >> 40) * (1.0f / 16777216.0f); }
   // Uniform integer in [0, n).
-  uint32_t below(uint32_t n) { return (uint32_t)(((next() >> 32) * (uint64_t)n) >> 32); }
+  GZ_HDI uint32_t below(uint32_t n) { return (uint32_t)(((next() >> 32) * (uint64_t)n) >> 32); }
   // Standard normal (Box-Muller on two uniforms in (0, 1]).
   float normal() {
     double u1 = ((double)(next() >> 11) + 1.0) * (1.0 / 9007199254740992.0);
@@ -37,7 +39,7 @@ struct SplitMix {
   }
 };
 
-inline uint64_t mix_seed(uint64_t seed, uint64_t stream) {
+GZ_HDI uint64_t mix_seed(uint64_t seed, uint64_t stream) {
   SplitMix m(seed ^ (stream * 0xD1B54A32D192ED03ull));
   return m.next();
 }
@@ -132,7 +134,7 @@ inline void make_resnet_weights(uint64_t seed, const WeightOpts& o, float* out) 
 // random legal moves from the empty board; a move that would end the game is
 // not played and the playout stops there, so every position is non-terminal.
 // Writes board[N] and returns the side to move (+1 first player, -1 second).
-inline int make_position(int game, uint64_t seed, uint64_t index, int8_t* board) {
+GZ_HDI int make_position(int game, uint64_t seed, uint64_t index, int8_t* board) {
   GameShape s = game_shape(game);
   SplitMix r(mix_seed(seed, 0x9051 + index));
   memset(board, 0, (size_t)s.board_bytes);

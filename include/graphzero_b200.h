@@ -115,6 +115,12 @@ gz_status gz_synth_weights(int game, int kind, uint64_t seed, float bias_scale, 
  * Chess: k ~ U{0..120} random legal plies from the initial position, 66-byte
  * records (64 squares, castling rights, en-passant square). */
 gz_status gz_synth_positions(int game, uint64_t seed, uint64_t first, int n, int8_t* boards, int8_t* side);
+/* The same positions made on the device (one thread per position; byte for
+ * byte what gz_synth_positions writes), into device buffers d_boards
+ * [n][board_bytes] and d_side [n], on `stream` (a cudaStream_t; NULL = the
+ * legacy default stream).  Asynchronous; launch errors return GZ_ERR_CUDA. */
+gz_status gz_synth_positions_device(int game, uint64_t seed, uint64_t first, int n, int8_t* d_boards, int8_t* d_side,
+                                    void* stream);
 
 /* ---- chess rules (host) ---------------------------------------------------
  * Replace the move generation of games/chess/chess.cu:677-1071 (which does
@@ -125,6 +131,31 @@ gz_status gz_chess_legal_count(const int8_t* board, int side, int* count);
 /* Leaf count of the legal move tree to `depth` (0..6): the rules'
  * known-answer check against published perft counts. */
 gz_status gz_chess_perft(const int8_t* board, int side, int depth, uint64_t* nodes);
+/* Chess as an IGame (games/game.cuh:17-20; games/chess/chess.cu:94-135,
+ * 216-282).  Actions live in the reference's space of 64 x 73 = 4672:
+ * from * 73 + t, t < 64 the destination square (ordinary moves, castling as
+ * the king's two-square step, promotion to a queen), t = 64 + u a straight
+ * underpromotion (u = 0 knight, 1 bishop, 2 rook; the reference's
+ * 64 + piece - KNIGHT), 67 + u and 70 + u underpromotions capturing toward
+ * the lower and the higher file.  Every legal move has its own index.
+ *   gz_chess_legal_actions: the legal moves' indices in generation order
+ *                           (actions[256]), *count of them.
+ *   gz_chess_valid_moves:   valid[4672] = 1 for legal actions.
+ *   gz_chess_next_state:    the record after `action` and the side to move
+ *                           next; GZ_ERR_INVALID_ARG if the action is illegal.
+ *   gz_chess_ended:         for the side to move: 0 while it has a legal
+ *                           move, -1 if checkmated, 2 for stalemate.  The
+ *                           50-move rule, repetitions and insufficient
+ *                           material are not tracked. */
+gz_status gz_chess_legal_actions(const int8_t* board, int side, int16_t* actions, int* count);
+gz_status gz_chess_valid_moves(const int8_t* board, int side, uint8_t* valid);
+gz_status gz_chess_next_state(const int8_t* board, int side, int action, int8_t* next_board, int* next_side);
+gz_status gz_chess_ended(const int8_t* board, int side, int* result);
+/* Legal actions of n positions on the device: d_boards [n][66], d_side [n]
+ * in; d_actions [n][256] (generation order, -1 after the last) and
+ * d_counts [n] out, on `stream`.  The same lists as gz_chess_legal_actions. */
+gz_status gz_chess_legal_actions_device(const int8_t* d_boards, const int8_t* d_side, int n, int16_t* d_actions,
+                                        int32_t* d_counts, void* stream);
 
 /* ---- network: INeuralNet replacement ------------------------------------ */
 /* create_gat_model / create_resnet_model / create_neural_net

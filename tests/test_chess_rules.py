@@ -80,3 +80,69 @@ def test_synthetic_positions_are_legal_and_deterministic():
     # the side to move varies and most playouts leave the initial position
     assert 0.3 < (side == 1).mean() < 0.7
     assert (np.abs(boards[:, :64].astype(np.int32)).sum(1) < 74).mean() > 0.5  # captures in most playouts
+
+
+def sq(name: str) -> int:
+    return (int(name[1]) - 1) * 8 + (ord(name[0]) - ord("a"))
+
+
+def test_action_indices_name_each_legal_move_once():
+    """The legal moves of random positions map to distinct indices in the
+    64 x 73 action space; valid_moves marks exactly those; each one plays
+    through next_state and an unlisted index is refused."""
+    boards, side = gz.synth_positions(gz.CHESS, 150, seed=11)
+    for b, s in zip(boards, side):
+        acts = gz.chess_legal_actions(b, int(s))
+        assert len(acts) == gz.chess_legal_count(b, int(s)) > 0
+        assert len(set(acts.tolist())) == len(acts)
+        valid = gz.chess_valid_moves(b, int(s))
+        assert valid.sum() == len(acts) and valid[acts].all()
+        assert gz.chess_ended(b, int(s)) == 0
+        for a in acts[:8]:
+            nb, ns = gz.chess_next_state(b, int(s), int(a))
+            assert ns == -int(s) and nb.shape == (66,)
+        bad = int(np.flatnonzero(valid == 0)[0])
+        with pytest.raises(gz.GZError):
+            gz.chess_next_state(b, int(s), bad)
+
+
+def test_action_layout_follows_the_reference():
+    """from * 73 + destination for ordinary moves and castling; a promoting
+    pawn: queen at its destination square, underpromotions at 64 + u
+    (straight; the reference's 64 + piece - KNIGHT), 67 + u and 70 + u
+    (capturing toward the lower / higher file)."""
+    b, s = fen_record("r1r4k/1P6/8/8/8/8/8/R3K2R w KQ - 0 1")
+    acts = set(gz.chess_legal_actions(b, s).tolist())
+    f = sq("b7") * 73
+    promo = {f + sq("b8"), f + 64, f + 65, f + 66, f + sq("a8"), f + 67, f + 68, f + 69, f + sq("c8"), f + 70, f + 71,
+             f + 72}
+    assert promo <= acts
+    assert sq("e1") * 73 + sq("g1") in acts  # castling king side
+    assert sq("e1") * 73 + sq("c1") not in acts  # queen side: c1 is attacked by the rook on c8
+    nb, _ = gz.chess_next_state(b, s, f + 69)  # bxa8=R
+    assert nb[sq("a8")] == 4 and nb[sq("b7")] == 0
+    nb, _ = gz.chess_next_state(b, s, f + sq("c8"))  # bxc8=Q
+    assert nb[sq("c8")] == 5
+    nb, _ = gz.chess_next_state(b, s, sq("e1") * 73 + sq("g1"))  # O-O: rook to f1, rights cleared
+    assert nb[sq("g1")] == 6 and nb[sq("f1")] == 4 and nb[sq("h1")] == 0 and (nb[64] & 3) == 0
+
+
+def test_game_end():
+    fools, s = fen_record("rnb1kbnr/pppp1ppp/8/4p3/6Pq/5P2/PPPPP2P/RNBQKBNR w KQkq - 1 3")
+    assert gz.chess_ended(fools, s) == -1 and gz.chess_legal_count(fools, s) == 0
+    stale, s = fen_record("7k/5Q2/6K1/8/8/8/8/8 b - - 0 1")
+    assert gz.chess_ended(stale, s) == 2
+    start, s = fen_record("rnbqkbnr/pppppppp/8/8/8/8/PPPPPPPP/RNBQKBNR w KQkq - 0 1")
+    assert gz.chess_ended(start, s) == 0 and len(gz.chess_legal_actions(start, s)) == 20
+
+
+def test_move_lists_stay_in_bounds_on_unreachable_records():
+    """A record with far more pieces than a game can have: the pseudo-legal
+    list stops at its 256-entry buffer instead of writing past it."""
+    rec = np.zeros(66, np.int8)
+    rec[:64] = 5  # 64 white queens
+    rec[0] = 6
+    rec[63] = -6
+    rec[65] = -1
+    assert 0 <= gz.chess_legal_count(rec, 1) <= 256
+    assert len(gz.chess_legal_actions(rec, 1)) <= 256
