@@ -125,3 +125,33 @@ def test_resnet_training_reduces_the_loss_and_predictions_follow(cuda):
     tol = max(1e-3, 1.5 * BOUNDS["fp16"])
     assert np.abs(pi - opi).max() < tol and np.abs(v - ov).max() < tol
     net.check()
+
+
+def test_resnet_forward_after_a_step_follows_its_rounding_model(cuda):
+    """One Adam step moves every trained weight by about lr, coherently with
+    the gradient; rounded to nearest in fp16 such weights would put the
+    policy 5.0e-3 from the oracle on these positions (simulated), so the
+    pack kernel rounds them stochastically by a hash of their blob index
+    (simulated: 8.2e-4; 1.3e-3 before the step, the tower's activation
+    floor).  The tensor-core forward on the stepped weights is held to 1.5x
+    the CPU rounding simulation of its formats (tests/rounding_sim.py) and
+    must stay under the round-to-nearest simulation."""
+    from rounding_sim import resnet_forward_rounded
+
+    n = 8
+    w = gz.synth_weights(G, gz.RESNET, seed=0x6A5A)
+    boards, side = gz.synth_positions(G, n, seed=0x6A5A + 1)
+    net = gz.Net(G, gz.RESNET, max_batch=n)
+    net.load_weights(w)
+    d = dev(boards, side, np.full((n, 7), 1.0 / 7, np.float32), np.zeros(n, np.float32))
+    net.train_step(*d, n, gz.train_config(learning_rate=1e-3))
+    w2 = net.save_weights()
+    pi, v = net.predict_host(boards, side)
+    opi, ov = oracle.resnet_forward(w2, boards, side)
+    err = max(float(np.abs(pi - opi).max()), float(np.abs(v - ov).max()))
+    sims = {}
+    for wround in ("sr", "rn"):
+        spi, sv = resnet_forward_rounded(w2, boards, side, op="fp16", wround=wround)
+        sims[wround] = max(float(np.abs(spi - opi).max()), float(np.abs(sv - ov).max()))
+    assert err <= 1.5 * sims["sr"] and err < sims["rn"], (err, sims)
+    net.check()
