@@ -556,7 +556,7 @@ class Mcts:
 
     def copy_leaves(self, stream=None) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
         L = self.trees * self.leaves
-        b = np.zeros((L, self.shape.nodes), np.int8)
+        b = np.zeros((L, self.shape.board_bytes), np.int8)
         s = np.zeros(L, np.int8)
         t = np.zeros(L, np.int8)
         _check(_lib.gz_mcts_copy_leaves(self._h, _ptr(b, C.c_int8), _ptr(s, C.c_int8), _ptr(t, C.c_int8),

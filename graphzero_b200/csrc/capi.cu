@@ -1075,8 +1075,7 @@ gz_status gz_selftest_wait_timeout(int device, int limit_us) {
 gz_status gz_mcts_create(const gz_mcts_config* cfg, int device, gz_mcts** out) {
   if (!cfg || !out) return fail(GZ_ERR_INVALID_ARG, "null argument");
   *out = nullptr;
-  if (cfg->game != kTicTacToe && cfg->game != kConnect4)
-    return fail(GZ_ERR_UNSUPPORTED, "the batched search supports TicTacToe and Connect4");
+  if (!valid_game(cfg->game)) return fail(GZ_ERR_INVALID_ARG, "bad game %d", cfg->game);
   if (cfg->trees <= 0 || cfg->leaves_per_tree <= 0 || cfg->node_capacity < 2 || cfg->virtual_loss < 0)
     return fail(GZ_ERR_INVALID_ARG, "bad search sizes");
   if (!(cfg->c_puct >= 0.f) || !(cfg->dirichlet_eps >= 0.f && cfg->dirichlet_eps <= 1.f) ||
@@ -1095,8 +1094,13 @@ gz_status gz_mcts_create(const gz_mcts_config* cfg, int device, gz_mcts** out) {
   d.leaves = cfg->leaves_per_tree;
   d.vl_k = cfg->virtual_loss;
   d.node_cap = cfg->node_capacity;
-  d.edge_cap = cfg->node_capacity * s.actions;
+  // every node's edges fit: TicTacToe and Connect4 reserve an edge per
+  // action; a chess node averages about 35 legal moves (at most 218), so the
+  // pool reserves 64 per node and a search that outgrows it reports
+  // kMctsEdgeCap through gz_mcts_check
+  d.edge_cap = cfg->node_capacity * (cfg->game == kChess ? 64 : s.actions);
   d.N = s.nodes;
+  d.board_bytes = s.board_bytes;
   d.A = s.actions;
   d.c_puct = cfg->c_puct;
   d.dir_alpha = cfg->dirichlet_alpha;
@@ -1113,7 +1117,12 @@ gz_status gz_mcts_create(const gz_mcts_config* cfg, int device, gz_mcts** out) {
   alloc(&d.tree, T * sizeof(MctsTree));
   alloc(&d.edges, EC * sizeof(MctsEdge));
   alloc(&d.path_edges, L * kMctsMaxDepth * 4); alloc(&d.path_len, L * 4); alloc(&d.leaf_legal, L * 4);
-  alloc(&d.leaf_board, L * d.N); alloc(&d.leaf_side, L); alloc(&d.leaf_terminal, L);
+  alloc(&d.leaf_board, L * d.board_bytes); alloc(&d.leaf_side, L); alloc(&d.leaf_terminal, L);
+  if (d.game == kChess) {
+    alloc(&d.ctree, T * sizeof(ChessTree));
+    alloc(&d.leaf_actions, L * kChessMaxLegal * sizeof(int16_t));
+    alloc(&d.leaf_count, L * 4);
+  }
   alloc(&d.err, 4);
   alloc(&m->d_pi, L * d.A * 4); alloc(&m->d_v, L * 4);
   alloc(&m->d_tmp, T * 4 * 2);
@@ -1129,6 +1138,21 @@ gz_status gz_mcts_create(const gz_mcts_config* cfg, int device, gz_mcts** out) {
     }
     cudaError_t e = cudaMemset(d.err, 0, 4);
     if (e == cudaSuccess) e = cudaMemcpy(d.tree, h.data(), T * sizeof(MctsTree), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && d.game == kChess) {  // chess roots start at the initial position
+      std::vector<ChessTree> hc(T);
+      chess::Pos p0;
+      chess::start_pos(p0);
+      for (ChessTree& tr : hc) {
+        memset(&tr, 0, sizeof tr);
+        chess::to_record(p0, tr.rec);
+        tr.side = 1;
+        tr.fe = -1;
+        tr.meta = (uint32_t)kNodeCreated << 16;
+        tr.node_count = 1;
+      }
+      e = cudaMemcpy(d.ctree, hc.data(), T * sizeof(ChessTree), cudaMemcpyHostToDevice);
+      if (e == cudaSuccess) e = cudaMemset(d.leaf_count, 0, L * 4);
+    }
     if (e == cudaSuccess) e = cudaMemset(d.path_len, 0, L * 4);
     if (e == cudaSuccess) e = cudaMemset(d.path_edges, 0, L * kMctsMaxDepth * 4);
     if (e == cudaSuccess) e = cudaMemset(d.leaf_legal, 0, L * 4);
@@ -1179,7 +1203,7 @@ gz_status gz_mcts_copy_leaves(gz_mcts* m, int8_t* boards, int8_t* side, int8_t* 
   GZ_DEVICE(m->device);
   cudaStream_t s = (cudaStream_t)stream;
   size_t L = (size_t)m->d.trees * m->d.leaves;
-  if (boards) GZ_CUDA(cudaMemcpyAsync(boards, m->d.leaf_board, L * m->d.N, cudaMemcpyDeviceToHost, s));
+  if (boards) GZ_CUDA(cudaMemcpyAsync(boards, m->d.leaf_board, L * m->d.board_bytes, cudaMemcpyDeviceToHost, s));
   if (side) GZ_CUDA(cudaMemcpyAsync(side, m->d.leaf_side, L, cudaMemcpyDeviceToHost, s));
   if (terminal) GZ_CUDA(cudaMemcpyAsync(terminal, m->d.leaf_terminal, L, cudaMemcpyDeviceToHost, s));
   GZ_CUDA(cudaStreamSynchronize(s));
@@ -1286,6 +1310,8 @@ static_assert(sizeof(gz_train_example) == 516, "TrainingExample layout of self_p
 gz_status gz_selfplay_create(gz_mcts* m, int max_examples, gz_selfplay** out) {
   if (!m || !out || max_examples <= 0) return fail(GZ_ERR_INVALID_ARG, "bad arguments");
   *out = nullptr;
+  if (m->d.game == kChess)
+    return fail(GZ_ERR_UNSUPPORTED, "self-play records TicTacToe and Connect4 games (the 64-cell example format)");
   GZ_DEVICE(m->device);
   gz_selfplay* sp = new gz_selfplay();
   sp->m = m;
@@ -1392,6 +1418,7 @@ gz_status gz_arena_play(gz_mcts* m, gz_net* net_a, gz_net* net_b, int n_games, i
                         int32_t* b_wins, int32_t* draws, void* stream) {
   if (!m || !net_a || !net_b || n_games < 0 || sims <= 0 || !a_wins || !b_wins || !draws)
     return fail(GZ_ERR_INVALID_ARG, "bad arguments");
+  if (m->d.game == kChess) return fail(GZ_ERR_UNSUPPORTED, "the arena plays TicTacToe and Connect4");
   if (net_a->game != m->d.game || net_b->game != m->d.game)
     return fail(GZ_ERR_INVALID_ARG, "nets and search play different games");
   if (net_a->device != m->device || net_b->device != m->device)

@@ -322,10 +322,29 @@ GZ_HDI int encode_action(const Move& m) {
   return m.from * 73 + (dfile == 0 ? 64 : dfile < 0 ? 67 : 70) + (m.promo - kKnight);
 }
 
+// The move that action index a names in position p (the inverse of
+// encode_action on p's legal moves; no legality check: a must come from
+// p's legal list).
+GZ_HDI Move decode_action(const Pos& p, int a) {
+  const int from = a / 73, t = a % 73;
+  Move m;
+  m.from = (int8_t)from;
+  if (t < 64) {
+    m.to = (int8_t)t;
+    const bool pawn_to_last = p.sq[from] * p.side == kPawn && rank_of(t) == (p.side > 0 ? 7 : 0);
+    m.promo = (int8_t)(pawn_to_last ? kQueen : 0);
+  } else {
+    const int u = (t - 64) % 3, dir = (t - 64) / 3;  // dir 0 straight, 1 lower file, 2 higher file
+    m.to = (int8_t)(from + 8 * p.side + (dir == 0 ? 0 : dir == 1 ? -1 : 1));
+    m.promo = (int8_t)(kKnight + u);
+  }
+  return m;
+}
+
 // The legal move with action index a, if any (returns false otherwise).
-GZ_HDI bool find_action(const Pos& p, int a, Move* out) {
+GZ_HDI bool find_action_with(const Pos& p, int a, Move* out, Move* scratch) {  // scratch holds 256 moves
   if (a < 0 || a >= 64 * 73) return false;
-  Move ms[256];
+  Move* ms = scratch;
   const int np = pseudo_moves(p, ms);
   for (int i = 0; i < np; ++i)
     if (ms[i].from == a / 73 && encode_action(ms[i]) == a && move_is_legal(p, ms[i])) {
@@ -335,15 +354,24 @@ GZ_HDI bool find_action(const Pos& p, int a, Move* out) {
   return false;
 }
 
+GZ_HDI bool find_action(const Pos& p, int a, Move* out) {
+  Move ms[256];
+  return find_action_with(p, a, out, ms);
+}
+
 // Game state for the side to move: 0 while it has a legal move; otherwise
 // -1 if its king is attacked (checkmate: the side to move has lost) and 2
 // for stalemate (a draw).  The 50-move rule, repetitions and insufficient
 // material are not tracked.
-GZ_HDI int outcome(const Pos& p) {
-  Move ms[256];
-  if (has_legal_move(p, ms)) return 0;
+GZ_HDI int outcome_with(const Pos& p, Move* scratch) {  // scratch holds 256 moves
+  if (has_legal_move(p, scratch)) return 0;
   const int k = king_square(p, p.side);
   return k >= 0 && attacked(p, k, -p.side) ? -1 : 2;
+}
+
+GZ_HDI int outcome(const Pos& p) {
+  Move ms[256];
+  return outcome_with(p, ms);
 }
 
 }  // namespace chess

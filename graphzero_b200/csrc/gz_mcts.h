@@ -58,8 +58,27 @@ struct alignas(16) MctsTree {  // 128 bytes per tree
 };
 static_assert(sizeof(MctsTree) == 128, "tree record");
 
+// Chess trees (game kChess) keep the root as the 66-byte record plus the
+// side to move, and their edges carry the action index (from * 73 + t, up
+// to 4671) in pad[0]; meta's action byte is unused.  Edge counts (<= 218
+// legal moves) still fit meta's 8 bits.
+struct alignas(16) ChessTree {  // 128 bytes per tree
+  int8_t rec[66];                // root position (squares, castling rights, en-passant square)
+  int8_t side;                   // player to move at the root
+  int8_t pad0;
+  int32_t fe;                    // root's first edge
+  uint32_t meta;                 // root's edge count << 8 | flags << 16
+  int32_t n, vl;
+  int32_t node_count, edge_count;
+  int32_t move_no;
+  int32_t pad[8];
+};
+static_assert(sizeof(ChessTree) == 128, "chess tree record");
+constexpr int kChessMaxLegal = 256;  // legal-action list length per leaf (<= 218 in chess)
+
 struct MctsDev {
   int game, trees, leaves, vl_k, node_cap, edge_cap, N, A;
+  int board_bytes;  // bytes per stored position (N, 66 for chess)
   float c_puct, dir_alpha, dir_eps;
   unsigned long long seed;
   MctsTree* tree;   // [trees]
@@ -73,6 +92,10 @@ struct MctsDev {
   int8_t* leaf_side;
   int8_t* leaf_terminal;
   int* err;  // first error code seen by a kernel (0 = none)
+  // chess only
+  ChessTree* ctree;       // [trees]
+  int16_t* leaf_actions;  // [slots][kChessMaxLegal] legal actions at the leaf, generation order
+  int32_t* leaf_count;    // [slots]
 };
 
 enum MctsErr : int { kMctsOk = 0, kMctsNodeCap = 1, kMctsEdgeCap = 2, kMctsDepth = 3 };

@@ -28,6 +28,7 @@
 #include <math.h>
 #include <stdint.h>
 
+#include "gz_chess.h"
 #include "gz_games.h"
 #include "gz_mcts.h"
 
@@ -488,47 +489,420 @@ __global__ void tree_sizes_kernel(MctsDev d, int32_t* nodes, int32_t* edges) {
   edges[t] = d.tree[t].edge_count;
 }
 
+// ---------------- chess (game kChess) ----------------
+// The same waves on chess positions.  A warp per tree picks each level's
+// edge by PUCT over up to 218 edges (lane j % 32 scores edge j; lowest index
+// on ties, as above); lane 0 replays the path's actions on the root record,
+// decides whether a new node ends the game (checkmate: a loss for its player
+// to move; stalemate: a draw), and lists an unexpanded leaf's legal actions
+// in generation order for the expansion.  Edges carry their action in pad[0].
+
+__device__ void chess_reset_tree(ChessTree* tr, const int8_t* rec, int side, int move_no) {
+  for (int i = 0; i < 66; ++i) tr->rec[i] = rec[i];
+  tr->side = (int8_t)(side >= 0 ? 1 : -1);
+  tr->fe = -1;
+  tr->meta = make_meta(0, 0, kNodeCreated);
+  tr->n = 0;
+  tr->vl = 0;
+  tr->node_count = 1;
+  tr->edge_count = 0;
+  tr->move_no = move_no;
+}
+
+__global__ void chess_reset_kernel(MctsDev d, const int8_t* __restrict__ boards, const int8_t* __restrict__ side) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= d.trees) return;
+  chess_reset_tree(d.ctree + t, boards + (size_t)t * 66, side[t], 0);
+}
+
+// PUCT score of an edge record (the select_tree arithmetic).
+__device__ __forceinline__ float chess_puct(const MctsDev& d, int4 ra, float sq) {
+  const int vlk = d.vl_k * ra.w;
+  const int nev = ra.z + vlk;
+  const float q = nev > 0 ? __fdiv_rn(__fsub_rn(__int_as_float(ra.y), (float)vlk), (float)nev) : 0.0f;
+  const float u1 = __fmul_rn(d.c_puct, __int_as_float(ra.x));
+  const float u2 = __fmul_rn(u1, sq);
+  const float u3 = __fdiv_rn(u2, __fadd_rn(1.0f, (float)nev));
+  return __fadd_rn(q, u3);
+}
+
+__device__ void chess_select_tree(const MctsDev& d, int t, int lane) {
+  ChessTree* tr = d.ctree + t;
+  MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
+  const int r_fe = tr->fe;
+  const uint32_t r_meta = tr->meta;
+  const int r_n = tr->n;
+  int r_vl = tr->vl;
+  int node_count = tr->node_count;
+  chess::Move ms[256];  // lane 0: the new node's reply check and the leaf's legal list
+  for (int k = 0; k < d.leaves; ++k) {
+    const size_t slot = (size_t)t * d.leaves + k;
+    int* pe = d.path_edges + slot * kMctsMaxDepth;
+    int fe = r_fe, ne = meta_edges(r_meta);
+    uint32_t flags = meta_flags(r_meta);
+    int np = r_n + d.vl_k * r_vl;
+    r_vl += 1;
+    chess::Pos p;
+    chess::from_record(tr->rec, tr->side, p);
+    int depth = 0;
+    // an expanded node without edges (a root loaded in a finished game) is a leaf
+    while ((flags & kNodeExpanded) && !(flags & kNodeTerminal) && ne > 0) {
+      const float sq = __fsqrt_rn((float)np);
+      float u = -INFINITY;
+      int idx = 0x7fffffff;
+      int4 ra = make_int4(0, 0, 0, 0), rb = make_int4(0, 0, 0, 0);
+      for (int j = lane; j < ne; j += 32) {
+        const int4* rec = (const int4*)(E + fe + j);
+        const int4 a0 = rec[0], a1 = rec[1];
+        float uj = chess_puct(d, a0, sq);
+        if (uj != uj) uj = -INFINITY;  // a NaN prior or value sum: every lane still agrees on the pick
+        if (uj > u || idx == 0x7fffffff) {
+          u = uj;
+          idx = j;
+          ra = a0;
+          rb = a1;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const float uo = __shfl_xor_sync(kFull, u, o);
+        const int io = __shfl_xor_sync(kFull, idx, o);
+        if (uo > u || (uo == u && io < idx)) { u = uo; idx = io; }
+      }
+      const int src = idx & 31, e = fe + idx;
+      const int c_nv = __shfl_sync(kFull, ra.z, src), c_vl = __shfl_sync(kFull, ra.w, src);
+      const int c_fe = __shfl_sync(kFull, rb.x, src);
+      const uint32_t c_meta = (uint32_t)__shfl_sync(kFull, rb.y, src);
+      const int c_act = __shfl_sync(kFull, rb.z, src);
+      uint32_t cflags = meta_flags(c_meta);
+      if (!(cflags & kNodeCreated) && node_count >= d.node_cap) {
+        if (lane == 0) set_err(d.err, kMctsNodeCap);
+        break;
+      }
+      if (depth + 1 >= kMctsMaxDepth) {
+        if (lane == 0) set_err(d.err, kMctsDepth);
+        break;
+      }
+      if (lane == 0) {
+        E[e].VL = c_vl + 1;
+        pe[depth] = e;
+      }
+      chess::apply(p, chess::decode_action(p, c_act));
+      ++depth;
+      if (!(cflags & kNodeCreated)) {
+        ++node_count;
+        int oc = 0;
+        if (lane == 0) oc = chess::outcome_with(p, ms);
+        oc = __shfl_sync(kFull, oc, 0);
+        cflags = kNodeCreated | (oc != 0 ? kNodeTerminal : 0u) | (oc == -1 ? kNodeLoss : 0u);
+        if (lane == 0) E[e].meta = make_meta(0, 0, cflags);
+      }
+      flags = cflags;
+      fe = c_fe;
+      ne = meta_edges(c_meta);
+      np = c_nv + d.vl_k * c_vl;
+    }
+    if (lane == 0) {
+      const bool term = (flags & kNodeTerminal) != 0;
+      d.path_len[slot] = depth;
+      d.leaf_side[slot] = p.side;
+      d.leaf_terminal[slot] = term ? 1 : 0;
+      chess::to_record(p, d.leaf_board + slot * 66);
+      int c = 0;
+      if (!term && !(flags & kNodeExpanded)) {
+        c = chess::legal_moves_inplace(p, ms);
+        int16_t* la = d.leaf_actions + slot * kChessMaxLegal;
+        for (int j = 0; j < c; ++j) la[j] = (int16_t)chess::encode_action(ms[j]);
+      }
+      d.leaf_count[slot] = c;
+    }
+  }
+  if (lane == 0) {
+    tr->vl = r_vl;
+    tr->node_count = node_count;
+  }
+}
+
+__device__ void chess_backup_tree(const MctsDev& d, const float* __restrict__ pi, const float* __restrict__ value,
+                                  int t, int lane) {
+  ChessTree* tr = d.ctree + t;
+  MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
+  int r_fe = tr->fe;
+  uint32_t r_meta = tr->meta;
+  int r_n = tr->n, r_vl = tr->vl, edge_count = tr->edge_count;
+  const int move_no = tr->move_no;
+  for (int k = 0; k < d.leaves; ++k) {
+    const size_t slot = (size_t)t * d.leaves + k;
+    const int* pe = d.path_edges + slot * kMctsMaxDepth;
+    const int len = d.path_len[slot];
+    const int e0 = lane < len ? pe[lane] : -1;
+    const int e1 = lane + 32 < len ? pe[lane + 32] : -1;
+    const int le = len > 0 ? __shfl_sync(kFull, len - 1 < 32 ? e0 : e1, (len - 1) & 31) : -1;
+    uint32_t lmeta = r_meta;
+    if (len > 0 && lane == 0) lmeta = E[le].meta;
+    lmeta = __shfl_sync(kFull, lmeta, 0);
+    const uint32_t lflags = meta_flags(lmeta);
+    float val;
+    if (lflags & kNodeTerminal) {
+      val = (lflags & kNodeLoss) ? -1.0f : 0.0f;
+    } else {
+      val = value[slot];
+      if (!(lflags & kNodeExpanded)) {
+        const float* p = pi + slot * d.A;
+        const int16_t* la = d.leaf_actions + slot * kChessMaxLegal;
+        const int cnt = d.leaf_count[slot];
+        float sum = 0.0f;
+        int fe = 0;
+        if (lane == 0) {
+          for (int j = 0; j < cnt; ++j) sum = __fadd_rn(sum, p[la[j]]);
+          fe = edge_count;
+          if (fe + cnt > d.edge_cap) {
+            set_err(d.err, kMctsEdgeCap);
+            fe = -1;
+          } else {
+            edge_count = fe + cnt;
+          }
+        }
+        sum = __shfl_sync(kFull, sum, 0);
+        fe = __shfl_sync(kFull, fe, 0);
+        if (fe >= 0) {
+          for (int j = lane; j < cnt; j += 32) {
+            const int a = la[j];
+            int4* rec = (int4*)(E + fe + j);
+            rec[0] = make_int4(__float_as_int(__fdiv_rn(p[a], sum)), __float_as_int(0.0f), 0, 0);
+            rec[1] = make_int4(-1, (int)make_meta(0, 0, 0), a, 0);
+          }
+          __syncwarp();
+          if (lane == 0) {
+            if (d.dir_eps > 0.0f && len == 0 && cnt > 0) {
+              // root noise, P = (1 - eps) P + eps Dir(alpha); the gammas are
+              // drawn twice (the sum, then each share) instead of stored
+              float gs = 0.0f;
+              for (int j = 0; j < cnt; ++j)
+                gs += sample_gamma(d.dir_alpha, d.seed, (unsigned long long)t, ((unsigned long long)move_no << 8) | j);
+              for (int j = 0; j < cnt; ++j) {
+                const float g =
+                    sample_gamma(d.dir_alpha, d.seed, (unsigned long long)t, ((unsigned long long)move_no << 8) | j);
+                E[fe + j].P = (1.0f - d.dir_eps) * E[fe + j].P + d.dir_eps * (gs > 0.0f ? g / gs : 1.0f / cnt);
+              }
+            }
+            const uint32_t nm = make_meta(0, cnt, lflags | kNodeExpanded);
+            if (len > 0) {
+              E[le].child_fe = fe;
+              E[le].meta = nm;
+            } else {
+              r_fe = fe;
+              r_meta = nm;
+            }
+          }
+          r_fe = __shfl_sync(kFull, r_fe, 0);
+          r_meta = __shfl_sync(kFull, r_meta, 0);
+        }
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int i = lane + 32 * h, e = h ? e1 : e0;
+      if (i < len) {
+        const float x = ((len - 1 - i) & 1) ? val : -val;
+        int4* rec = (int4*)(E + e);
+        int4 s = rec[0];
+        s.y = __float_as_int(__fadd_rn(__int_as_float(s.y), x));
+        s.z += 1;
+        s.w -= 1;
+        rec[0] = s;
+      }
+    }
+    r_n += 1;
+    r_vl -= 1;
+    __syncwarp();
+  }
+  if (lane == 0) {
+    tr->fe = r_fe;
+    tr->meta = r_meta;
+    tr->n = r_n;
+    tr->vl = r_vl;
+    tr->edge_count = edge_count;
+  }
+}
+
+__global__ void chess_select_kernel(MctsDev d) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t < d.trees) chess_select_tree(d, t, threadIdx.x & 31);
+}
+
+__global__ void chess_backup_kernel(MctsDev d, const float* __restrict__ pi, const float* __restrict__ value) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t < d.trees) chess_backup_tree(d, pi, value, t, threadIdx.x & 31);
+}
+
+__global__ void chess_backup_select_kernel(MctsDev d, const float* __restrict__ pi, const float* __restrict__ value) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t >= d.trees) return;
+  chess_backup_tree(d, pi, value, t, threadIdx.x & 31);
+  __syncwarp();
+  chess_select_tree(d, t, threadIdx.x & 31);
+}
+
+__global__ void chess_root_visits_kernel(MctsDev d, int32_t* __restrict__ visits, float* __restrict__ wsum) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= d.trees) return;
+  const ChessTree* tr = d.ctree + t;
+  const MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
+  for (int a = 0; a < d.A; ++a) {
+    visits[(size_t)t * d.A + a] = 0;
+    if (wsum) wsum[(size_t)t * d.A + a] = 0.0f;
+  }
+  if (!(meta_flags(tr->meta) & kNodeExpanded)) return;
+  const int fe = tr->fe, ne = meta_edges(tr->meta);
+  for (int k = 0; k < ne; ++k) {
+    const MctsEdge& e = E[fe + k];
+    visits[(size_t)t * d.A + e.pad[0]] = e.Nv;
+    if (wsum) wsum[(size_t)t * d.A + e.pad[0]] = e.W;
+  }
+}
+
+// choose_kernel's rule on chess roots (edges in generation order); an
+// unexpanded root plays its first legal action (0 if it has none).
+__global__ void chess_choose_kernel(MctsDev d, int temp_moves, int32_t* __restrict__ actions) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= d.trees) return;
+  const ChessTree* tr = d.ctree + t;
+  const MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
+  const int fe = tr->fe, ne = (meta_flags(tr->meta) & kNodeExpanded) ? meta_edges(tr->meta) : 0;
+  int pick = -1;
+  if (ne > 0) {
+    long long total = 0;
+    int best = 0;
+    for (int k = 0; k < ne; ++k) {
+      const int nv = E[fe + k].Nv;
+      total += nv;
+      if (nv > E[fe + best].Nv) best = k;
+    }
+    pick = best;
+    if (tr->move_no < temp_moves && total > 0) {
+      const unsigned long long h = rng64(d.seed, (unsigned long long)t, (unsigned long long)tr->move_no, 0xC4);
+      const long long x = (long long)(((h >> 32) * (unsigned long long)total) >> 32);
+      long long cum = 0;
+      for (int k = 0; k < ne; ++k) {
+        cum += E[fe + k].Nv;
+        if (cum > x) { pick = k; break; }
+      }
+    }
+  }
+  if (pick >= 0) {
+    actions[t] = E[fe + pick].pad[0];
+  } else {
+    chess::Pos p;
+    chess::from_record(tr->rec, tr->side, p);
+    chess::Move ms[256];
+    actions[t] = chess::legal_moves_inplace(p, ms) > 0 ? chess::encode_action(ms[0]) : 0;
+  }
+}
+
+// play_kernel's rule on chess roots: the action is checked against the
+// legal moves (an illegal one ends the game as a draw); a finished game
+// (checkmate or stalemate after the move) restarts from the initial
+// position with white to move.
+__global__ void chess_play_kernel(MctsDev d, const int32_t* __restrict__ actions, int reserve,
+                                  int8_t* __restrict__ done) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= d.trees) return;
+  ChessTree* tr = d.ctree + t;
+  const MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
+  const int a = actions[t];
+  const MctsEdge* ce = nullptr;
+  if (meta_flags(tr->meta) & kNodeExpanded) {
+    const int fe = tr->fe, ne = meta_edges(tr->meta);
+    for (int k = 0; k < ne; ++k)
+      if (E[fe + k].pad[0] == a && (meta_flags(E[fe + k].meta) & kNodeCreated)) ce = E + fe + k;
+  }
+  chess::Pos p;
+  chess::from_record(tr->rec, tr->side, p);
+  chess::Move m, ms[256];
+  int oc = 2;
+  if (chess::find_action_with(p, a, &m, ms)) {
+    chess::apply(p, m);
+    oc = chess::outcome_with(p, ms);
+  }
+  if (done) done[t] = (int8_t)(oc != 0);
+  int8_t rec[66];
+  if (oc != 0) {
+    chess::Pos s0;
+    chess::start_pos(s0);
+    chess::to_record(s0, rec);
+    chess_reset_tree(tr, rec, 1, 0);
+  } else if (ce && tr->node_count + reserve <= d.node_cap) {
+    chess::to_record(p, tr->rec);
+    tr->side = p.side;
+    tr->fe = ce->child_fe;
+    tr->meta = make_meta(0, meta_edges(ce->meta), meta_flags(ce->meta));
+    tr->n = ce->Nv;
+    tr->vl = ce->VL;
+    tr->move_no += 1;
+  } else {
+    chess::to_record(p, rec);
+    chess_reset_tree(tr, rec, p.side, tr->move_no + 1);
+  }
+}
+
+__global__ void chess_tree_sizes_kernel(MctsDev d, int32_t* nodes, int32_t* edges) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= d.trees) return;
+  nodes[t] = d.ctree[t].node_count;
+  edges[t] = d.ctree[t].edge_count;
+}
+
 inline int blocks_for(int n, int per) { return (n + per - 1) / per; }
 
 }  // namespace
 
 cudaError_t mcts_launch_reset(const MctsDev& d, const int8_t* boards, const int8_t* side, cudaStream_t s) {
-  reset_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, boards, side);
+  if (d.game == kChess) chess_reset_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, boards, side);
+  else reset_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, boards, side);
   return cudaGetLastError();
 }
 
 cudaError_t mcts_launch_select(const MctsDev& d, cudaStream_t s) {
-  select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d);
+  if (d.game == kChess) chess_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d);
+  else select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d);
   return cudaGetLastError();
 }
 
 cudaError_t mcts_launch_backup(const MctsDev& d, const float* pi, const float* v, cudaStream_t s) {
-  backup_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
+  if (d.game == kChess) chess_backup_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
+  else backup_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
   return cudaGetLastError();
 }
 
 cudaError_t mcts_launch_backup_select(const MctsDev& d, const float* pi, const float* v, cudaStream_t s) {
-  backup_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
+  if (d.game == kChess) chess_backup_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
+  else backup_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
   return cudaGetLastError();
 }
 
 cudaError_t mcts_launch_root_visits(const MctsDev& d, int32_t* visits, float* wsum, cudaStream_t s) {
-  root_visits_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, visits, wsum);
+  if (d.game == kChess) chess_root_visits_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, visits, wsum);
+  else root_visits_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, visits, wsum);
   return cudaGetLastError();
 }
 
 cudaError_t mcts_launch_choose(const MctsDev& d, int temp_moves, int32_t* actions, cudaStream_t s) {
-  choose_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, temp_moves, actions);
+  if (d.game == kChess) chess_choose_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, temp_moves, actions);
+  else choose_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, temp_moves, actions);
   return cudaGetLastError();
 }
 
 cudaError_t mcts_launch_play(const MctsDev& d, const int32_t* actions, int reserve, int8_t* done, cudaStream_t s) {
-  play_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, actions, reserve, done);
+  if (d.game == kChess) chess_play_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, actions, reserve, done);
+  else play_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, actions, reserve, done);
   return cudaGetLastError();
 }
 
 cudaError_t mcts_launch_tree_sizes(const MctsDev& d, int32_t* nodes, int32_t* edges, cudaStream_t s) {
-  tree_sizes_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, nodes, edges);
+  if (d.game == kChess) chess_tree_sizes_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, nodes, edges);
+  else tree_sizes_kernel<<<blocks_for(d.trees, 128), 128, 0, s>>>(d, nodes, edges);
   return cudaGetLastError();
 }
 

@@ -213,10 +213,17 @@ gz_status gz_nccl_unique_id(uint8_t out[128]);
 gz_status gz_nccl_comm_init(const uint8_t id[128], int world, int rank, int device, void** comm);
 gz_status gz_nccl_comm_destroy(void* comm);
 
-/* ---- batched PUCT search (mcts/mcts.cu, self_play/self_play.cu:610-758) -- */
+/* ---- batched PUCT search (mcts/mcts.cu, self_play/self_play.cu:610-758) --
+ * Every game: TicTacToe and Connect4 boards of `nodes` bytes; chess
+ * 66-byte records with actions in the 64 x 73 space of gz_chess_valid_moves
+ * (root statistics [trees][4672]; a node reached by checkmate is a loss for
+ * its player to move, stalemate a draw; a finished game restarts from the
+ * initial position).  A chess pool reserves 64 edges per node (about 35 are
+ * used on average; gz_mcts_check reports an overflow).  Self-play and the
+ * arena play TicTacToe and Connect4 (GZ_ERR_UNSUPPORTED for chess). */
 gz_status gz_mcts_create(const gz_mcts_config* cfg, int device, gz_mcts** out);
 gz_status gz_mcts_destroy(gz_mcts* m);
-/* Root positions, device arrays boards [trees][nodes], side [trees]
+/* Root positions, device arrays boards [trees][board bytes], side [trees]
  * (replaces mcts_init, mcts/mcts.cu:10). */
 gz_status gz_mcts_reset_roots(gz_mcts* m, const int8_t* d_boards, const int8_t* d_side, void* stream);
 /* One selection pass; fills the leaf batch (trees * leaves_per_tree). */

@@ -82,8 +82,8 @@ def test_create_without_gpu_fails_cleanly():
 
 
 def test_mcts_config_validation():
-    cfg = gz.MctsConfig(gz.CHESS, 4, 4, 1.5, 3, 64, 1.0, 0.0, 1)
+    cfg = gz.MctsConfig(7, 4, 4, 1.5, 3, 64, 1.0, 0.0, 1)  # no such game
     h = C.c_void_p()
-    assert gz._lib.gz_mcts_create(C.byref(cfg), 0, C.byref(h)) == gz.ERR_UNSUPPORTED
+    assert gz._lib.gz_mcts_create(C.byref(cfg), 0, C.byref(h)) == gz.ERR_INVALID_ARG
     cfg = gz.MctsConfig(gz.CONNECT4, 0, 4, 1.5, 3, 64, 1.0, 0.0, 1)
     assert gz._lib.gz_mcts_create(C.byref(cfg), 0, C.byref(h)) == gz.ERR_INVALID_ARG
