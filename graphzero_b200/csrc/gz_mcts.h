@@ -29,6 +29,7 @@ enum : uint32_t {
   kNodeExpanded = 2u,  // its edges exist
   kNodeTerminal = 4u,  // the game is over at the child
   kNodeLoss = 8u,      // terminal with a loss for the child's player to move (value -1; else 0)
+  kNodeChecked = 16u,  // chess: the game-end check of the node has run (the wave's leaf pass)
 };
 
 __host__ __device__ __forceinline__ uint32_t meta_action(uint32_t m) { return m & 0xffu; }

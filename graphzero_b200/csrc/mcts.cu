@@ -496,6 +496,10 @@ __global__ void tree_sizes_kernel(MctsDev d, int32_t* nodes, int32_t* edges) {
 // decides whether a new node ends the game (checkmate: a loss for its player
 // to move; stalemate: a draw), and lists an unexpanded leaf's legal actions
 // in generation order for the expansion.  Edges carry their action in pad[0].
+// The end-of-game check of a new node and the leaf's legal list run after
+// the wave's selections, one thread per leaf (chess_leaf_kernel): a new node
+// is unexpanded, so it ends a selection whether or not the game ends there,
+// and nothing in the selections depends on the check.
 
 __device__ void chess_reset_tree(ChessTree* tr, const int8_t* rec, int side, int move_no) {
   for (int i = 0; i < 66; ++i) tr->rec[i] = rec[i];
@@ -534,7 +538,6 @@ __device__ void chess_select_tree(const MctsDev& d, int t, int lane) {
   const int r_n = tr->n;
   int r_vl = tr->vl;
   int node_count = tr->node_count;
-  chess::Move ms[256];  // lane 0: the new node's reply check and the leaf's legal list
   for (int k = 0; k < d.leaves; ++k) {
     const size_t slot = (size_t)t * d.leaves + k;
     int* pe = d.path_edges + slot * kMctsMaxDepth;
@@ -589,12 +592,9 @@ __device__ void chess_select_tree(const MctsDev& d, int t, int lane) {
       }
       chess::apply(p, chess::decode_action(p, c_act));
       ++depth;
-      if (!(cflags & kNodeCreated)) {
+      if (!(cflags & kNodeCreated)) {  // a new node: counted; its game-end check follows in the leaf pass
         ++node_count;
-        int oc = 0;
-        if (lane == 0) oc = chess::outcome_with(p, ms);
-        oc = __shfl_sync(kFull, oc, 0);
-        cflags = kNodeCreated | (oc != 0 ? kNodeTerminal : 0u) | (oc == -1 ? kNodeLoss : 0u);
+        cflags = kNodeCreated;
         if (lane == 0) E[e].meta = make_meta(0, 0, cflags);
       }
       flags = cflags;
@@ -603,18 +603,9 @@ __device__ void chess_select_tree(const MctsDev& d, int t, int lane) {
       np = c_nv + d.vl_k * c_vl;
     }
     if (lane == 0) {
-      const bool term = (flags & kNodeTerminal) != 0;
       d.path_len[slot] = depth;
       d.leaf_side[slot] = p.side;
-      d.leaf_terminal[slot] = term ? 1 : 0;
       chess::to_record(p, d.leaf_board + slot * 66);
-      int c = 0;
-      if (!term && !(flags & kNodeExpanded)) {
-        c = chess::legal_moves_inplace(p, ms);
-        int16_t* la = d.leaf_actions + slot * kChessMaxLegal;
-        for (int j = 0; j < c; ++j) la[j] = (int16_t)chess::encode_action(ms[j]);
-      }
-      d.leaf_count[slot] = c;
     }
   }
   if (lane == 0) {
@@ -725,6 +716,37 @@ __device__ void chess_backup_tree(const MctsDev& d, const float* __restrict__ pi
     tr->vl = r_vl;
     tr->edge_count = edge_count;
   }
+}
+
+// The wave's leaf pass, one thread per selection: a node created in this
+// wave gets its game-end check (checkmate: a loss for its player to move;
+// stalemate: a draw), and a non-terminal unexpanded leaf its legal actions
+// in generation order.  Two selections that end on the same new node write
+// the same flags.
+__global__ void chess_leaf_kernel(MctsDev d) {
+  const int slot = blockIdx.x * blockDim.x + threadIdx.x;
+  if (slot >= d.trees * d.leaves) return;
+  const int t = slot / d.leaves, len = d.path_len[slot];
+  MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
+  const int le = len > 0 ? d.path_edges[(size_t)slot * kMctsMaxDepth + len - 1] : -1;
+  uint32_t flags = meta_flags(len > 0 ? E[le].meta : d.ctree[t].meta);
+  chess::Pos p;
+  chess::from_record(d.leaf_board + (size_t)slot * 66, d.leaf_side[slot], p);
+  chess::Move ms[256];
+  if (len > 0 && !(flags & kNodeChecked)) {  // created this wave, so not expanded
+    const int oc = chess::outcome_with(p, ms);
+    flags |= kNodeChecked | (oc != 0 ? kNodeTerminal : 0u) | (oc == -1 ? kNodeLoss : 0u);
+    E[le].meta = make_meta(0, 0, flags);
+  }
+  const bool term = (flags & kNodeTerminal) != 0;
+  d.leaf_terminal[slot] = term ? 1 : 0;
+  int c = 0;
+  if (!term && !(flags & kNodeExpanded)) {
+    c = chess::legal_moves_inplace(p, ms);
+    int16_t* la = d.leaf_actions + (size_t)slot * kChessMaxLegal;
+    for (int j = 0; j < c; ++j) la[j] = (int16_t)chess::encode_action(ms[j]);
+  }
+  d.leaf_count[slot] = c;
 }
 
 __global__ void chess_select_kernel(MctsDev d) {
@@ -865,8 +887,10 @@ cudaError_t mcts_launch_reset(const MctsDev& d, const int8_t* boards, const int8
 }
 
 cudaError_t mcts_launch_select(const MctsDev& d, cudaStream_t s) {
-  if (d.game == kChess) chess_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d);
-  else select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d);
+  if (d.game == kChess) {
+    chess_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d);
+    chess_leaf_kernel<<<blocks_for(d.trees * d.leaves, 128), 128, 0, s>>>(d);
+  } else select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d);
   return cudaGetLastError();
 }
 
@@ -877,8 +901,10 @@ cudaError_t mcts_launch_backup(const MctsDev& d, const float* pi, const float* v
 }
 
 cudaError_t mcts_launch_backup_select(const MctsDev& d, const float* pi, const float* v, cudaStream_t s) {
-  if (d.game == kChess) chess_backup_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
-  else backup_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
+  if (d.game == kChess) {
+    chess_backup_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
+    chess_leaf_kernel<<<blocks_for(d.trees * d.leaves, 128), 128, 0, s>>>(d);
+  } else backup_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
   return cudaGetLastError();
 }
 
