@@ -12,7 +12,8 @@ weights reach every GPU through one NCCL broadcast before timing, and the
 reported time is the maximum over ranks.  Prints ONE JSON line on rank 0.
 The c1 line also carries, under "configs", the other leaf-evaluation
 workloads (c0 TicTacToe fp32, c2 Connect4 ResNet, c3 chess GAT) measured on
-the same GPU, each with its roofline and CPU baseline, and under "train" the
+the same GPU, each with its roofline and CPU baseline (c3 also with the
+batched search on chess positions under "search"), and under "train" the
 training step time of the Connect4 GAT and ResNet at batch 64.
 
 --impl reference times the CPU restatement of the same math (the reference's
@@ -441,6 +442,36 @@ def roofline(cfg: dict, kernel_name: str, kernel_s: float) -> dict:
             "flops_per_launch": flops, "peak_source": src}
 
 
+def chess_search_bench(net, dev: int, stream, trees: int = 1024, leaves: int = 4, sims: int = 200) -> dict:
+    """Batched PUCT on chess positions with the chess net: `trees` roots made
+    by the on-device position generator, `sims` simulations each from the
+    roots (select, evaluate, backup), timed with CUDA events."""
+    import torch
+
+    m = gz.Mcts(CHESS, trees, leaves, c_puct=1.5, virtual_loss=3, node_capacity=sims + 8, dirichlet_alpha=0.3,
+                dirichlet_eps=0.25, seed=0xC35, device=dev)
+    boards, side = gz.synth_positions_device(CHESS, trees, seed=0xC36, device=dev, stream=stream)
+    for _ in range(2):  # warm-up, then the timed search from fresh roots
+        m.reset_roots(boards, side, stream)
+        m.run(net, 3 * leaves if _ == 0 else sims, stream)
+    torch.cuda.synchronize()
+    m.reset_roots(boards, side, stream)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    m.run(net, sims, stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    el = ev0.elapsed_time(ev1) / 1e3
+    m.check()
+    nodes, edges = m.tree_sizes()
+    waves = math.ceil(sims / leaves)
+    m.close()
+    return {"sims_per_s": trees * waves * leaves / el, "ms_per_wave": el / waves * 1e3,
+            "config": f"{trees} chess roots (on-device random playouts) x {sims} sims, leaf batch {trees * leaves}, "
+                      f"c_puct 1.5, virtual loss 3, Dirichlet(0.3, 0.25), the c3 net",
+            "nodes_per_tree": float(nodes.mean()), "edges_per_node": float(edges.sum() / max(1, nodes.sum()))}
+
+
 def other_config(name: str, dev: int, stream, with_cpu: bool) -> dict:
     """One more leaf-evaluation workload on this GPU (one rank): value,
     roofline and a bounded CPU baseline sample."""
@@ -452,6 +483,8 @@ def other_config(name: str, dev: int, stream, with_cpu: bool) -> dict:
            "steps": cfg["steps"], "warmup": 5, "ms_per_step": r["elapsed"] / cfg["steps"] * 1e3,
            "config": config_block(cfg, 1), "roofline": roofline(cfg, net.kernel_name, r["kernel_s"]),
            "clocks": r["clocks"], "gpu_launches": cfg["steps"]}
+    if cfg["game"] == CHESS:
+        out["search"] = chess_search_bench(net, dev, stream)
     net.close()
     if with_cpu:
         out["cpu_baseline"] = cpu_baseline(cfg, seconds=8.0)
