@@ -231,41 +231,45 @@ GZ_HDI int pseudo_moves(const Pos& p, Move* out) {
   return n;
 }
 
-// Does pseudo-legal move m leave the mover's king unattacked?
-GZ_HDI bool move_is_legal(const Pos& p, const Move& m) {
+// Does pseudo-legal move m leave the mover's king unattacked?  ks is the
+// mover's king square before the move (king_square(p, p.side)); the king
+// stands there afterwards unless it is the piece that moves.
+GZ_HDI bool move_is_legal(const Pos& p, const Move& m, int ks) {
   Pos q = p;
   apply(q, m);
-  const int k = king_square(q, p.side);
+  const int k = m.from == ks ? m.to : ks;
   return k >= 0 && !attacked(q, k, -p.side);
 }
+
+GZ_HDI bool move_is_legal(const Pos& p, const Move& m) { return move_is_legal(p, m, king_square(p, p.side)); }
 
 // Legal moves of the side to move, in pseudo_moves' order; returns the
 // count (<= 256).
 GZ_HDI int legal_moves(const Pos& p, Move* out) {
   Move ps[256];
-  const int np = pseudo_moves(p, ps);
+  const int np = pseudo_moves(p, ps), ks = king_square(p, p.side);
   int n = 0;
   for (int i = 0; i < np; ++i)
-    if (move_is_legal(p, ps[i])) out[n++] = ps[i];
+    if (move_is_legal(p, ps[i], ks)) out[n++] = ps[i];
   return n;
 }
 
 // Legal moves in place: the first `return` entries of ms are the legal ones
 // (ms must hold 256).  One buffer instead of two, for device threads.
 GZ_HDI int legal_moves_inplace(const Pos& p, Move* ms) {
-  const int np = pseudo_moves(p, ms);
+  const int np = pseudo_moves(p, ms), ks = king_square(p, p.side);
   int n = 0;
   for (int i = 0; i < np; ++i)
-    if (move_is_legal(p, ms[i])) ms[n++] = ms[i];
+    if (move_is_legal(p, ms[i], ks)) ms[n++] = ms[i];
   return n;
 }
 
 // Has the side to move a legal move?  `scratch` holds 256 moves.
 GZ_HDI bool has_legal_move(const Pos& p, Move* scratch) {
   Move* ms = scratch;
-  const int np = pseudo_moves(p, ms);
+  const int np = pseudo_moves(p, ms), ks = king_square(p, p.side);
   for (int i = 0; i < np; ++i)
-    if (move_is_legal(p, ms[i])) return true;
+    if (move_is_legal(p, ms[i], ks)) return true;
   return false;
 }
 
