@@ -153,18 +153,16 @@ GZ_HDI void apply(Pos& p, const Move& m) {
   p.side = (int8_t)-me;
 }
 
-// Pseudo-legal moves of the side to move, in a fixed order (squares
-// ascending; per pawn: push, double push, captures toward the lower then the
-// higher file, promotions Q R B N; knight and king steps k = 0..7, then
-// castling king side, queen side; sliders diagonal rays then orthogonal
-// ones).  Returns the count; `out` holds 256 and the list stops there
-// (reachable chess positions have far fewer; a record with more pieces than
-// a game can reach may hit the cap, and it keeps every write in bounds).
-GZ_HDI int pseudo_moves(const Pos& p, Move* out) {
+// Pseudo-legal moves of the piece of the side to move on square s (none if
+// the square holds no such piece), at most `cap` of them: per pawn push,
+// double push, captures toward the lower then the higher file, promotions
+// Q R B N; knight and king steps k = 0..7, then castling king side, queen
+// side; sliders diagonal rays then orthogonal ones.
+GZ_HDI int piece_moves(const Pos& p, int s, Move* out, int cap) {
   const int me = p.side;
   int n = 0;
   auto add = [&](int from, int to, int promo) {
-    if (n < 256) out[n++] = Move{(int8_t)from, (int8_t)to, (int8_t)promo};
+    if (n < cap) out[n++] = Move{(int8_t)from, (int8_t)to, (int8_t)promo};
   };
   auto add_pawn = [&](int from, int to) {
     const int last = me > 0 ? 7 : 0;
@@ -177,57 +175,66 @@ GZ_HDI int pseudo_moves(const Pos& p, Move* out) {
       add(from, to, 0);
     }
   };
-  for (int s = 0; s < 64; ++s) {
-    const int v = p.sq[s];
-    if (v == 0 || sgn(v) != me) continue;
-    const int type = v * me, f = file_of(s), r = rank_of(s);
-    if (type == kPawn) {
-      const int r1 = r + me;
-      if (!on_board(f, r1)) continue;
-      if (p.sq[r1 * 8 + f] == 0) {
-        add_pawn(s, r1 * 8 + f);
-        const int start = me > 0 ? 1 : 6, r2 = r + 2 * me;
-        if (r == start && p.sq[r2 * 8 + f] == 0) add(s, r2 * 8 + f, 0);
+  const int v = p.sq[s];
+  if (v == 0 || sgn(v) != me) return 0;
+  const int type = v * me, f = file_of(s), r = rank_of(s);
+  if (type == kPawn) {
+    const int r1 = r + me;
+    if (!on_board(f, r1)) return 0;
+    if (p.sq[r1 * 8 + f] == 0) {
+      add_pawn(s, r1 * 8 + f);
+      const int start = me > 0 ? 1 : 6, r2 = r + 2 * me;
+      if (r == start && p.sq[r2 * 8 + f] == 0) add(s, r2 * 8 + f, 0);
+    }
+    for (int df = -1; df <= 1; df += 2) {
+      const int cf = f + df;
+      if (!on_board(cf, r1)) continue;
+      const int t = r1 * 8 + cf, tv = p.sq[t];
+      if ((tv != 0 && sgn(tv) == -me) || t == p.ep) add_pawn(s, t);
+    }
+  } else if (type == kKnight || type == kKing) {
+    for (int k = 0; k < 8; ++k) {
+      const int nf = f + (type == kKnight ? knight_df(k) : king_df(k));
+      const int nr = r + (type == kKnight ? knight_dr(k) : king_dr(k));
+      if (!on_board(nf, nr)) continue;
+      const int tv = p.sq[nr * 8 + nf];
+      if (tv == 0 || sgn(tv) == -me) add(s, nr * 8 + nf, 0);
+    }
+    if (type == kKing) {
+      const int home = me > 0 ? 4 : 60, ks = me > 0 ? 0x1 : 0x4, qs = me > 0 ? 0x2 : 0x8;
+      if (s == home && !attacked(p, s, -me)) {
+        if ((p.castle & ks) && p.sq[s + 3] == me * kRook && p.sq[s + 1] == 0 && p.sq[s + 2] == 0 &&
+            !attacked(p, s + 1, -me) && !attacked(p, s + 2, -me))
+          add(s, s + 2, 0);
+        if ((p.castle & qs) && p.sq[s - 4] == me * kRook && p.sq[s - 1] == 0 && p.sq[s - 2] == 0 &&
+            p.sq[s - 3] == 0 && !attacked(p, s - 1, -me) && !attacked(p, s - 2, -me))
+          add(s, s - 2, 0);
       }
-      for (int df = -1; df <= 1; df += 2) {
-        const int cf = f + df;
-        if (!on_board(cf, r1)) continue;
-        const int t = r1 * 8 + cf, tv = p.sq[t];
-        if ((tv != 0 && sgn(tv) == -me) || t == p.ep) add_pawn(s, t);
-      }
-    } else if (type == kKnight || type == kKing) {
-      for (int k = 0; k < 8; ++k) {
-        const int nf = f + (type == kKnight ? knight_df(k) : king_df(k));
-        const int nr = r + (type == kKnight ? knight_dr(k) : king_dr(k));
-        if (!on_board(nf, nr)) continue;
+    }
+  } else {
+    const bool diag = type == kBishop || type == kQueen, line = type == kRook || type == kQueen;
+    for (int k = 0; k < 8; ++k) {
+      if (k < 4 ? !diag : !line) continue;
+      const int df = k < 4 ? diag_df(k) : line_df(k - 4), dr = k < 4 ? diag_dr(k) : line_dr(k - 4);
+      for (int nf = f + df, nr = r + dr; on_board(nf, nr); nf += df, nr += dr) {
         const int tv = p.sq[nr * 8 + nf];
-        if (tv == 0 || sgn(tv) == -me) add(s, nr * 8 + nf, 0);
-      }
-      if (type == kKing) {
-        const int home = me > 0 ? 4 : 60, ks = me > 0 ? 0x1 : 0x4, qs = me > 0 ? 0x2 : 0x8;
-        if (s == home && !attacked(p, s, -me)) {
-          if ((p.castle & ks) && p.sq[s + 3] == me * kRook && p.sq[s + 1] == 0 && p.sq[s + 2] == 0 &&
-              !attacked(p, s + 1, -me) && !attacked(p, s + 2, -me))
-            add(s, s + 2, 0);
-          if ((p.castle & qs) && p.sq[s - 4] == me * kRook && p.sq[s - 1] == 0 && p.sq[s - 2] == 0 &&
-              p.sq[s - 3] == 0 && !attacked(p, s - 1, -me) && !attacked(p, s - 2, -me))
-            add(s, s - 2, 0);
-        }
-      }
-    } else {
-      const bool diag = type == kBishop || type == kQueen, line = type == kRook || type == kQueen;
-      for (int k = 0; k < 8; ++k) {
-        if (k < 4 ? !diag : !line) continue;
-        const int df = k < 4 ? diag_df(k) : line_df(k - 4), dr = k < 4 ? diag_dr(k) : line_dr(k - 4);
-        for (int nf = f + df, nr = r + dr; on_board(nf, nr); nf += df, nr += dr) {
-          const int tv = p.sq[nr * 8 + nf];
-          if (tv != 0 && sgn(tv) == me) break;
-          add(s, nr * 8 + nf, 0);
-          if (tv != 0) break;
-        }
+        if (tv != 0 && sgn(tv) == me) break;
+        add(s, nr * 8 + nf, 0);
+        if (tv != 0) break;
       }
     }
   }
+  return n;
+}
+
+// Pseudo-legal moves of the side to move, squares ascending, each square's
+// in piece_moves' order.  Returns the count; `out` holds 256 and the list
+// stops there (reachable chess positions have far fewer; a record with more
+// pieces than a game can reach may hit the cap, and it keeps every write in
+// bounds).
+GZ_HDI int pseudo_moves(const Pos& p, Move* out) {
+  int n = 0;
+  for (int s = 0; s < 64; ++s) n += piece_moves(p, s, out + n, 256 - n);
   return n;
 }
 

@@ -497,7 +497,7 @@ __global__ void tree_sizes_kernel(MctsDev d, int32_t* nodes, int32_t* edges) {
 // to move; stalemate: a draw), and lists an unexpanded leaf's legal actions
 // in generation order for the expansion.  Edges carry their action in pad[0].
 // The end-of-game check of a new node and the leaf's legal list run after
-// the wave's selections, one thread per leaf (chess_leaf_kernel): a new node
+// the wave's selections, a warp per leaf (chess_leaf_kernel): a new node
 // is unexpanded, so it ends a selection whether or not the game ends there,
 // and nothing in the selections depends on the check.
 
@@ -718,35 +718,61 @@ __device__ void chess_backup_tree(const MctsDev& d, const float* __restrict__ pi
   }
 }
 
-// The wave's leaf pass, one thread per selection: a node created in this
-// wave gets its game-end check (checkmate: a loss for its player to move;
+// The wave's leaf pass, a warp per selection: a node created in this wave
+// gets its game-end check (checkmate: a loss for its player to move;
 // stalemate: a draw), and a non-terminal unexpanded leaf its legal actions
-// in generation order.  Two selections that end on the same new node write
-// the same flags.
+// in generation order.  Lane l generates and tests the moves of squares l
+// and l + 32 (at most 27 per piece), and a prefix sum over the lanes places
+// them: squares ascending, each square's moves in piece_moves' order, as
+// legal_moves lists them.  Two selections that end on the same new node
+// write the same flags.
 __global__ void chess_leaf_kernel(MctsDev d) {
-  const int slot = blockIdx.x * blockDim.x + threadIdx.x;
-  if (slot >= d.trees * d.leaves) return;
+  const int slot = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (slot >= d.trees * d.leaves) return;  // whole warps
   const int t = slot / d.leaves, len = d.path_len[slot];
   MctsEdge* E = d.edges + (size_t)t * d.edge_cap;
   const int le = len > 0 ? d.path_edges[(size_t)slot * kMctsMaxDepth + len - 1] : -1;
   uint32_t flags = meta_flags(len > 0 ? E[le].meta : d.ctree[t].meta);
   chess::Pos p;
   chess::from_record(d.leaf_board + (size_t)slot * 66, d.leaf_side[slot], p);
-  chess::Move ms[256];
-  if (len > 0 && !(flags & kNodeChecked)) {  // created this wave, so not expanded
-    const int oc = chess::outcome_with(p, ms);
+  const bool fresh = len > 0 && !(flags & kNodeChecked);  // created this wave, so not expanded
+  const bool need_list = fresh || (!(flags & kNodeTerminal) && !(flags & kNodeExpanded));
+  int c = 0, ks = -1;
+  if (need_list) {
+    const int king = p.side * chess::kKing;
+    const unsigned b0 = __ballot_sync(kFull, p.sq[lane] == king), b1 = __ballot_sync(kFull, p.sq[lane + 32] == king);
+    ks = b0 ? __ffs(b0) - 1 : b1 ? 31 + __ffs(b1) : -1;  // the lowest square, as king_square
+    int16_t* la = d.leaf_actions + (size_t)slot * kChessMaxLegal;
+    int base = 0;
+    for (int h = 0; h < 2; ++h) {
+      chess::Move mv[28];
+      const int nm = chess::piece_moves(p, lane + 32 * h, mv, 28);
+      int nl = 0;
+      for (int k = 0; k < nm; ++k)
+        if (chess::move_is_legal(p, mv[k], ks)) mv[nl++] = mv[k];
+      int inc = nl;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFull, inc, o);
+        if (lane >= o) inc += y;
+      }
+      const int off = base + inc - nl;
+      for (int k = 0; k < nl; ++k)
+        if (off + k < kChessMaxLegal) la[off + k] = (int16_t)chess::encode_action(mv[k]);
+      base += __shfl_sync(kFull, inc, 31);
+    }
+    c = base < kChessMaxLegal ? base : kChessMaxLegal;
+  }
+  if (fresh) {
+    const int oc = c > 0 ? 0 : (ks >= 0 && chess::attacked(p, ks, -p.side)) ? -1 : 2;
     flags |= kNodeChecked | (oc != 0 ? kNodeTerminal : 0u) | (oc == -1 ? kNodeLoss : 0u);
-    E[le].meta = make_meta(0, 0, flags);
+    if (lane == 0) E[le].meta = make_meta(0, 0, flags);
   }
   const bool term = (flags & kNodeTerminal) != 0;
-  d.leaf_terminal[slot] = term ? 1 : 0;
-  int c = 0;
-  if (!term && !(flags & kNodeExpanded)) {
-    c = chess::legal_moves_inplace(p, ms);
-    int16_t* la = d.leaf_actions + (size_t)slot * kChessMaxLegal;
-    for (int j = 0; j < c; ++j) la[j] = (int16_t)chess::encode_action(ms[j]);
+  if (lane == 0) {
+    d.leaf_terminal[slot] = term ? 1 : 0;
+    d.leaf_count[slot] = term ? 0 : c;
   }
-  d.leaf_count[slot] = c;
 }
 
 __global__ void chess_select_kernel(MctsDev d) {
@@ -889,7 +915,7 @@ cudaError_t mcts_launch_reset(const MctsDev& d, const int8_t* boards, const int8
 cudaError_t mcts_launch_select(const MctsDev& d, cudaStream_t s) {
   if (d.game == kChess) {
     chess_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d);
-    chess_leaf_kernel<<<blocks_for(d.trees * d.leaves, 128), 128, 0, s>>>(d);
+    chess_leaf_kernel<<<blocks_for(d.trees * d.leaves, 4), 128, 0, s>>>(d);
   } else select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d);
   return cudaGetLastError();
 }
@@ -903,7 +929,7 @@ cudaError_t mcts_launch_backup(const MctsDev& d, const float* pi, const float* v
 cudaError_t mcts_launch_backup_select(const MctsDev& d, const float* pi, const float* v, cudaStream_t s) {
   if (d.game == kChess) {
     chess_backup_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
-    chess_leaf_kernel<<<blocks_for(d.trees * d.leaves, 128), 128, 0, s>>>(d);
+    chess_leaf_kernel<<<blocks_for(d.trees * d.leaves, 4), 128, 0, s>>>(d);
   } else backup_select_kernel<<<blocks_for(d.trees, 4), 128, 0, s>>>(d, pi, v);
   return cudaGetLastError();
 }
